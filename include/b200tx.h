@@ -1,0 +1,121 @@
+/*
+ * b200tx.h -- C ABI of libb200tx, the sm_100a (B200) kernels behind the
+ * Transformer forward of the `solution` package.
+ *
+ * The reference (Wendystar0628/ML-Guided-Program-Search-for-Shape-Specialized-
+ * Transformer-Optimization) is pure Python: its hot path calls Triton kernels
+ * through Python wrappers that return `(tensor, marker)`.  Each entry point
+ * below replaces one of those operators; the reference file:line it stands in
+ * for is cited beside it.  The Python wrappers in solution/kernels/ bind these
+ * symbols with ctypes.
+ *
+ * Conventions
+ *   - Plain device pointers, element counts and a cudaStream_t; no framework
+ *     types.  Tensors are dense row-major with the shapes given per function.
+ *   - Nothing here allocates device memory, synchronises the device or the
+ *     stream, or launches on any stream other than the one passed in, so every
+ *     call can be captured in a CUDA graph.
+ *   - Return value 0 = launched.  A negative value is an error; the message is
+ *     in b200tx_last_error() (thread-local).  Argument errors are detected on
+ *     the host before anything is launched.
+ *   - Kernels never trap.  A device-side wait that runs out (a hung pipeline)
+ *     records a code that b200tx_device_error() returns.
+ */
+#ifndef B200TX_H_
+#define B200TX_H_
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types accepted by the dtype arguments. */
+#define B200TX_F32 0
+#define B200TX_BF16 1
+
+/* Epilogues of b200tx_linear. */
+#define B200TX_EPI_BIAS 0
+#define B200TX_EPI_BIAS_GELU 1
+
+/* Status codes. */
+#define B200TX_OK 0
+#define B200TX_ERR_INVALID_ARGUMENT -1
+#define B200TX_ERR_UNSUPPORTED -2
+#define B200TX_ERR_CUDA -3
+#define B200TX_ERR_DRIVER -4
+
+/* ABI version of this header; bumped when a signature changes. */
+int b200tx_abi_version(void);
+
+/* Message describing the last failed call on this host thread ("" if none). */
+const char* b200tx_last_error(void);
+
+/* Reads (and, if `clear` != 0, resets) the device error word of the current
+ * device: 0 when healthy, else the code of the first kernel wait that ran out.
+ * Synchronises the device; diagnostic use only. */
+int b200tx_device_error(int clear, unsigned int* code_out);
+
+/* Multiprocessor count and compute capability of the current device; returns
+ * B200TX_ERR_UNSUPPORTED unless it is a compute capability 10.0 device. */
+int b200tx_device_check(int* sm_count_out, int* cc_major_out, int* cc_minor_out);
+
+/*
+ * LayerNorm of each row, optionally after a residual add:
+ *     r = residual_in + update            (update may be NULL)
+ *     normed = (r - mean(r)) / sqrt(var(r) + eps) * gamma + beta
+ *     residual_out = r                    (if residual_out != NULL)
+ * residual_in  [rows, cols] in_dtype (F32 or BF16)
+ * update       [rows, cols] update_dtype (F32 or BF16), or NULL
+ * residual_out [rows, cols] F32, or NULL; may equal residual_in (in place)
+ * normed       [rows, cols] out_dtype (F32 or BF16)
+ * gamma, beta  [cols] F32
+ * Replaces: solution/kernels/norm/triton_initial.py:38-66 (initial LN, no
+ * update), solution/kernels/norm/triton_residual.py:38-73 and
+ * solution/kernels/norm/triton_mixed_residual.py:40-77 (residual + LN; the
+ * `final_boundary` fp32 output is out_dtype = F32), and the torch path
+ * residual_add + nn.LayerNorm at solution/transformer.py:1629-1632.
+ */
+int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void* update,
+                               int update_dtype, float* residual_out, void* normed,
+                               int out_dtype, const float* gamma, const float* beta,
+                               int64_t rows, int64_t cols, float eps, cudaStream_t stream);
+
+/*
+ * out[M, N] = epilogue(a[M, K] . w[N, K]^T + bias[N]) on the tcgen05 tensor
+ * cores, bf16 inputs, fp32 accumulation, output F32 or BF16.
+ * a, w: BF16, row-major, K contiguous; bias: F32 [N] or NULL.
+ * epilogue: B200TX_EPI_BIAS or B200TX_EPI_BIAS_GELU (exact erf GELU).
+ * Requires K % 8 == 0 and N % 8 == 0 (16-byte TMA row pitch); 16-byte
+ * aligned a, w and out.
+ * Replaces: solution/kernels/projection/triton_qkv_layout.py:59-113 (packed
+ * QKV), solution/kernels/projection/triton_attention_output.py:69-147
+ * (out-proj), solution/kernels/ffn/triton_linear_exact_gelu.py:68-132 (FFN in
+ * + GELU), and the fp16-shadow F.linear at solution/transformer.py:333-353.
+ */
+int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                  int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream);
+
+/*
+ * Causal (or full) multi-head attention over the packed projection output.
+ * qkv  [batch, seq, 3, heads, head_dim] BF16 -- the [B, S, 3D] output of the
+ *      packed QKV linear (rows q;k;v of W_qkv), D = heads * head_dim
+ * out  [batch, seq, heads, head_dim] BF16 -- the [B, S, D] context, ready for
+ *      the out-projection
+ * softmax(q k^T * scale (+ causal mask)) v with fp32 softmax statistics.
+ * head_dim must be 64.
+ * Replaces: solution/shape14/triton_streaming_dh64.py:68-190 (streaming
+ * Dh64, BSD output), solution/kernels/attention/triton_s1024_dh32.py:72-265,
+ * solution/operators/attention/sdpa.py:76-170 (SDPA / query-blocked
+ * reference attention) together with split_qkv
+ * (solution/operators/projection/qkv_layout.py:22-50).
+ */
+int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t head_dim, float scale, int causal, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200TX_H_ */

@@ -1,0 +1,338 @@
+// attention_kernels.cuh -- causal flash attention forward for head_dim 64 on the
+// sm_100 tensor cores, reading Q/K/V straight out of the packed QKV projection
+// and writing the context in [B, S, H*64] (BSD) order for the out-projection.
+//
+// Replaces the reference's attention primitives:
+//   streaming Dh64 kernel   solution/shape14/triton_streaming_dh64.py:68-190
+//   shape13 Dh32 kernel     solution/kernels/attention/triton_s1024_dh32.py:72-265
+//   query-blocked reference solution/operators/attention/sdpa.py:116-170
+// Semantics (official/torch_transformer_benchmark.py:95-118):
+//   softmax(Q K^T * Dh^-1/2, causal -inf above the diagonal) computed in fp32,
+//   probabilities cast to the activation dtype (bf16 here), times V.
+// No [S, S] tensor exists anywhere: scores live in TMEM one 128x128 tile at a
+// time and the softmax keeps its running max and sum in registers.
+//
+// One CTA = one 128-row query tile of one (batch, head); 192 threads, two CTAs
+// per SM so one CTA's softmax overlaps the other's MMAs.
+//   warp 0      TMA: Q once, then K_j, V_j through a 3-slot ring of 16 KB tiles
+//   warp 1      one thread issues S = Q K_j^T (4 x 128x128x16 UMMAs) and
+//               O += P_j V_j (8 x 128x64x16 UMMAs, V consumed MN-major)
+//   warps 2..5  softmax, one query row per thread: two passes over the S row in
+//               TMEM (max, then exp2 / sum / bf16 P into swizzled shared memory)
+// TMEM: S in columns [0,128), O in columns [128,192) of a 256-column allocation.
+// The running max is only moved when a row's maximum grows by more than 8 (in
+// log2 units); until then P may reach 2^8, which fp32 O and l absorb exactly as
+// if the max had been moved, and O is rescaled in TMEM only for such warps.
+// Query tiles are dispatched longest-first (diagonal tile index descending)
+// so the causal triangle balances across the grid.
+#pragma once
+
+#include "sm100_common.cuh"
+
+namespace b200tx {
+
+constexpr int kAttnBM = 128;
+constexpr int kAttnBN = 128;
+constexpr int kAttnDh = 64;
+constexpr int kAttnRing = 3;
+constexpr int kAttnThreads = 192;
+constexpr uint32_t kAttnTmemCols = 256;
+constexpr uint32_t kAttnTmemO = 128;
+constexpr uint32_t kAttnTileBytes = kAttnBM * kAttnDh * 2;  // 16 KB (Q, K or V tile)
+constexpr uint32_t kAttnPHalfBytes = kAttnBM * 64 * 2;      // 16 KB: 64 key columns of P
+constexpr size_t kAttnSmemBytes =
+    1024 + kAttnTileBytes * (1 + kAttnRing) + 2 * kAttnPHalfBytes;  // 97 KB
+
+struct AttnArgs {
+  __nv_bfloat16* out;  // [B, S, H*64]
+  int batch;
+  int seq;
+  int heads;
+  int num_q_tiles;
+  float scale_log2;  // Dh^-1/2 * log2(e)
+  int causal;
+};
+
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attention_fwd_dh64_kernel(const __grid_constant__ CUtensorMap tmap_qkv, AttnArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t q_full_bar;
+  __shared__ uint64_t ring_full_bar[kAttnRing];
+  __shared__ uint64_t ring_empty_bar[kAttnRing];
+  __shared__ uint64_t s_full_bar;
+  __shared__ uint64_t p_full_bar;
+  __shared__ uint64_t o_done_bar;
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* smem_q = smem;
+  uint8_t* smem_ring = smem + kAttnTileBytes;
+  uint8_t* smem_p = smem_ring + kAttnRing * kAttnTileBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Longest query tiles first.
+  const int hb_count = args.heads * args.batch;
+  const int q_tile = args.num_q_tiles - 1 - static_cast<int>(blockIdx.x / hb_count);
+  const int hb = static_cast<int>(blockIdx.x % hb_count);
+  const int head = hb % args.heads;
+  const int batch = hb / args.heads;
+  const int kv_tiles_total = (args.seq + kAttnBN - 1) / kAttnBN;
+  const int n_kv = args.causal ? (q_tile + 1) : kv_tiles_total;
+  const int d_model = args.heads * kAttnDh;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensor_map(&tmap_qkv);
+    mbar_init(&q_full_bar, 1);
+    for (int s = 0; s < kAttnRing; ++s) {
+      mbar_init(&ring_full_bar[s], 1);
+      mbar_init(&ring_empty_bar[s], 1);
+    }
+    mbar_init(&s_full_bar, 1);
+    mbar_init(&p_full_bar, 128);
+    mbar_init(&o_done_bar, 1);
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, kAttnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&q_full_bar, kAttnTileBytes);
+      tma_load_3d(smem_q, &tmap_qkv, &q_full_bar, head * kAttnDh, q_tile * kAttnBM, batch);
+      const int items = 2 * n_kv;  // K_0, V_0, K_1, V_1, ...
+      int issued = 0;
+      for (int i = 0; i < items; ++i) {
+        const int slot = i % kAttnRing;
+        const uint32_t ph = (i / kAttnRing) & 1;
+        if (!mbar_wait(&ring_empty_bar[slot], ph ^ 1u, kErrAttnProducerWait, &abort_flag)) break;
+        mbar_arrive_expect_tx(&ring_full_bar[slot], kAttnTileBytes);
+        const int j = i >> 1;
+        const int col = (i & 1 ? 2 * d_model : d_model) + head * kAttnDh;
+        tma_load_3d(smem_ring + slot * kAttnTileBytes, &tmap_qkv, &ring_full_bar[slot], col,
+                    j * kAttnBN, batch);
+        ++issued;
+      }
+      // Wait for the loads still in flight (complete already on the normal path).
+      volatile int no_abort = 0;
+      mbar_wait(&q_full_bar, 0, kErrAttnProducerWait, &no_abort);
+      const int first = issued > kAttnRing ? issued - kAttnRing : 0;
+      for (int i = first; i < issued; ++i) {
+        mbar_wait(&ring_full_bar[i % kAttnRing], (i / kAttnRing) & 1, kErrAttnProducerWait,
+                  &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kAttnBM, kAttnBN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kAttnBM, kAttnDh, false, true);
+      const uint32_t q_addr = smem_u32(smem_q);
+      const uint32_t p_addr = smem_u32(smem_p);
+      const uint32_t s_tmem = tmem_base;
+      const uint32_t o_tmem = tmem_base + kAttnTmemO;
+      bool issued_any = false;
+      auto issue_qk = [&](int j) -> bool {
+        const int i = 2 * j;
+        const int slot = i % kAttnRing;
+        if (!mbar_wait(&ring_full_bar[slot], (i / kAttnRing) & 1, kErrAttnMmaWait, &abort_flag))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem_ring + slot * kAttnTileBytes);
+#pragma unroll
+        for (int k = 0; k < kAttnDh / 16; ++k) {
+          umma_bf16_ss(s_tmem, sw128_desc(q_addr + k * 32, 16, 1024),
+                       sw128_desc(k_addr + k * 32, 16, 1024), idesc_qk, k != 0 ? 1u : 0u);
+        }
+        issued_any = true;
+        umma_commit(&ring_empty_bar[slot]);
+        umma_commit(&s_full_bar);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full_bar, 0, kErrAttnMmaWait, &abort_flag);
+      if (ok) {
+        tc_fence_after();
+        ok = issue_qk(0);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        // Softmax of tile j finished: S is free, P_j is in shared memory and O
+        // has been rescaled where needed.
+        if (!mbar_wait(&p_full_bar, j & 1, kErrAttnMmaWait, &abort_flag)) break;
+        tc_fence_after();
+        if (j + 1 < n_kv && !issue_qk(j + 1)) break;
+        const int i = 2 * j + 1;
+        const int slot = i % kAttnRing;
+        if (!mbar_wait(&ring_full_bar[slot], (i / kAttnRing) & 1, kErrAttnMmaWait, &abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem_ring + slot * kAttnTileBytes);
+#pragma unroll
+        for (int k = 0; k < kAttnBN / 16; ++k) {
+          const uint32_t pa = p_addr + (k >> 2) * kAttnPHalfBytes + (k & 3) * 32;
+          const uint32_t vb = v_addr + k * 16 * 128;  // 16 key rows of 128 B
+          umma_bf16_ss(o_tmem, sw128_desc(pa, 16, 1024), sw128_desc(vb, kAttnTileBytes, 1024),
+                       idesc_pv, (j | k) != 0 ? 1u : 0u);
+        }
+        umma_commit(&ring_empty_bar[slot]);
+        umma_commit(&o_done_bar);
+      }
+      if (issued_any) {
+        umma_commit(&drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait(&drain_bar, 0, kErrAttnMmaWait, &no_abort);
+      }
+    }
+  } else {
+    // Softmax warps: warp w owns TMEM lanes 32*(w%4) .. +31 = query rows.
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q_idx = q_tile * kAttnBM + row;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t p_row = smem_u32(smem_p) + row * 128;
+    const uint32_t swz = row & 7;
+    const float c = args.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = mbar_wait(&s_full_bar, j & 1, kErrAttnSoftmaxWait, &abort_flag);
+      if (__any_sync(0xffffffffu, !ok)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      // Columns at or beyond `limit` are masked: above the diagonal on the
+      // diagonal tile, beyond the sequence on a non-causal ragged last tile.
+      int limit = kAttnBN;
+      if (args.causal) {
+        if (j == q_tile) limit = row + 1;
+      } else if ((j + 1) * kAttnBN > args.seq) {
+        limit = args.seq - j * kAttnBN;
+      }
+      // Pass 1: row maximum.
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int cc = 0; cc < kAttnBN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32cols(lane_base + cc * 32, r);
+        tmem_wait_ld();
+        if (limit >= (cc + 1) * 32) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (cc * 32 + i < limit) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+      }
+      const float mx_scaled = mx * c;
+      const bool need = mx_scaled > m_run + 8.0f;
+      const float m_new = need ? mx_scaled : m_run;
+      // P_{j-1} and O are busy until the previous P.V has completed.
+      if (j > 0) {
+        ok = mbar_wait(&o_done_bar, (j - 1) & 1, kErrAttnSoftmaxWait, &abort_flag);
+        if (__any_sync(0xffffffffu, !ok)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        tc_fence_after();
+      }
+      // Pass 2: probabilities, row sum, bf16 P in the 128-byte-swizzled
+      // K-major layout the UMMA descriptor expects.
+      float sum = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < kAttnBN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32cols(lane_base + cc * 32, r);
+        tmem_wait_ld();
+        float p[32];
+        if (limit >= (cc + 1) * 32) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(r[i]), c, -m_new));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            p[i] = (cc * 32 + i < limit) ? fast_exp2(fmaf(__uint_as_float(r[i]), c, -m_new)) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sum += p[i];
+        const uint32_t half_base = p_row + (cc >> 1) * kAttnPHalfBytes;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t chunk = (cc & 1) * 4 + q;  // 16-byte chunk within the 128-byte row
+          const int b = q * 8;
+          st_shared_v4(half_base + ((chunk ^ swz) << 4), pack_bf16x2(p[b], p[b + 1]),
+                       pack_bf16x2(p[b + 2], p[b + 3]), pack_bf16x2(p[b + 4], p[b + 5]),
+                       pack_bf16x2(p[b + 6], p[b + 7]));
+        }
+      }
+      fence_proxy_async_smem();
+      const float alpha = need ? fast_exp2(m_run - m_new) : 1.0f;  // exp2(-inf) = 0 on j == 0
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(lane_base + kAttnTmemO + cc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32cols(lane_base + kAttnTmemO + cc * 32, r);
+        }
+        tmem_wait_st();
+      }
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      tc_fence_before();
+      mbar_arrive(&p_full_bar);
+    }
+    if (ok) {
+      ok = mbar_wait(&o_done_bar, (n_kv - 1) & 1, kErrAttnSoftmaxWait, &abort_flag);
+      const bool all_ok = !__any_sync(0xffffffffu, !ok);
+      __syncwarp();
+      if (all_ok) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+        __nv_bfloat16* out_row =
+            args.out + (static_cast<int64_t>(batch) * args.seq + q_idx) * d_model + head * kAttnDh;
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(lane_base + kAttnTmemO + cc * 32, r);
+          tmem_wait_ld();
+          if (q_idx < args.seq) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              st_global_v4(out_row + cc * 32 + i,
+                           pack_bf16x2(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l));
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAttnTmemCols);
+  }
+}
+
+}  // namespace b200tx

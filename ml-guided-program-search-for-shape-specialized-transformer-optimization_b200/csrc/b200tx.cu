@@ -1,0 +1,385 @@
+// b200tx.cu -- the single translation unit of libb200tx: host-side argument
+// checks, TMA descriptor encoding and launches for the sm_100a kernels in the
+// *.cuh files next to it, behind the C ABI declared in include/b200tx.h.
+//
+// One translation unit keeps the device error word a plain __device__ variable
+// (no relocatable device code) and lets every kernel see it.
+
+#include "b200tx.h"
+
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <type_traits>
+
+#include "attention_kernels.cuh"
+#include "gemm_kernels.cuh"
+#include "norm_kernels.cuh"
+#include "sm100_common.cuh"
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(B200TX_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
+}
+
+struct DeviceState {
+  bool probed = false;
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  bool gemm_attr[4] = {false, false, false, false};
+  bool attn_attr = false;
+};
+
+std::mutex g_mutex;
+DeviceState g_devices[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+// Looks up the current device, checks it is an sm_100 part and fills `state`.
+int current_device(DeviceState** state) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(B200TX_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& s = g_devices[dev];
+  if (!s.probed) {
+    err = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(SM count)");
+    err = cudaDeviceGetAttribute(&s.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(cc major)");
+    err = cudaDeviceGetAttribute(&s.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(cc minor)");
+    s.probed = true;
+  }
+  if (s.cc_major != 10 || s.cc_minor != 0) {
+    return fail(B200TX_ERR_UNSUPPORTED,
+                "libb200tx is built for sm_100a only; device %d has compute capability %d.%d", dev,
+                s.cc_major, s.cc_minor);
+  }
+  *state = &s;
+  return B200TX_OK;
+}
+
+int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_encode_tiled == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      return fail(B200TX_ERR_DRIVER, "driver entry point cuTensorMapEncodeTiled unavailable");
+    }
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  *out = g_encode_tiled;
+  return B200TX_OK;
+}
+
+// Tiled bf16 tensor map with a 128-byte swizzle; out-of-range elements of a
+// box read as zero.  dims/strides innermost first; strides in bytes for dims 1..
+int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  int rc = encoder(&encode);
+  if (rc != B200TX_OK) return rc;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5];
+  cuuint32_t es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+                        const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) {
+    return fail(B200TX_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", int(res));
+  }
+  return B200TX_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ norms
+template <int NV, typename InT, typename UpdT, typename OutT>
+cudaError_t launch_norm_vec(const b200tx::NormArgs& a, cudaStream_t stream) {
+  const unsigned grid =
+      static_cast<unsigned>((a.rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock);
+  b200tx::residual_layernorm_vec_kernel<NV, InT, UpdT, OutT>
+      <<<grid, b200tx::kNormWarpsPerBlock * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename InT, typename UpdT, typename OutT>
+cudaError_t launch_norm(const b200tx::NormArgs& a, bool vec_ok, cudaStream_t stream) {
+  if (vec_ok && a.cols % 128 == 0) {
+    switch (a.cols / 128) {
+      case 1: return launch_norm_vec<1, InT, UpdT, OutT>(a, stream);
+      case 2: return launch_norm_vec<2, InT, UpdT, OutT>(a, stream);
+      case 4: return launch_norm_vec<4, InT, UpdT, OutT>(a, stream);
+      case 6: return launch_norm_vec<6, InT, UpdT, OutT>(a, stream);
+      case 8: return launch_norm_vec<8, InT, UpdT, OutT>(a, stream);
+      case 12: return launch_norm_vec<12, InT, UpdT, OutT>(a, stream);
+      case 16: return launch_norm_vec<16, InT, UpdT, OutT>(a, stream);
+      case 24: return launch_norm_vec<24, InT, UpdT, OutT>(a, stream);
+      case 32: return launch_norm_vec<32, InT, UpdT, OutT>(a, stream);
+      default: break;
+    }
+  }
+  const unsigned grid =
+      static_cast<unsigned>((a.rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock);
+  b200tx::residual_layernorm_generic_kernel<InT, UpdT, OutT>
+      <<<grid, b200tx::kNormWarpsPerBlock * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename InT, typename UpdT>
+cudaError_t launch_norm_out(const b200tx::NormArgs& a, int out_dtype, bool vec_ok,
+                            cudaStream_t stream) {
+  if (out_dtype == B200TX_BF16) return launch_norm<InT, UpdT, __nv_bfloat16>(a, vec_ok, stream);
+  return launch_norm<InT, UpdT, float>(a, vec_ok, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200tx_abi_version(void) { return kAbiVersion; }
+
+const char* b200tx_last_error(void) { return g_last_error.c_str(); }
+
+int b200tx_device_check(int* sm_count_out, int* cc_major_out, int* cc_minor_out) {
+  DeviceState* s = nullptr;
+  int rc = current_device(&s);
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    const DeviceState& d = g_devices[dev];
+    if (sm_count_out) *sm_count_out = d.sm_count;
+    if (cc_major_out) *cc_major_out = d.cc_major;
+    if (cc_minor_out) *cc_minor_out = d.cc_minor;
+  }
+  return rc;
+}
+
+int b200tx_device_error(int clear, unsigned int* code_out) {
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceSynchronize");
+  unsigned int code = 0;
+  err = cudaMemcpyFromSymbol(&code, b200tx::g_device_error, sizeof(code));
+  if (err != cudaSuccess) return cuda_fail(err, "reading the device error word");
+  if (clear) {
+    const unsigned int zero = 0;
+    err = cudaMemcpyToSymbol(b200tx::g_device_error, &zero, sizeof(zero));
+    if (err != cudaSuccess) return cuda_fail(err, "clearing the device error word");
+  }
+  if (code_out) *code_out = code;
+  return B200TX_OK;
+}
+
+int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void* update,
+                               int update_dtype, float* residual_out, void* normed,
+                               int out_dtype, const float* gamma, const float* beta,
+                               int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  if (residual_in == nullptr || normed == nullptr || gamma == nullptr || beta == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: null tensor pointer");
+  if (rows <= 0 || cols <= 0 || cols > (1 << 20))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: bad shape [%lld, %lld]",
+                (long long)rows, (long long)cols);
+  if ((rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock > 0x7fffffffLL)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: too many rows");
+  if (in_dtype != B200TX_F32 && in_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: in_dtype %d", in_dtype);
+  if (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: out_dtype %d", out_dtype);
+  if (update != nullptr && update_dtype != B200TX_F32 && update_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: update_dtype %d", update_dtype);
+  if (update != nullptr && in_dtype != B200TX_F32)
+    return fail(B200TX_ERR_UNSUPPORTED,
+                "residual_layer_norm: a residual add needs an F32 residual stream");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+
+  b200tx::NormArgs a;
+  a.residual_in = residual_in;
+  a.update = update;
+  a.residual_out = residual_out;
+  a.normed = normed;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.rows = rows;
+  a.cols = static_cast<int>(cols);
+  a.eps = eps;
+  const bool vec_ok = aligned16(residual_in) && aligned16(normed) && aligned16(gamma) &&
+                      aligned16(beta) && (update == nullptr || aligned16(update)) &&
+                      (residual_out == nullptr || aligned16(residual_out));
+  cudaError_t err;
+  if (update == nullptr) {
+    if (in_dtype == B200TX_F32)
+      err = launch_norm_out<float, void>(a, out_dtype, vec_ok, stream);
+    else
+      err = launch_norm_out<__nv_bfloat16, void>(a, out_dtype, vec_ok, stream);
+  } else if (update_dtype == B200TX_BF16) {
+    err = launch_norm_out<float, __nv_bfloat16>(a, out_dtype, vec_ok, stream);
+  } else {
+    err = launch_norm_out<float, float>(a, out_dtype, vec_ok, stream);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, "residual_layer_norm launch");
+  return B200TX_OK;
+}
+
+int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                  int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
+  if (a == nullptr || w == nullptr || out == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: null tensor pointer");
+  if (M <= 0 || N <= 0 || K <= 0 || M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: bad shape M=%lld N=%lld K=%lld",
+                (long long)M, (long long)N, (long long)K);
+  if (K % 8 != 0 || N % 8 != 0)
+    return fail(B200TX_ERR_UNSUPPORTED, "linear: K (%lld) and N (%lld) must be multiples of 8",
+                (long long)K, (long long)N);
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) ||
+      (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 3u) != 0))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: operands must be 16-byte aligned");
+  if (epilogue != B200TX_EPI_BIAS && epilogue != B200TX_EPI_BIAS_GELU)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: epilogue %d", epilogue);
+  if (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: out_dtype %d", out_dtype);
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+
+  CUtensorMap map_a, map_w;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
+    const uint32_t box[2] = {b200tx::kGemmBK, b200tx::kGemmBM};
+    rc = encode_bf16_map(&map_a, a, 2, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
+    const uint32_t box[2] = {b200tx::kGemmBK, b200tx::kGemmBN};
+    rc = encode_bf16_map(&map_w, w, 2, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+  }
+  b200tx::GemmArgs args;
+  args.bias = bias;
+  args.out = out;
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  args.num_m_tiles = static_cast<int>((M + b200tx::kGemmBM - 1) / b200tx::kGemmBM);
+  args.num_n_tiles = static_cast<int>((N + b200tx::kGemmBN - 1) / b200tx::kGemmBN);
+  const int64_t tiles = static_cast<int64_t>(args.num_m_tiles) * args.num_n_tiles;
+  if (tiles > 0x7fffffffLL) return fail(B200TX_ERR_UNSUPPORTED, "linear: too many tiles");
+  const unsigned grid = static_cast<unsigned>(tiles < dev->sm_count ? tiles : dev->sm_count);
+
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::GemmArgs);
+  KernelFn kernel;
+  const int variant = epilogue * 2 + (out_dtype == B200TX_F32 ? 1 : 0);
+  switch (variant) {
+    case 0: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
+    case 1: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, float>; break;
+    case 2: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
+    default: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, float>; break;
+  }
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->gemm_attr[variant]) {
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(b200tx::kGemmSmemBytes));
+      if (err != cudaSuccess) return cuda_fail(err, "linear: cudaFuncSetAttribute");
+      dev->gemm_attr[variant] = true;
+    }
+  }
+  kernel<<<grid, b200tx::kGemmThreads, b200tx::kGemmSmemBytes, stream>>>(map_a, map_w, args);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_fail(err, "linear launch");
+  return B200TX_OK;
+}
+
+int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t head_dim, float scale, int causal, cudaStream_t stream) {
+  if (qkv == nullptr || out == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: null tensor pointer");
+  if (batch <= 0 || seq <= 0 || heads <= 0)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: bad shape B=%lld S=%lld H=%lld",
+                (long long)batch, (long long)seq, (long long)heads);
+  if (head_dim != b200tx::kAttnDh)
+    return fail(B200TX_ERR_UNSUPPORTED, "attention: head_dim %lld (only 64 is built)",
+                (long long)head_dim);
+  if (!aligned16(qkv) || !aligned16(out))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
+  if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
+  const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
+  const int64_t blocks = q_tiles * heads * batch;
+  if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
+    return fail(B200TX_ERR_UNSUPPORTED, "attention: problem too large for one launch");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+
+  const int64_t d_model = heads * head_dim;
+  CUtensorMap map_qkv;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(3 * d_model) * 2,
+                                 static_cast<uint64_t>(3 * d_model) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t box[3] = {b200tx::kAttnDh, b200tx::kAttnBM, 1};
+    rc = encode_bf16_map(&map_qkv, qkv, 3, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+  }
+  b200tx::AttnArgs args;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.batch = static_cast<int>(batch);
+  args.seq = static_cast<int>(seq);
+  args.heads = static_cast<int>(heads);
+  args.num_q_tiles = static_cast<int>(q_tiles);
+  args.scale_log2 = scale * 1.4426950408889634f;
+  args.causal = causal ? 1 : 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->attn_attr) {
+      cudaError_t err =
+          cudaFuncSetAttribute(b200tx::attention_fwd_dh64_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(b200tx::kAttnSmemBytes));
+      if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
+      dev->attn_attr = true;
+    }
+  }
+  b200tx::attention_fwd_dh64_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttnThreads,
+                                      b200tx::kAttnSmemBytes, stream>>>(map_qkv, args);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+  return B200TX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,281 @@
+"""ctypes binding of libb200tx (include/b200tx.h).
+
+This module is the only place that touches the C ABI.  It loads the in-tree
+``solution/_lib/libb200tx.so`` and exposes one checked Python call per entry
+point.  There is no fallback: when the library is missing or the device is not
+an sm_100 part, every call raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200tx.so"
+ABI_VERSION = 1
+
+F32 = 0
+BF16 = 1
+EPI_BIAS = 0
+EPI_BIAS_GELU = 1
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+_load_error: str | None = None
+
+_c_int64 = ctypes.c_int64
+_c_void_p = ctypes.c_void_p
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    lib.b200tx_abi_version.restype = ctypes.c_int
+    lib.b200tx_abi_version.argtypes = []
+    lib.b200tx_last_error.restype = ctypes.c_char_p
+    lib.b200tx_last_error.argtypes = []
+    lib.b200tx_device_error.restype = ctypes.c_int
+    lib.b200tx_device_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    lib.b200tx_device_check.restype = ctypes.c_int
+    lib.b200tx_device_check.argtypes = [
+        ctypes.POINTER(ctypes.c_int),
+        ctypes.POINTER(ctypes.c_int),
+        ctypes.POINTER(ctypes.c_int),
+    ]
+    lib.b200tx_residual_layer_norm.restype = ctypes.c_int
+    lib.b200tx_residual_layer_norm.argtypes = [
+        _c_void_p,  # residual_in
+        ctypes.c_int,  # in_dtype
+        _c_void_p,  # update
+        ctypes.c_int,  # update_dtype
+        _c_void_p,  # residual_out
+        _c_void_p,  # normed
+        ctypes.c_int,  # out_dtype
+        _c_void_p,  # gamma
+        _c_void_p,  # beta
+        _c_int64,  # rows
+        _c_int64,  # cols
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_linear.restype = ctypes.c_int
+    lib.b200tx_linear.argtypes = [
+        _c_void_p,  # a
+        _c_void_p,  # w
+        _c_void_p,  # bias
+        _c_void_p,  # out
+        ctypes.c_int,  # out_dtype
+        _c_int64,  # M
+        _c_int64,  # N
+        _c_int64,  # K
+        ctypes.c_int,  # epilogue
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_attention.restype = ctypes.c_int
+    lib.b200tx_attention.argtypes = [
+        _c_void_p,  # qkv
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # heads
+        _c_int64,  # head_dim
+        ctypes.c_float,  # scale
+        ctypes.c_int,  # causal
+        _c_void_p,  # stream
+    ]
+
+
+def library_path() -> Path:
+    return LIB_PATH
+
+
+def library_available() -> bool:
+    """Whether the shared library can be loaded (does not require a GPU)."""
+
+    try:
+        load()
+    except RuntimeError:
+        return False
+    return True
+
+
+def load() -> ctypes.CDLL:
+    """Load libb200tx once; raise RuntimeError with the reason on failure."""
+
+    global _lib, _load_error
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if _load_error is not None:
+            raise RuntimeError(_load_error)
+        if not LIB_PATH.exists():
+            _load_error = (
+                f"libb200tx.so not built at {LIB_PATH}; run build_native.py "
+                "(there is no CPU or Triton fallback)"
+            )
+            raise RuntimeError(_load_error)
+        try:
+            lib = ctypes.CDLL(str(LIB_PATH))
+        except OSError as exc:
+            _load_error = f"cannot load {LIB_PATH}: {exc}"
+            raise RuntimeError(_load_error) from exc
+        _declare(lib)
+        version = lib.b200tx_abi_version()
+        if version != ABI_VERSION:
+            _load_error = f"libb200tx ABI {version} != expected {ABI_VERSION}; rebuild it"
+            raise RuntimeError(_load_error)
+        _lib = lib
+        return lib
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        message = load().b200tx_last_error().decode("utf-8", "replace")
+        raise RuntimeError(f"{what} failed (status {status}): {message}")
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return F32
+    if dtype == torch.bfloat16:
+        return BF16
+    raise ValueError(f"unsupported dtype {dtype}; libb200tx takes float32 or bfloat16")
+
+
+def device_check() -> tuple[int, int, int]:
+    """Return (sm_count, cc_major, cc_minor) of the current device; raise if not sm_100."""
+
+    lib = load()
+    sm = ctypes.c_int(0)
+    major = ctypes.c_int(0)
+    minor = ctypes.c_int(0)
+    _check(
+        lib.b200tx_device_check(ctypes.byref(sm), ctypes.byref(major), ctypes.byref(minor)),
+        "b200tx_device_check",
+    )
+    return sm.value, major.value, minor.value
+
+
+def device_error(clear: bool = True) -> int:
+    """Read the device error word (synchronises the device)."""
+
+    lib = load()
+    code = ctypes.c_uint(0)
+    _check(lib.b200tx_device_error(int(clear), ctypes.byref(code)), "b200tx_device_error")
+    return int(code.value)
+
+
+def residual_layer_norm(
+    residual_in: torch.Tensor,
+    update: torch.Tensor | None,
+    residual_out: torch.Tensor | None,
+    normed: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+) -> None:
+    """Launch b200tx_residual_layer_norm on the current stream (no checks beyond the C side)."""
+
+    cols = residual_in.shape[-1]
+    rows = residual_in.numel() // cols
+    lib = load()
+    _check(
+        lib.b200tx_residual_layer_norm(
+            residual_in.data_ptr(),
+            dtype_code(residual_in.dtype),
+            None if update is None else update.data_ptr(),
+            F32 if update is None else dtype_code(update.dtype),
+            None if residual_out is None else residual_out.data_ptr(),
+            normed.data_ptr(),
+            dtype_code(normed.dtype),
+            gamma.data_ptr(),
+            beta.data_ptr(),
+            rows,
+            cols,
+            float(eps),
+            _stream(residual_in.device),
+        ),
+        "b200tx_residual_layer_norm",
+    )
+
+
+def linear(
+    a: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor | None,
+    out: torch.Tensor,
+    epilogue: int,
+) -> None:
+    """Launch b200tx_linear: out = epilogue(a . w^T + bias)."""
+
+    k = a.shape[-1]
+    m = a.numel() // k
+    n = w.shape[0]
+    lib = load()
+    _check(
+        lib.b200tx_linear(
+            a.data_ptr(),
+            w.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            out.data_ptr(),
+            dtype_code(out.dtype),
+            m,
+            n,
+            k,
+            int(epilogue),
+            _stream(a.device),
+        ),
+        "b200tx_linear",
+    )
+
+
+def attention(
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    batch: int,
+    seq: int,
+    heads: int,
+    head_dim: int,
+    scale: float,
+    causal: bool,
+) -> None:
+    """Launch b200tx_attention over a packed [B, S, 3D] projection."""
+
+    lib = load()
+    _check(
+        lib.b200tx_attention(
+            qkv.data_ptr(),
+            out.data_ptr(),
+            int(batch),
+            int(seq),
+            int(heads),
+            int(head_dim),
+            float(scale),
+            int(bool(causal)),
+            _stream(qkv.device),
+        ),
+        "b200tx_attention",
+    )
+
+
+__all__ = [
+    "ABI_VERSION",
+    "BF16",
+    "EPI_BIAS",
+    "EPI_BIAS_GELU",
+    "F32",
+    "attention",
+    "device_check",
+    "device_error",
+    "dtype_code",
+    "library_available",
+    "library_path",
+    "linear",
+    "load",
+    "residual_layer_norm",
+]
