@@ -1,0 +1,423 @@
+#!/usr/bin/env python3
+"""Forward-throughput benchmark of the sm_100a Transformer (one JSON line).
+
+Workload (N=1): BASELINE config C2 -- B=8, S=2048, D=1024, 16 heads
+(head_dim 64), 2 layers, causal, FFN 4096 exact GELU; x ~ N(0,1) from seed 1,
+weights = the reference module's seeded default init (seed 0).  A "step" is
+one full forward over that batch.  Under torchrun each rank runs its own C2
+batch (batch sharding, no collective): per-GPU work is fixed, ``scaling`` is
+"weak" and ``value`` is the total tokens/s of all ranks over the slowest
+rank's time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+``value``      tokens/s with x already in HBM, each step bracketed by CUDA
+               events on the launching stream, L2 flushed before every step.
+``e2e``        tokens/s through the public API with x in pinned host memory:
+               H2D copy of x, forward, D2H copy of the whole output, per step.
+``roofline``   the dominant kernel (by time) of the step, timed live with
+               CUDA events around its launches inside the timed region.
+``cpu_baseline`` the CPU oracle (numpy fp32 restatement of the reference
+               forward) on one batch row, on this host's cores.
+``--impl reference`` times that CPU restatement alone, as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+from types import SimpleNamespace
+
+REPO = Path(__file__).resolve().parent
+PACKAGE_DIR = REPO / "ml-guided-program-search-for-shape-specialized-transformer-optimization_b200"
+for _p in (str(PACKAGE_DIR), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+WORKLOAD = dict(batch_size=8, seq_len=2048, d_model=1024, num_heads=16, ffn_dim=4096, num_layers=2, causal=True)
+INPUT_SEED = 1
+WEIGHT_SEED = 0
+METRIC = "fwd tokens/s"
+UNIT = "tokens/s"
+WORKLOAD_NAME = "C2 resident mid shape: B8 S2048 D1024 H16(Dh64) F4096 L2 causal"
+L2_FLUSH_BYTES = 256 * 1024 * 1024
+
+
+def _env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def _peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _profile_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+
+    path = REPO / "profiles" / f"{kernel}_c2.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle",
+        0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.1) -> None:
+        self.device_index = device_index
+        self.period_s = period_s
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz: int | None = None
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        self._nvml = None
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid_index = self.device_index
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if visible:
+                parts = [p.strip() for p in visible.split(",") if p.strip()]
+                if self.device_index < len(parts) and parts[self.device_index].isdigit():
+                    uuid_index = int(parts[self.device_index])
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(uuid_index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+            return self
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def _run(self) -> None:
+        pynvml = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(int(pynvml.nvmlDeviceGetClockInfo(self._handle, pynvml.NVML_CLOCK_SM)))
+                mask = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(self._handle))
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period_s)
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
+
+    def summary(self) -> dict:
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(steps: int = 1, warmup: int = 0) -> dict:
+    """The oracle forward on one batch row of the workload, on this host's cores."""
+
+    from oracle import OfficialConfig, official_input, official_state_dict
+    from oracle.reference_forward import transformer_forward
+    from oracle.weights import state_to_numpy
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((info.get("num_threads", 1) for info in threadpool_info()), default=1)
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count() or 1
+    cfg = OfficialConfig(**WORKLOAD)
+    state = state_to_numpy(official_state_dict(cfg, seed=WEIGHT_SEED))
+    x = official_input(cfg, INPUT_SEED, batch_rows=slice(0, 1)).numpy()
+    kwargs = dict(num_heads=cfg.num_heads, num_layers=cfg.num_layers, causal=cfg.causal)
+    for _ in range(warmup):
+        transformer_forward(x, state, **kwargs)
+    times = []
+    for _ in range(max(1, steps)):
+        start = time.perf_counter()
+        transformer_forward(x, state, **kwargs)
+        times.append(time.perf_counter() - start)
+    per_step = statistics.median(times)
+    tokens = cfg.seq_len
+    return {
+        "value": tokens / per_step,
+        "unit": UNIT,
+        "cores": int(threads),
+        "kind": "port",
+        "sample": f"oracle (numpy fp32) forward of 1 of the 8 batch rows ({tokens} tokens), median of {len(times)}",
+        "seconds_per_sample": per_step,
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = _env_int("RANK", 0)
+    if rank != 0:
+        return
+    base = cpu_baseline(steps=args.steps, warmup=min(args.warmup, 1))
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": base["seconds_per_sample"] * 1000.0,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) input, seeded default-init weights)",
+        "config": {"workload": WORKLOAD_NAME, "sample": "one batch row per step", "global_batch": 1,
+                   "seq_len": WORKLOAD["seq_len"], "parallelism": "cpu"},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def build_model(device: torch.device):
+    from oracle import OfficialConfig, official_state_dict
+    from solution.transformer import UserOptimizedTransformer, copy_model_weights
+
+    cfg = SimpleNamespace(**WORKLOAD)
+    model = UserOptimizedTransformer(cfg)
+    copy_model_weights(official_state_dict(OfficialConfig(**WORKLOAD), seed=WEIGHT_SEED), model)
+    return model.to(device).eval()
+
+
+def run_gpu(args: argparse.Namespace) -> None:
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local_rank = _env_int("LOCAL_RANK", 0)
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        dist = dist_mod
+
+    from oracle import OfficialConfig, official_input
+    from solution import _native
+    from solution.transformer import KernelEventRecorder
+
+    _native.device_check()
+    cfg = OfficialConfig(**WORKLOAD)
+    model = build_model(device)
+    # Each rank owns its own C2 batch; rank r uses seed 1 + r (rank 0 = the BASELINE input).
+    x_host = official_input(cfg, INPUT_SEED + rank).pin_memory()
+    x_dev = x_host.to(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    tokens_per_rank = cfg.batch_size * cfg.seq_len
+
+    def barrier() -> None:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.inference_mode():
+        for _ in range(max(3, args.warmup)):
+            model(x_dev)
+        torch.cuda.synchronize()
+
+        recorder = KernelEventRecorder()
+        model.kernel_events = recorder
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        with ClockSampler(local_rank) as clocks:
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record()
+                model(x_dev)
+                ends[i].record()
+            barrier()
+        model.kernel_events = None
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        kernel_ms = recorder.durations_ms()
+
+        # End to end through the public API from pinned host memory.
+        out_host = torch.empty(x_host.shape, dtype=torch.float32).pin_memory()
+        for _ in range(2):
+            out_host.copy_(model(x_host.to(device, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_start = torch.cuda.Event(enable_timing=True)
+        e2e_end = torch.cuda.Event(enable_timing=True)
+        e2e_start.record()
+        for _ in range(args.steps):
+            y = model(x_host.to(device, non_blocking=True))
+            out_host.copy_(y, non_blocking=True)
+        e2e_end.record()
+        barrier()
+        e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
+
+    total_ms = sum(step_ms)
+    stats = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    total_ms_max, e2e_ms_max = stats.tolist()
+    ms_per_step = total_ms_max / args.steps
+    value = world * tokens_per_rank * args.steps / (total_ms_max / 1000.0)
+    e2e_value = world * tokens_per_rank / (e2e_ms_max / 1000.0)
+
+    # Dominant kernel of the step and its roofline.
+    per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
+    launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
+    dominant = max(per_role, key=per_role.get)
+    peaks, peak_source = _peaks()
+    b, s, d, f, layers = cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
+    m = b * s
+    flops_per_launch = {
+        "attention": 2.0 * b * s * s * d,  # causal, counted as 2BS^2D like the reference
+        "qkv_projection": 2.0 * m * 3 * d * d,
+        "attention_output_projection": 2.0 * m * d * d,
+        "ffn_input_projection": 2.0 * m * f * d,
+        "ffn_output_projection": 2.0 * m * d * f,
+    }
+    bytes_per_launch = {"residual_norm": 12.0 * m * d, "initial_norm": 6.0 * m * d}
+    avg_launch_ms = per_role[dominant] / max(1, launches[dominant])
+    if dominant in flops_per_launch:
+        achieved = flops_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e12
+        peak = float(peaks["bf16_tflops_sustained"])
+        roofline = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dominant,
+                    "algorithmic_per_launch": flops_per_launch[dominant]}
+    else:
+        achieved = bytes_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        roofline = {"bound": "hbm", "unit": "GB/s", "kernel": dominant,
+                    "algorithmic_per_launch": bytes_per_launch[dominant]}
+    roofline.update(
+        achieved=achieved,
+        peak=peak,
+        peak_source=f"{peak_source} ({'bf16_tflops_sustained' if roofline['bound'] == 'tensor' else 'hbm_gbs'})",
+        frac=achieved / peak,
+        traffic=_profile_traffic(dominant),
+        avg_launch_ms=avg_launch_ms,
+    )
+    attention_ms = per_role.get("attention", 0.0) / max(1, launches.get("attention", 1))
+    kernel_table = {
+        role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]} for role in sorted(per_role)
+    }
+    model_flops = layers * (2.0 * b * s * s * d + 8.0 * b * s * d * d + 4.0 * b * s * d * f)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": ms_per_step,
+            "p50_latency_ms": statistics.median(step_ms),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: x ~ N(0,1) seed 1+rank (CPU generator), reference default-init weights seed 0",
+            "config": {
+                "workload": WORKLOAD_NAME,
+                "global_batch": cfg.batch_size * world,
+                "seq_len": cfg.seq_len,
+                "parallelism": f"dp{world} (batch-sharded, no collective)",
+                "io_dtype": "float32 in/out, bf16 GEMM/attention operands, fp32 accumulation and residual",
+                "l2": "flushed (256 MB write) before every timed step",
+                "runtime": model.active_config.schedule.runtime.value,
+            },
+            "attention_tflops": flops_per_launch["attention"] / (attention_ms / 1000.0) / 1e12 if attention_ms else None,
+            "model_tflops": model_flops / (ms_per_step / 1000.0) / 1e12,
+            "kernels": kernel_table,
+            "roofline": roofline,
+            "e2e": {
+                "value": e2e_value,
+                "unit": UNIT,
+                "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
+                "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
+                "ms_per_step": e2e_ms_max,
+            },
+            "gpu_launches": int(sum(len(v) for v in kernel_ms.values())),
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.skip_cpu_baseline:
+            line["cpu_baseline"] = {
+                k: v for k, v in cpu_baseline(steps=1).items() if k in ("value", "unit", "cores", "kind", "sample")
+            }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("native", "reference"), default="native")
+    parser.add_argument("--skip-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.steps <= 0:
+        raise SystemExit("--steps must be positive")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -217,9 +217,6 @@ int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void
     return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: out_dtype %d", out_dtype);
   if (update != nullptr && update_dtype != B200TX_F32 && update_dtype != B200TX_BF16)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: update_dtype %d", update_dtype);
-  if (update != nullptr && in_dtype != B200TX_F32)
-    return fail(B200TX_ERR_UNSUPPORTED,
-                "residual_layer_norm: a residual add needs an F32 residual stream");
   DeviceState* dev = nullptr;
   int rc = current_device(&dev);
   if (rc != B200TX_OK) return rc;
@@ -238,15 +235,20 @@ int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void
                       aligned16(beta) && (update == nullptr || aligned16(update)) &&
                       (residual_out == nullptr || aligned16(residual_out));
   cudaError_t err;
-  if (update == nullptr) {
-    if (in_dtype == B200TX_F32)
+  if (in_dtype == B200TX_F32) {
+    if (update == nullptr)
       err = launch_norm_out<float, void>(a, out_dtype, vec_ok, stream);
+    else if (update_dtype == B200TX_BF16)
+      err = launch_norm_out<float, __nv_bfloat16>(a, out_dtype, vec_ok, stream);
     else
-      err = launch_norm_out<__nv_bfloat16, void>(a, out_dtype, vec_ok, stream);
-  } else if (update_dtype == B200TX_BF16) {
-    err = launch_norm_out<float, __nv_bfloat16>(a, out_dtype, vec_ok, stream);
+      err = launch_norm_out<float, float>(a, out_dtype, vec_ok, stream);
   } else {
-    err = launch_norm_out<float, float>(a, out_dtype, vec_ok, stream);
+    if (update == nullptr)
+      err = launch_norm_out<__nv_bfloat16, void>(a, out_dtype, vec_ok, stream);
+    else if (update_dtype == B200TX_BF16)
+      err = launch_norm_out<__nv_bfloat16, __nv_bfloat16>(a, out_dtype, vec_ok, stream);
+    else
+      err = launch_norm_out<__nv_bfloat16, float>(a, out_dtype, vec_ok, stream);
   }
   if (err != cudaSuccess) return cuda_fail(err, "residual_layer_norm launch");
   return B200TX_OK;

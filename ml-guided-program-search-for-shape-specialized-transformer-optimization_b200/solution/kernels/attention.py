@@ -1,0 +1,87 @@
+"""Causal flash attention on the sm_100a tensor cores (csrc/attention_kernels.cuh).
+
+Replaces the reference's streaming Dh64 kernel
+(solution/shape14/triton_streaming_dh64.py:68-346), the shape13 kernel
+(solution/kernels/attention/triton_s1024_dh32.py:72-366), the SDPA and
+query-blocked reference operators (solution/operators/attention/sdpa.py:76-170)
+and ``split_qkv`` (solution/operators/projection/qkv_layout.py:22-50): the
+kernel reads Q/K/V head tiles straight out of the packed ``[B, S, 3D]`` QKV
+projection and writes the ``[B, S, D]`` context the out-projection consumes.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _native
+from ._common import is_sm100_cuda, launch, library_ready, require
+
+SM100_FLASH_ATTENTION_BACKEND = "sm100_flash_attention"
+HEAD_DIM = 64
+
+
+def sm100_flash_attention_available() -> bool:
+    return library_ready()
+
+
+def can_use_sm100_flash_attention(qkv: torch.Tensor, num_heads: int) -> bool:
+    """Whether the flash kernel can read this packed projection (never raises)."""
+
+    try:
+        if not library_ready() or torch.is_grad_enabled() or not is_sm100_cuda(qkv):
+            return False
+        if qkv.dtype != torch.bfloat16 or qkv.ndim != 3 or not qkv.is_contiguous():
+            return False
+        if num_heads <= 0 or qkv.shape[-1] != 3 * num_heads * HEAD_DIM:
+            return False
+        return qkv.data_ptr() % 16 == 0
+    except Exception:  # noqa: BLE001 - predicate contract: never raise
+        return False
+
+
+def sm100_flash_attention(
+    qkv: torch.Tensor,
+    num_heads: int,
+    *,
+    causal: bool = True,
+    out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, str]:
+    """``softmax(q k^T / 8 [+ causal]) v`` per head; returns the ``[B, S, D]`` context."""
+
+    if not can_use_sm100_flash_attention(qkv, num_heads):
+        raise RuntimeError("sm100 flash attention is ineligible for the requested inputs")
+    batch, seq, width = qkv.shape
+    d_model = width // 3
+    result = (
+        torch.empty((batch, seq, d_model), dtype=torch.bfloat16, device=qkv.device)
+        if out is None
+        else out
+    )
+    require(
+        tuple(result.shape) == (batch, seq, d_model)
+        and result.dtype == torch.bfloat16
+        and result.is_contiguous()
+        and result.data_ptr() % 16 == 0,
+        "out must be a contiguous, 16-byte aligned bf16 [B, S, D] tensor",
+    )
+    launch(
+        _native.attention,
+        qkv,
+        result,
+        batch,
+        seq,
+        num_heads,
+        HEAD_DIM,
+        HEAD_DIM**-0.5,
+        causal,
+    )
+    return result, SM100_FLASH_ATTENTION_BACKEND
+
+
+__all__ = [
+    "HEAD_DIM",
+    "SM100_FLASH_ATTENTION_BACKEND",
+    "can_use_sm100_flash_attention",
+    "sm100_flash_attention",
+    "sm100_flash_attention_available",
+]

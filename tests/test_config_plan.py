@@ -1,0 +1,215 @@
+"""ConfigSpec / PlanBuilder contract on the CPU (no GPU needed).
+
+Mirrors the reference's program tests (tests/solution/test_program_primitives.py
+plan/trace equality on a tiny model, rejection codes) for the sm100 program.
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import replace
+
+import pytest
+import torch
+
+from solution.config import (
+    CONFIG_SCHEMA_VERSION,
+    ConfigSpec,
+    PrecisionPlan,
+    RuntimeBackend,
+    ScheduleConfig,
+    Sm100AttentionParams,
+    Sm100GemmParams,
+    Sm100NormParams,
+    default_program,
+    default_schedule,
+    portable_config,
+    portable_streamed_config,
+)
+from solution.plan import ExecutionContext
+from solution.plan_builder import (
+    CompileRejection,
+    ConfigRejectedError,
+    ConstraintViolation,
+    HardwareCapabilities,
+    PlanBuilder,
+)
+
+
+def _context(**overrides: object) -> ExecutionContext:
+    base = dict(
+        batch_size=2,
+        seq_len=128,
+        d_model=256,
+        num_heads=4,
+        causal=True,
+        device=torch.device("cuda", 0),
+        dtype=torch.float32,
+        training=False,
+        grad_enabled=False,
+        input_contiguous=True,
+        has_valid_token_mask=False,
+        mask_compatible=True,
+        ffn_dim=1024,
+        num_layers=2,
+    )
+    base.update(overrides)
+    return ExecutionContext(**base)  # type: ignore[arg-type]
+
+
+B200 = HardwareCapabilities.sm100()
+
+
+def _codes(result) -> set[str]:  # noqa: ANN001
+    return {v.code for v in result.violations}
+
+
+def test_round_trip_and_canonical_json() -> None:
+    cfg = portable_config()
+    payload = json.loads(cfg.canonical_json())
+    assert payload["schema_version"] == CONFIG_SCHEMA_VERSION == 5
+    again = ConfigSpec.from_dict(payload)
+    assert again == cfg
+    assert again.config_id == cfg.config_id
+    assert cfg.config_id.startswith("cfg-") and len(cfg.config_id) == 4 + 64
+
+
+def test_config_id_changes_with_schedule() -> None:
+    a = portable_config()
+    b = ConfigSpec(program=default_program(), schedule=default_schedule(RuntimeBackend.CUDA_GRAPH))
+    assert a.config_id != b.config_id
+
+
+def test_schema_v4_and_unknown_fields_are_rejected() -> None:
+    payload = portable_config().to_dict()
+    payload["schema_version"] = 4
+    with pytest.raises(ValueError):
+        ConfigSpec.from_dict(payload)
+    payload = portable_config().to_dict()
+    payload["program"]["extra"] = "x"
+    with pytest.raises(ValueError):
+        ConfigSpec.from_dict(payload)
+    payload = portable_config().to_dict()
+    payload["program"]["attention"] = "triton_streaming_dh64"
+    with pytest.raises(ValueError):
+        ConfigSpec.from_dict(payload)
+
+
+def test_launch_params_must_name_a_built_variant() -> None:
+    with pytest.raises(ValueError):
+        Sm100GemmParams(tile_m=128, tile_n=128, tile_k=64, stages=4)
+    with pytest.raises(ValueError):
+        Sm100AttentionParams(block_m=64)
+    with pytest.raises(ValueError):
+        Sm100NormParams(rows_per_cta=4)
+    with pytest.raises(ValueError):
+        Sm100GemmParams(tile_m=0)
+
+
+def test_launch_records_required_exactly() -> None:
+    schedule = replace(default_schedule(), attention_launch=None)
+    with pytest.raises(ValueError, match="attention_launch"):
+        ConfigSpec(program=default_program(), schedule=schedule)
+
+
+def test_schedule_field_rules() -> None:
+    with pytest.raises(ValueError):
+        ScheduleConfig(runtime=RuntimeBackend.EAGER, batch_tile_size=4)
+    with pytest.raises(ValueError):
+        ScheduleConfig(runtime=RuntimeBackend.STREAMED)
+    with pytest.raises(ValueError):
+        ScheduleConfig(runtime=RuntimeBackend.EAGER, reuse_unchanged_input=True)
+    with pytest.raises(ValueError):
+        ScheduleConfig(runtime="compiled_forward")
+    s = ScheduleConfig(runtime=RuntimeBackend.BATCH_TILED_CUDA_GRAPH, batch_tile_size=8)
+    assert s.batch_tile_size == 8
+
+
+def test_plan_accepted_on_sm100_snapshot() -> None:
+    result = PlanBuilder().evaluate(portable_config(), _context(), B200)
+    assert result.accepted, result.violations
+    plan = result.require_plan()
+    trace = plan.expected_trace.to_dict()
+    assert trace["attention_calls"] == 2
+    assert trace["residual_norm_calls"] == 4
+    assert trace["initial_norm_calls"] == 1
+    assert trace["attention_backend"] == "sm100_flash"
+    assert trace["complete"] is True
+    described = plan.describe()
+    assert described["causal_mask"] == "online_causal"
+    assert described["attention_output_layout"] == "bsd"
+    assert plan.output_dtype == "float32"
+
+
+def test_precision_plan_sets_update_dtypes() -> None:
+    cfg = ConfigSpec(
+        program=default_program(PrecisionPlan.BF16_CORE_FP32_UPDATES), schedule=default_schedule()
+    )
+    plan = PlanBuilder().build(cfg, _context(), B200)
+    assert plan.attention_output_update_dtype == "float32"
+    assert plan.ffn_output_update_dtype == "float32"
+    plan = PlanBuilder().build(portable_config(), _context(), B200)
+    assert plan.attention_output_update_dtype == "bfloat16"
+
+
+@pytest.mark.parametrize(
+    ("overrides", "hardware", "code"),
+    [
+        ({"device": torch.device("cpu")}, HardwareCapabilities("cpu", None, None, None, True), "requires_cuda"),
+        ({}, HardwareCapabilities("cuda", (9, 0), 232448, 132, True), "requires_sm100"),
+        ({}, replace(B200, kernel_library=False), "backend_unavailable"),
+        ({"training": True}, B200, "requires_inference"),
+        ({"grad_enabled": True}, B200, "requires_inference"),
+        ({"dtype": torch.float16}, B200, "unsupported_dtype"),
+        ({"input_contiguous": False}, B200, "requires_contiguous_input"),
+        ({"has_valid_token_mask": True}, B200, "mask_not_supported"),
+        ({"d_model": 256, "num_heads": 2}, B200, "unsupported_shape"),  # head_dim 128
+        ({"d_model": 250, "num_heads": 5}, B200, "unsupported_shape"),
+        ({"ffn_dim": 1020}, B200, "unsupported_shape"),
+        ({"num_heads": 3}, B200, "not_divisible"),
+        ({"seq_len": 0}, B200, "non_positive"),
+    ],
+)
+def test_structured_rejections(overrides: dict, hardware: HardwareCapabilities, code: str) -> None:
+    result = PlanBuilder().evaluate(portable_config(), _context(**overrides), hardware)
+    assert not result.accepted
+    assert code in _codes(result)
+    with pytest.raises(ConfigRejectedError):
+        result.require_plan()
+
+
+def test_runtime_rules() -> None:
+    tiled = ConfigSpec(
+        program=default_program(),
+        schedule=default_schedule(RuntimeBackend.BATCH_TILED_CUDA_GRAPH, batch_tile_size=2),
+    )
+    assert "tile_not_smaller_than_batch" in _codes(PlanBuilder().evaluate(tiled, _context(), B200))
+    plan = PlanBuilder().build(tiled, _context(batch_size=8), B200)
+    assert plan.inner_context.batch_size == 2 and plan.outer_context.batch_size == 8
+
+    streamed = portable_streamed_config(microbatch_size=3)
+    assert "microbatch_not_divisor" in _codes(PlanBuilder().evaluate(streamed, _context(batch_size=8), B200))
+    assert "microbatch_exceeds_batch" in _codes(PlanBuilder().evaluate(streamed, _context(batch_size=2), B200))
+    plan = PlanBuilder().build(portable_streamed_config(microbatch_size=2), _context(batch_size=8), B200)
+    assert plan.use_streamed_execution and plan.inner_context.batch_size == 2
+
+
+def test_rejection_types() -> None:
+    v = ConstraintViolation("c", "f", "m")
+    assert v.to_dict() == {"code": "c", "field": "f", "message": "m"}
+    with pytest.raises(ValueError):
+        CompileRejection("cfg-x", ())
+    err = ConfigRejectedError(CompileRejection("cfg-x", (v,)))
+    assert "f:c" in str(err)
+
+
+def test_detect_on_cpu_host_is_not_sm100() -> None:
+    caps = HardwareCapabilities.detect(torch.device("cpu"))
+    assert caps.device_type == "cpu" and not caps.is_sm100
+
+
+def test_type_errors() -> None:
+    with pytest.raises(TypeError):
+        PlanBuilder().evaluate("not a config", _context(), B200)  # type: ignore[arg-type]
+    with pytest.raises(TypeError):
+        PlanBuilder().evaluate(portable_config(), "ctx", B200)  # type: ignore[arg-type]

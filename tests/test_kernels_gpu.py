@@ -1,0 +1,210 @@
+"""Kernel-level parity: each libb200tx kernel, called through the C ABI, against
+the CPU oracle on the same seeded inputs, including ragged and tiny edge cases.
+
+Tolerances: the fp32 residual sum is exact; fp32 outputs agree to fp32
+rounding; bf16 outputs carry one bf16 rounding (relative 2^-9), so they are
+checked at rel-L2 <= 4e-3; attention rounds P to bf16 before P.V (as the
+reference casts probabilities to the activation dtype), checked at
+rel-L2 <= 1e-2 and max-abs <= 2e-2.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import parity_errors
+
+from oracle import attention_core, gelu_erf, layer_norm
+from solution import _native
+from solution.kernels import (
+    sm100_flash_attention,
+    sm100_initial_layer_norm,
+    sm100_linear,
+    sm100_residual_layer_norm,
+)
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+def _bf16_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _clean_error_word():
+    _native.device_error(clear=True)
+    yield
+    assert _native.device_error(clear=True) == 0, "a kernel wait timed out"
+
+
+@pytest.mark.parametrize(
+    ("rows", "cols", "update_dtype", "in_dtype"),
+    [
+        (1, 128, torch.bfloat16, torch.float32),
+        (7, 256, torch.bfloat16, torch.float32),
+        (1000, 768, torch.bfloat16, torch.float32),
+        (513, 1024, torch.float32, torch.float32),
+        (64, 2048, torch.bfloat16, torch.float32),
+        (33, 4096, torch.bfloat16, torch.float32),
+        (17, 96, torch.bfloat16, torch.float32),  # generic path (cols % 128 != 0)
+        (9, 4104, torch.float32, torch.float32),  # generic path, wide
+        (40, 1024, torch.bfloat16, torch.bfloat16),  # bf16 residual input
+    ],
+)
+def test_residual_layer_norm(rows: int, cols: int, update_dtype: torch.dtype, in_dtype: torch.dtype) -> None:
+    g = torch.Generator().manual_seed(rows * 31 + cols)
+    resid = (torch.randn(rows, cols, generator=g) * 2).to(in_dtype)
+    update = torch.randn(rows, cols, generator=g).to(update_dtype)
+    norm = torch.nn.LayerNorm(cols)
+    with torch.no_grad():
+        norm.weight.copy_(torch.randn(cols, generator=g))
+        norm.bias.copy_(torch.randn(cols, generator=g))
+    norm = norm.to(DEV)
+    ref_r = resid.float().numpy() + update.float().numpy()
+    ref_n = layer_norm(ref_r, norm.weight.detach().cpu().numpy(), norm.bias.detach().cpu().numpy())
+    with torch.inference_mode():
+        r, n, marker = sm100_residual_layer_norm(resid.to(DEV), update.to(DEV), norm, final_boundary=False)
+        _, n32, _ = sm100_residual_layer_norm(resid.to(DEV), update.to(DEV), norm, final_boundary=True)
+    torch.cuda.synchronize()
+    assert marker == "sm100_residual_layer_norm"
+    np.testing.assert_array_equal(r.cpu().numpy(), ref_r.astype(np.float32))
+    max_abs, rel = parity_errors(_bf16_np(n), ref_n)
+    assert rel < 4e-3 and max_abs < 6e-2, (max_abs, rel)
+    max_abs, rel = parity_errors(n32.cpu().numpy(), ref_n)
+    assert max_abs < 2e-4 and rel < 1e-5, (max_abs, rel)
+
+
+def test_residual_layer_norm_in_place() -> None:
+    g = torch.Generator().manual_seed(5)
+    resid = torch.randn(300, 1024, generator=g)
+    update = torch.randn(300, 1024, generator=g).to(torch.bfloat16)
+    norm = torch.nn.LayerNorm(1024).to(DEV)
+    expected = resid.numpy() + update.float().numpy()
+    stream = resid.to(DEV)
+    with torch.inference_mode():
+        sm100_residual_layer_norm(stream, update.to(DEV), norm, final_boundary=False, residual_out=stream)
+    np.testing.assert_array_equal(stream.cpu().numpy(), expected)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_initial_layer_norm(dtype: torch.dtype) -> None:
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(129, 768, generator=g).to(dtype)
+    norm = torch.nn.LayerNorm(768).to(DEV)
+    ref = layer_norm(x.float().numpy(), np.ones(768, np.float32), np.zeros(768, np.float32))
+    with torch.inference_mode():
+        n, marker = sm100_initial_layer_norm(x.to(DEV), norm)
+    assert marker == "sm100_initial_layer_norm" and n.dtype == torch.bfloat16
+    max_abs, rel = parity_errors(_bf16_np(n), ref)
+    assert rel < 4e-3 and max_abs < 4e-2
+
+
+@pytest.mark.parametrize(
+    ("m", "n", "k", "gelu", "out_dtype", "bias"),
+    [
+        (1, 8, 8, False, torch.float32, True),
+        (127, 264, 72, True, torch.bfloat16, True),
+        (128, 256, 64, False, torch.float32, False),
+        (129, 768, 768, True, torch.float32, True),
+        (1000, 3072, 1024, False, torch.bfloat16, True),
+        (4097, 1024, 4096, False, torch.float32, True),
+        (300, 2304, 768, True, torch.bfloat16, True),
+    ],
+)
+def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias: bool) -> None:
+    g = torch.Generator().manual_seed(m + 7 * n + 13 * k)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) / k**0.5).to(torch.bfloat16)
+    b = torch.randn(n, generator=g) if bias else None
+    ref = a.float().numpy() @ w.float().numpy().T
+    if b is not None:
+        ref = ref + b.numpy()
+    if gelu:
+        ref = gelu_erf(ref.astype(np.float32))
+    with torch.inference_mode():
+        out, marker = sm100_linear(
+            a.to(DEV), w.to(DEV), None if b is None else b.to(DEV), gelu=gelu, out_dtype=out_dtype
+        )
+    torch.cuda.synchronize()
+    assert marker == ("sm100_linear_gelu" if gelu else "sm100_linear")
+    max_abs, rel = parity_errors(out.float().cpu().numpy(), ref)
+    if out_dtype == torch.float32:
+        assert rel < 1e-5, rel
+    else:
+        assert rel < 4e-3, rel
+
+
+def test_linear_three_dimensional_input() -> None:
+    g = torch.Generator().manual_seed(1)
+    a = torch.randn(3, 50, 256, generator=g).to(torch.bfloat16)
+    w = torch.randn(512, 256, generator=g).to(torch.bfloat16)
+    with torch.inference_mode():
+        out, _ = sm100_linear(a.to(DEV), w.to(DEV), None, out_dtype=torch.float32)
+    ref = a.float().numpy() @ w.float().numpy().T
+    assert out.shape == (3, 50, 512)
+    assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
+
+
+def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int) -> None:
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(batch, seq, 3 * heads * 64, generator=g).to(torch.bfloat16)
+    q, k, v = qkv.float().view(batch, seq, 3, heads, 64).permute(2, 0, 3, 1, 4).numpy()
+    ref = attention_core(q, k, v, causal).transpose(0, 2, 1, 3).reshape(batch, seq, heads * 64)
+    with torch.inference_mode():
+        out, marker = sm100_flash_attention(qkv.to(DEV), heads, causal=causal)
+    torch.cuda.synchronize()
+    assert marker == "sm100_flash_attention"
+    max_abs, rel = parity_errors(_bf16_np(out), ref)
+    assert rel < 1e-2 and max_abs < 2e-2, (batch, seq, heads, causal, max_abs, rel)
+
+
+@pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal"),
+    [
+        (1, 1, 1, True),
+        (2, 17, 1, True),
+        (1, 127, 2, True),
+        (1, 128, 1, True),
+        (3, 129, 2, True),
+        (1, 300, 5, True),
+        (2, 1000, 2, True),
+        (1, 1, 1, False),
+        (2, 200, 2, False),
+        (1, 385, 1, False),
+    ],
+)
+def test_attention_edges(batch: int, seq: int, heads: int, causal: bool) -> None:
+    _attention_case(batch, seq, heads, causal, seed=batch * 1000 + seq + heads)
+
+
+def test_attention_long_sequence() -> None:
+    """Many KV tiles per query tile (64 on the last), running max moved repeatedly."""
+
+    _attention_case(1, 8192, 2, True, seed=77)
+
+
+def test_attention_is_deterministic() -> None:
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(2, 700, 3 * 4 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    with torch.inference_mode():
+        a, _ = sm100_flash_attention(qkv, 4)
+        b, _ = sm100_flash_attention(qkv, 4)
+    assert torch.equal(a, b)
+
+
+def test_attention_large_logits_stay_finite() -> None:
+    """Scores of |s| ~ 100 exercise the stale-max threshold and rescaling."""
+
+    g = torch.Generator().manual_seed(8)
+    qkv = (torch.randn(1, 512, 3 * 64, generator=g) * 6).to(torch.bfloat16)
+    q, k, v = qkv.float().view(1, 512, 3, 1, 64).permute(2, 0, 3, 1, 4).numpy()
+    ref = attention_core(q, k, v, True).transpose(0, 2, 1, 3).reshape(1, 512, 64)
+    with torch.inference_mode():
+        out, _ = sm100_flash_attention(qkv.to(DEV), 1)
+    got = _bf16_np(out)
+    assert np.isfinite(got).all()
+    max_abs, rel = parity_errors(got, ref)
+    assert rel < 2e-2, rel
