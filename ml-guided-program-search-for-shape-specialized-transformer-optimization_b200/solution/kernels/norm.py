@@ -82,7 +82,11 @@ def sm100_residual_layer_norm(
     if out_dtype is None:
         out_dtype = torch.float32 if final_boundary else torch.bfloat16
     require(out_dtype in _IO, "out_dtype must be float32 or bfloat16")
-    residual = torch.empty_like(value) if residual_out is None else residual_out
+    residual = (
+        torch.empty(value.shape, dtype=torch.float32, device=value.device)
+        if residual_out is None
+        else residual_out
+    )
     normalized = (
         torch.empty(value.shape, dtype=out_dtype, device=value.device)
         if normalized_out is None
