@@ -20,6 +20,9 @@ rank's time.
 ``cpu_baseline`` the CPU oracle (numpy fp32 restatement of the reference
                forward) on one batch row, on this host's cores.
 ``--impl reference`` times that CPU restatement alone, as the reference arm.
+``--kernel NAME`` times one libb200tx kernel alone on its C2-shaped operands
+               (attention, qkv, out_proj, ffn_in, ffn_out, residual_norm) and
+               prints its own JSON line; ncu profiles in profiles/ use this mode.
 """
 
 from __future__ import annotations
@@ -403,6 +406,81 @@ def run_gpu(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def run_kernel(args: argparse.Namespace) -> None:
+    """Time one libb200tx kernel on its C2 operands (CUDA events, L2 flushed)."""
+
+    from solution import _native
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _native.device_check()
+    g = torch.Generator(device=device).manual_seed(0)
+    b, s, d, h, f = (WORKLOAD[k] for k in ("batch_size", "seq_len", "d_model", "num_heads", "ffn_dim"))
+    m = b * s
+
+    def randn(*shape, scale=1.0, dtype=torch.bfloat16):
+        return (torch.randn(*shape, device=device, generator=g) * scale).to(dtype)
+
+    gemm = {
+        "qkv": (d, 3 * d, False),
+        "out_proj": (d, d, False),
+        "ffn_in": (d, f, True),
+        "ffn_out": (f, d, False),
+    }
+    if args.kernel in ("attention", "attention_single"):
+        qkv = randn(b, s, 3 * d)
+        out = torch.empty(b, s, d, device=device, dtype=torch.bfloat16)
+        variant = _native.ATTN_PAIRED if args.kernel == "attention" else _native.ATTN_SINGLE
+        launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
+        work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
+    elif args.kernel in gemm:
+        k, n, gelu = gemm[args.kernel]
+        a = randn(m, k)
+        w = randn(n, k, scale=k**-0.5)
+        bias = randn(n, dtype=torch.float32)
+        out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        epi = _native.EPI_BIAS_GELU if gelu else _native.EPI_BIAS
+        launch = lambda: _native.linear(a, w, bias, out, epi)  # noqa: E731
+        work, unit, bound = 2.0 * m * n * k, "TFLOP/s", "tensor"
+    elif args.kernel == "residual_norm":
+        resid = randn(m, d, dtype=torch.float32)
+        upd = randn(m, d)
+        normed = torch.empty(m, d, device=device, dtype=torch.bfloat16)
+        gamma = torch.ones(d, device=device)
+        beta = torch.zeros(d, device=device)
+        launch = lambda: _native.residual_layer_norm(resid, upd, resid, normed, gamma, beta, 1e-5)  # noqa: E731
+        work, unit, bound = 12.0 * m * d, "GB/s", "hbm"
+    else:
+        raise SystemExit(f"unknown kernel {args.kernel}")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for _ in range(max(3, args.warmup)):
+        launch()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record()
+        launch()
+        ends[i].record()
+    torch.cuda.synchronize()
+    if _native.device_error() != 0:
+        raise SystemExit("a kernel wait timed out")
+    ms = statistics.median(s.elapsed_time(e) for s, e in zip(starts, ends))
+    peaks, source = _peaks()
+    if unit == "TFLOP/s":
+        achieved = work / (ms / 1000.0) / 1e12
+        peak = float(peaks["bf16_tflops"])
+    else:
+        achieved = work / (ms / 1000.0) / 1e9
+        peak = float(peaks["hbm_gbs"])
+    print(json.dumps({
+        "kernel": args.kernel, "workload": WORKLOAD_NAME, "ms": ms, "achieved": achieved, "unit": unit,
+        "bound": bound, "peak": peak, "peak_source": f"{source} burst", "frac": achieved / peak,
+        "steps": args.steps,
+    }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -410,11 +488,19 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument(
+        "--kernel",
+        choices=("attention", "attention_single", "qkv", "out_proj", "ffn_in", "ffn_out", "residual_norm"),
+        default=None,
+    )
     args = parser.parse_args()
     if args.steps <= 0:
         raise SystemExit("--steps must be positive")
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.kernel is not None:
+        run_kernel(args)
         return
     run_gpu(args)
 

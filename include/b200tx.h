@@ -39,6 +39,10 @@ extern "C" {
 #define B200TX_EPI_BIAS 0
 #define B200TX_EPI_BIAS_GELU 1
 
+/* Attention kernel variants (b200tx_attention_ex). */
+#define B200TX_ATTN_PAIRED 0 /* two 128-row query tiles per CTA, P kept in TMEM */
+#define B200TX_ATTN_SINGLE 1 /* one 128-row query tile per CTA, P through shared memory */
+
 /* Status codes. */
 #define B200TX_OK 0
 #define B200TX_ERR_INVALID_ARGUMENT -1
@@ -113,6 +117,18 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
  */
 int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
                      int64_t head_dim, float scale, int causal, cudaStream_t stream);
+
+/*
+ * b200tx_attention with an explicit kernel variant (B200TX_ATTN_PAIRED, the
+ * default of b200tx_attention, or B200TX_ATTN_SINGLE).  Both compute the same
+ * function; the execution plan's attention launch record picks one.
+ * Replaces the same reference operators as b200tx_attention; the variant is the
+ * sm100 counterpart of the reference's attention launch parameters
+ * (TritonAttentionParams, solution/config.py:189-234).
+ */
+int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                        int64_t head_dim, float scale, int causal, int variant,
+                        cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -335,4 +335,338 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Paired-tile variant: one CTA = two consecutive 128-row query tiles of one
+// (batch, head), one CTA per SM, 320 threads.
+//   warp 0      TMA: Q0/Q1 once; K_j and V_j through separate 3-slot rings
+//   warp 1      one thread issues, per query tile w, S_w = Q_w K_j^T (SS UMMA)
+//               and O_w += P_w V_j (TS UMMA: P read straight from TMEM),
+//               ping-ponging the two tiles so one tile's MMAs run while the
+//               other tile's softmax works
+//   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1: one row per
+//               thread, the whole 128-column S row loaded into registers in one
+//               pass, bf16 P written back over S in TMEM (tcgen05.st)
+// TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,320), O1 [320,384).
+// tcgen05.mma operations of one thread execute in issue order, so the
+// S_w(j+1) UMMA, issued after O_w += P_w(j) V_j, never overwrites P_w(j) early,
+// and the commit that signals S_w(j+1) also proves that P_w(j) V_j is done.
+// ---------------------------------------------------------------------------
+constexpr int kAttn2Threads = 320;
+// The running max moves only once a row maximum exceeds it by this much (log2
+// units): P may then reach 2^8, which fp32 exp2, fp32 O and fp32 l carry
+// exactly, and O is rescaled in TMEM only on those rare steps.
+constexpr float kAttnMaxSlack = 8.0f;
+constexpr int kAttn2Ring = 3;
+constexpr uint32_t kAttn2TmemCols = 512;
+constexpr size_t kAttn2SmemBytes = 1024 + kAttnTileBytes * (2 + 2 * kAttn2Ring);  // 129 KB
+
+__global__ void __launch_bounds__(kAttn2Threads, 1)
+    attention_fwd_dh64_pair_kernel(const __grid_constant__ CUtensorMap tmap_qkv, AttnArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t q_full_bar;
+  __shared__ uint64_t k_full_bar[kAttn2Ring];
+  __shared__ uint64_t k_empty_bar[kAttn2Ring];
+  __shared__ uint64_t v_full_bar[kAttn2Ring];
+  __shared__ uint64_t v_empty_bar[kAttn2Ring];
+  __shared__ uint64_t s_full_bar[2];
+  __shared__ uint64_t p_full_bar[2];
+  __shared__ uint64_t o_final_bar[2];
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* smem_q = smem;                                  // Q0, Q1
+  uint8_t* smem_k = smem + 2 * kAttnTileBytes;             // K ring
+  uint8_t* smem_v = smem_k + kAttn2Ring * kAttnTileBytes;  // V ring
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int num_pairs = (args.num_q_tiles + 1) >> 1;
+  const int hb_count = args.heads * args.batch;
+  const int pair = num_pairs - 1 - static_cast<int>(blockIdx.x / hb_count);  // longest first
+  const int hb = static_cast<int>(blockIdx.x % hb_count);
+  const int head = hb % args.heads;
+  const int batch = hb / args.heads;
+  const int kv_tiles_total = (args.seq + kAttnBN - 1) / kAttnBN;
+  const int q_tile0 = 2 * pair;
+  const bool active1 = q_tile0 + 1 < args.num_q_tiles;
+  const int n_kv0 = args.causal ? q_tile0 + 1 : kv_tiles_total;
+  const int n_kv1 = active1 ? (args.causal ? q_tile0 + 2 : kv_tiles_total) : 0;
+  const int n_kv = n_kv0 > n_kv1 ? n_kv0 : n_kv1;
+  const int d_model = args.heads * kAttnDh;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensor_map(&tmap_qkv);
+    mbar_init(&q_full_bar, 1);
+    for (int s = 0; s < kAttn2Ring; ++s) {
+      mbar_init(&k_full_bar[s], 1);
+      mbar_init(&k_empty_bar[s], 1);
+      mbar_init(&v_full_bar[s], 1);
+      mbar_init(&v_empty_bar[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&s_full_bar[w], 1);
+      mbar_init(&p_full_bar[w], 128);
+      mbar_init(&o_final_bar[w], 1);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, kAttn2TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&q_full_bar, (active1 ? 2u : 1u) * kAttnTileBytes);
+      tma_load_3d(smem_q, &tmap_qkv, &q_full_bar, head * kAttnDh, q_tile0 * kAttnBM, batch);
+      if (active1)
+        tma_load_3d(smem_q + kAttnTileBytes, &tmap_qkv, &q_full_bar, head * kAttnDh,
+                    (q_tile0 + 1) * kAttnBM, batch);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int slot = j % kAttn2Ring;
+        const uint32_t ph = (j / kAttn2Ring) & 1;
+        if (!mbar_wait(&k_empty_bar[slot], ph ^ 1u, kErrAttnProducerWait, &abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full_bar[slot], kAttnTileBytes);
+        tma_load_3d(smem_k + slot * kAttnTileBytes, &tmap_qkv, &k_full_bar[slot],
+                    d_model + head * kAttnDh, j * kAttnBN, batch);
+        if (!mbar_wait(&v_empty_bar[slot], ph ^ 1u, kErrAttnProducerWait, &abort_flag)) {
+          ++issued;  // K_j is in flight
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full_bar[slot], kAttnTileBytes);
+        tma_load_3d(smem_v + slot * kAttnTileBytes, &tmap_qkv, &v_full_bar[slot],
+                    2 * d_model + head * kAttnDh, j * kAttnBN, batch);
+        ++issued;
+      }
+      // Wait for the loads still in flight (complete already on the normal path).
+      volatile int no_abort = 0;
+      mbar_wait(&q_full_bar, 0, kErrAttnProducerWait, &no_abort);
+      const int first = issued > kAttn2Ring ? issued - kAttn2Ring : 0;
+      for (int j = first; j < issued; ++j) {
+        const uint32_t ph = (j / kAttn2Ring) & 1;
+        mbar_wait(&k_full_bar[j % kAttn2Ring], ph, kErrAttnProducerWait, &no_abort);
+        mbar_wait(&v_full_bar[j % kAttn2Ring], ph, kErrAttnProducerWait, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kAttnBM, kAttnBN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kAttnBM, kAttnDh, false, true);
+      const uint32_t q_addr = smem_u32(smem_q);
+      bool issued_any = false;
+      // S_w = Q_w K_j^T; commits s_full[w] and, when K_j has no further user,
+      // frees its ring slot.
+      auto issue_qk = [&](int w, int j) -> bool {
+        const int slot = j % kAttn2Ring;
+        if (w == 0 || !(j < n_kv0)) {  // first user of K_j waits for it
+          if (!mbar_wait(&k_full_bar[slot], (j / kAttn2Ring) & 1, kErrAttnMmaWait, &abort_flag))
+            return false;
+          tc_fence_after();
+        }
+        const uint32_t k_addr = smem_u32(smem_k + slot * kAttnTileBytes);
+        const uint32_t qa = q_addr + w * kAttnTileBytes;
+        const uint32_t s_tmem = tmem_base + w * kAttnBN;
+#pragma unroll
+        for (int k = 0; k < kAttnDh / 16; ++k) {
+          umma_bf16_ss(s_tmem, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(k_addr + k * 32, 16, 1024),
+                       idesc_qk, k != 0 ? 1u : 0u);
+        }
+        issued_any = true;
+        umma_commit(&s_full_bar[w]);
+        const bool last_user = (w == 1) || !(j < n_kv1);
+        if (last_user) umma_commit(&k_empty_bar[slot]);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full_bar, 0, kErrAttnMmaWait, &abort_flag);
+      if (ok) tc_fence_after();
+      if (ok && n_kv0 > 0) ok = issue_qk(0, 0);
+      if (ok && n_kv1 > 0) ok = issue_qk(1, 0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int slot = j % kAttn2Ring;
+        bool v_ready = false;
+        for (int w = 0; w < 2 && ok; ++w) {
+          const int n_kv_this = w == 0 ? n_kv0 : n_kv1;
+          if (!(j < n_kv_this)) continue;
+          // Softmax of (w, j) done: P_w(j) is in TMEM, O_w rescaled.
+          if (!mbar_wait(&p_full_bar[w], j & 1, kErrAttnMmaWait, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!v_ready) {
+            if (!mbar_wait(&v_full_bar[slot], (j / kAttn2Ring) & 1, kErrAttnMmaWait, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            v_ready = true;
+          }
+          const uint32_t v_addr = smem_u32(smem_v + slot * kAttnTileBytes);
+          const uint32_t p_tmem = tmem_base + w * kAttnBN;
+          const uint32_t o_tmem = tmem_base + 2 * kAttnBN + w * kAttnDh;
+#pragma unroll
+          for (int k = 0; k < kAttnBN / 16; ++k) {
+            umma_bf16_ts(o_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 16 * 128, kAttnTileBytes, 1024),
+                         idesc_pv, (j | k) != 0 ? 1u : 0u);
+          }
+          const bool last_v_user = (w == 1) || !(j < n_kv1);
+          if (last_v_user) umma_commit(&v_empty_bar[slot]);
+          if (j + 1 < n_kv_this) {
+            ok = issue_qk(w, j + 1);
+          } else {
+            umma_commit(&o_final_bar[w]);
+          }
+        }
+      }
+      if (issued_any) {
+        umma_commit(&drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait(&drain_bar, 0, kErrAttnMmaWait, &no_abort);
+      }
+    }
+  } else {
+    // Softmax warpgroup w = (warp - 2) / 4 owns query tile q_tile0 + w; warp
+    // `warp` reads TMEM lanes 32*(warp%4) .. +31 = its 32 query rows.
+    const int w = (warp - 2) >> 2;
+    const int n_kv_mine = w == 0 ? n_kv0 : n_kv1;
+    const int q_tile = q_tile0 + w;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q_idx = q_tile * kAttnBM + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem_base + lane_off + w * kAttnBN;
+    const uint32_t o_tmem = tmem_base + lane_off + 2 * kAttnBN + w * kAttnDh;
+    const float c = args.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = n_kv_mine > 0;
+    for (int j = 0; ok && j < n_kv_mine; ++j) {
+      ok = mbar_wait(&s_full_bar[w], j & 1, kErrAttnSoftmaxWait, &abort_flag);
+      if (__any_sync(0xffffffffu, !ok)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      uint32_t s[kAttnBN];
+      tmem_ld_32cols(s_tmem + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_ld_32cols(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_ld_32cols(s_tmem + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+      tmem_ld_32cols(s_tmem + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+      tmem_wait_ld();
+      int limit = kAttnBN;
+      if (args.causal) {
+        if (j == q_tile) limit = row + 1;
+      } else if ((j + 1) * kAttnBN > args.seq) {
+        limit = args.seq - j * kAttnBN;
+      }
+      if (limit < kAttnBN) {
+#pragma unroll
+        for (int i = 0; i < kAttnBN; ++i)
+          if (i >= limit) s[i] = __float_as_uint(-INFINITY);
+      }
+      // Row maximum: eight independent max3 chains, then a short tree.
+      float mp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(s[k]);
+#pragma unroll
+      for (int i = 8; i < kAttnBN; i += 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mp[k] = max3(mp[k], __uint_as_float(s[i + k]), __uint_as_float(s[i + 8 + k]));
+      }
+      const float mx = fmaxf(max3(mp[0], mp[1], mp[2]), max3(max3(mp[3], mp[4], mp[5]), mp[6], mp[7]));
+      const float mx_scaled = mx * c;
+      const bool need = mx_scaled > m_run + kAttnMaxSlack;
+      const float m_new = need ? mx_scaled : m_run;
+      const float alpha = need ? fast_exp2(m_run - m_new) : 1.0f;  // 0 on the first tile
+      // P = exp2(s * c - m): one f32x2 FMA per pair, one MUFU ex2 per element,
+      // packed to bf16 and stored straight back over S; the row sum adds the
+      // fp32 probabilities in four independent f32x2 chains.
+      const uint64_t c2 = f32x2(c, c);
+      const uint64_t neg_m2 = f32x2(-m_new, -m_new);
+      uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int quarter_row = 0; quarter_row < 4; ++quarter_row) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = quarter_row * 32 + 2 * i;
+          const float2 x = unpack_f32x2(
+              fma_f32x2(f32x2(__uint_as_float(s[e]), __uint_as_float(s[e + 1])), c2, neg_m2));
+          const float p0 = fast_exp2(x.x);
+          const float p1 = fast_exp2(x.y);
+          packed[i] = pack_bf16x2(p0, p1);
+          acc[i & 3] = add_f32x2(acc[i & 3], f32x2(p0, p1));
+        }
+        tmem_st_16cols(s_tmem + quarter_row * 16, packed);
+      }
+      // Rescale O_w now that S is dead (fewer live registers).  O_w is idle here: the commit behind s_full also covers O_w += P_w(j-1) V.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(o_tmem + cc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32cols(o_tmem + cc * 32, r);
+        }
+      }
+      const float2 a01 = unpack_f32x2(add_f32x2(add_f32x2(acc[0], acc[1]), add_f32x2(acc[2], acc[3])));
+      const float row_sum = a01.x + a01.y;
+      tmem_wait_st();
+      l_run = l_run * alpha + row_sum;
+      m_run = m_new;
+      tc_fence_before();
+      mbar_arrive(&p_full_bar[w]);
+    }
+    if (ok) {
+      ok = mbar_wait(&o_final_bar[w], 0, kErrAttnSoftmaxWait, &abort_flag);
+      const bool all_ok = !__any_sync(0xffffffffu, !ok);
+      __syncwarp();
+      if (all_ok) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+        __nv_bfloat16* out_row =
+            args.out + (static_cast<int64_t>(batch) * args.seq + q_idx) * d_model + head * kAttnDh;
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(o_tmem + cc * 32, r);
+          tmem_wait_ld();
+          if (q_idx < args.seq) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              st_global_v4(out_row + cc * 32 + i,
+                           pack_bf16x2(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l));
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAttn2TmemCols);
+  }
+}
+
 }  // namespace b200tx

@@ -22,7 +22,7 @@
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 constexpr int kMaxDevices = 64;
 
 thread_local std::string g_last_error;
@@ -47,7 +47,7 @@ struct DeviceState {
   int cc_major = 0;
   int cc_minor = 0;
   bool gemm_attr[4] = {false, false, false, false};
-  bool attn_attr = false;
+  bool attn_attr[2] = {false, false};
 };
 
 std::mutex g_mutex;
@@ -326,8 +326,8 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
   return B200TX_OK;
 }
 
-int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
-                     int64_t head_dim, float scale, int causal, cudaStream_t stream) {
+int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                        int64_t head_dim, float scale, int causal, int variant, cudaStream_t stream) {
   if (qkv == nullptr || out == nullptr)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: null tensor pointer");
   if (batch <= 0 || seq <= 0 || heads <= 0)
@@ -336,11 +336,14 @@ int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int
   if (head_dim != b200tx::kAttnDh)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: head_dim %lld (only 64 is built)",
                 (long long)head_dim);
+  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: variant %d", variant);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
   const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
-  const int64_t blocks = q_tiles * heads * batch;
+  const int64_t units = variant == B200TX_ATTN_PAIRED ? (q_tiles + 1) / 2 : q_tiles;
+  const int64_t blocks = units * heads * batch;
   if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: problem too large for one launch");
   DeviceState* dev = nullptr;
@@ -366,22 +369,30 @@ int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int
   args.num_q_tiles = static_cast<int>(q_tiles);
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
+  using KernelFn = void (*)(CUtensorMap, b200tx::AttnArgs);
+  const KernelFn kernel = variant == B200TX_ATTN_PAIRED ? b200tx::attention_fwd_dh64_pair_kernel
+                                                        : b200tx::attention_fwd_dh64_kernel;
+  const size_t smem = variant == B200TX_ATTN_PAIRED ? b200tx::kAttn2SmemBytes : b200tx::kAttnSmemBytes;
+  const int threads = variant == B200TX_ATTN_PAIRED ? b200tx::kAttn2Threads : b200tx::kAttnThreads;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!dev->attn_attr) {
-      cudaError_t err =
-          cudaFuncSetAttribute(b200tx::attention_fwd_dh64_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(b200tx::kAttnSmemBytes));
+    if (!dev->attn_attr[variant]) {
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
       if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
-      dev->attn_attr = true;
+      dev->attn_attr[variant] = true;
     }
   }
-  b200tx::attention_fwd_dh64_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttnThreads,
-                                      b200tx::kAttnSmemBytes, stream>>>(map_qkv, args);
+  kernel<<<static_cast<unsigned>(blocks), threads, smem, stream>>>(map_qkv, args);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "attention launch");
   return B200TX_OK;
+}
+
+int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t head_dim, float scale, int causal, cudaStream_t stream) {
+  return b200tx_attention_ex(qkv, out, batch, seq, heads, head_dim, scale, causal,
+                             B200TX_ATTN_PAIRED, stream);
 }
 
 }  // extern "C"

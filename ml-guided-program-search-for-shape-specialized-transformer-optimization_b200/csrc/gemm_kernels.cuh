@@ -10,10 +10,12 @@
 // Both operands are K-major (nn.Linear weight layout), so one kernel covers
 // every projection of the block.
 //
-// Structure: persistent CTAs (one per SM), 192 threads.
+// Structure: persistent CTAs (one per SM), 320 threads.
 //   warp 0      TMA producer: A tile 128x64 and W tile 256x64 per stage, 4-stage ring
 //   warp 1      one elected thread issues 4 UMMAs (128x256x16) per stage
-//   warps 2..5  epilogue: TMEM -> registers (tcgen05.ld 32x32b), + bias,
+//   warps 2..9  epilogue: two warps per TMEM lane quarter, each owning 128 of the
+//               256 accumulator columns: TMEM -> registers (tcgen05.ld 32x32b,
+//               double-buffered), + bias (staged once per tile in shared memory),
 //               optional GELU, cast, 16-byte global stores
 // The fp32 accumulator for a 128x256 tile uses 256 TMEM columns; two of them
 // (all 512 columns) let the epilogue of tile t overlap the MMAs of tile t+1.
@@ -29,7 +31,8 @@ constexpr int kGemmBM = 128;
 constexpr int kGemmBN = 256;
 constexpr int kGemmBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpilogueThreads = 256;
 constexpr uint32_t kGemmTmemCols = 512;
 constexpr uint32_t kGemmTileABytes = kGemmBM * kGemmBK * 2;  // 16 KB
 constexpr uint32_t kGemmTileBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
@@ -45,8 +48,29 @@ struct GemmArgs {
   int num_m_tiles, num_n_tiles;
 };
 
+// Exact-erf GELU, 0.5 x (1 + erf(x / sqrt 2)), with erf from Abramowitz &
+// Stegun, Handbook of Mathematical Functions, formula 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7.
+// With h = 0.5 |x| poly(t) exp(-z^2):  GELU(x) = x - h for x >= 0, and -h for
+// x < 0 (odd symmetry of erf: 1 + erf(-z) = poly(t) exp(-z^2)).  One reciprocal and one exp2 on MUFU, the rest on FMA;
+// the approximation error is ~70x below one bf16 rounding of the output.
 __device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f;
+  constexpr float kA2 = -0.284496736f;
+  constexpr float kA3 = 1.421413741f;
+  constexpr float kA4 = -1.453152027f;
+  constexpr float kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float z = fabsf(x) * kInvSqrt2;
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(kP, z, 1.0f)));
+  const float poly = t * fmaf(fmaf(fmaf(fmaf(kA5, t, kA4), t, kA3), t, kA2), t, kA1);
+  const float e = fast_exp2(-(z * z) * kLog2e);
+  const float h = 0.5f * fabsf(x) * poly * e;
+  return x >= 0.0f ? x - h : -h;
 }
 
 template <int EPI, typename OutT>
@@ -61,6 +85,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  __shared__ float bias_tile[8][kGemmBN / 2];  // one 128-column slice per epilogue warp
 
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* smem_a = smem;
@@ -80,7 +105,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full_bar[a], 1);
-      mbar_init(&acc_empty_bar[a], 128);
+      mbar_init(&acc_empty_bar[a], kGemmEpilogueThreads);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -176,69 +201,78 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its lane quarter) and
+    // the column half (w-2)/4 of the 256-column accumulator.
     const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
+      const int m_tile = tile / args.num_n_tiles;
+      const int n_tile = tile - m_tile * args.num_n_tiles;
+      // Stage this warp's 128 bias values for the tile before waiting for the
+      // accumulator.  Each warp owns its slice, so only warp-level
+      // synchronisation is needed (no CTA barrier that an aborting warp could
+      // leave the others stuck on).
+      float* warp_bias = bias_tile[warp - 2];
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int col = n_tile * kGemmBN + col_half * (kGemmBN / 2) + i * 32 + lane;
+        warp_bias[i * 32 + lane] = (args.bias != nullptr && col < args.N) ? __ldg(args.bias + col) : 0.f;
+      }
+      __syncwarp();
       bool ok = mbar_wait(&acc_full_bar[acc], acc_phase, kErrGemmEpilogueWait, &abort_flag);
       if (__any_sync(0xffffffffu, !ok)) break;
       __syncwarp();
       tc_fence_after();
-      const int m_tile = tile / args.num_n_tiles;
-      const int n_tile = tile - m_tile * args.num_n_tiles;
       const int64_t row = static_cast<int64_t>(m_tile) * kGemmBM + row_in_tile;
-      const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kGemmBN;
-#pragma unroll 1
-      for (int c = 0; c < kGemmBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32cols(taddr + c * 32, r);
-        tmem_wait_ld();
-        if (c == kGemmBN / 32 - 1) {
-          // The accumulator is fully read: hand it back to the MMA warp
-          // before the last stores.
-          tc_fence_before();
-          mbar_arrive(&acc_empty_bar[acc]);
-        }
-        const int col0 = n_tile * kGemmBN + c * 32;
-        if (row >= args.M || col0 >= args.N) continue;
-        // N % 8 == 0 (checked on the host), so each group of eight columns is
-        // either entirely inside the matrix or entirely past its edge.
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             acc * kGemmBN + col_half * (kGemmBN / 2);
+      constexpr int kChunks = kGemmBN / 2 / 32;  // 4 chunks of 32 columns
+      uint32_t buf[2][32];
+      tmem_ld_32cols(taddr, buf[0]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        if (c + 1 < kChunks) tmem_ld_32cols(taddr + (c + 1) * 32, buf[(c + 1) & 1]);
+        const uint32_t (&r)[32] = buf[c & 1];
+        const int col_in_tile = col_half * (kGemmBN / 2) + c * 32;
+        const int col0 = n_tile * kGemmBN + col_in_tile;
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (args.bias != nullptr && col0 + i < args.N)
-            b = __ldg(reinterpret_cast<const float4*>(args.bias + col0 + i));
-          v[i + 0] = __uint_as_float(r[i + 0]) + b.x;
-          v[i + 1] = __uint_as_float(r[i + 1]) + b.y;
-          v[i + 2] = __uint_as_float(r[i + 2]) + b.z;
-          v[i + 3] = __uint_as_float(r[i + 3]) + b.w;
-        }
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + warp_bias[c * 32 + i];
         if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
         }
-        OutT* out_row = static_cast<OutT*>(args.out) + row * args.N + col0;
-        if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+        if (row < args.M) {
+          // N % 8 == 0 (checked on the host): each group of eight columns is
+          // either entirely inside the matrix or entirely past its edge.
+          OutT* out_row = static_cast<OutT*>(args.out) + row * args.N + col0;
+          if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            if (col0 + i < args.N)
-              st_global_v4(out_row + i, pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
-                           pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
-          }
-        } else {
+            for (int i = 0; i < 32; i += 8) {
+              if (col0 + i < args.N)
+                st_global_v4(out_row + i, pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+            }
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            if (col0 + i < args.N)
-              st_global_v4(out_row + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]),
-                           __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3]));
+            for (int i = 0; i < 32; i += 4) {
+              if (col0 + i < args.N)
+                st_global_v4(out_row + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]),
+                             __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3]));
+            }
           }
         }
+        if (c + 1 < kChunks) tmem_wait_ld();
       }
+      // Every column of this thread's lane has been read: release the buffer.
+      tc_fence_before();
+      mbar_arrive(&acc_empty_bar[acc]);
     }
   }
 

@@ -15,12 +15,14 @@ from pathlib import Path
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200tx.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 F32 = 0
 BF16 = 1
 EPI_BIAS = 0
 EPI_BIAS_GELU = 1
+ATTN_PAIRED = 0
+ATTN_SINGLE = 1
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -82,6 +84,19 @@ def _declare(lib: ctypes.CDLL) -> None:
         _c_int64,  # head_dim
         ctypes.c_float,  # scale
         ctypes.c_int,  # causal
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_attention_ex.restype = ctypes.c_int
+    lib.b200tx_attention_ex.argtypes = [
+        _c_void_p,  # qkv
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # heads
+        _c_int64,  # head_dim
+        ctypes.c_float,  # scale
+        ctypes.c_int,  # causal
+        ctypes.c_int,  # variant
         _c_void_p,  # stream
     ]
 
@@ -243,12 +258,13 @@ def attention(
     head_dim: int,
     scale: float,
     causal: bool,
+    variant: int = ATTN_PAIRED,
 ) -> None:
-    """Launch b200tx_attention over a packed [B, S, 3D] projection."""
+    """Launch b200tx_attention_ex over a packed [B, S, 3D] projection."""
 
     lib = load()
     _check(
-        lib.b200tx_attention(
+        lib.b200tx_attention_ex(
             qkv.data_ptr(),
             out.data_ptr(),
             int(batch),
@@ -257,14 +273,17 @@ def attention(
             int(head_dim),
             float(scale),
             int(bool(causal)),
+            int(variant),
             _stream(qkv.device),
         ),
-        "b200tx_attention",
+        "b200tx_attention_ex",
     )
 
 
 __all__ = [
     "ABI_VERSION",
+    "ATTN_PAIRED",
+    "ATTN_SINGLE",
     "BF16",
     "EPI_BIAS",
     "EPI_BIAS_GELU",

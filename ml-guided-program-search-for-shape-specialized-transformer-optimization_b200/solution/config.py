@@ -149,7 +149,10 @@ def _exact_fields(value: dict[str, Any], expected: frozenset[str], *, field: str
 # sets are rejected by the dataclasses, so a search never proposes a variant
 # that does not exist.
 SM100_GEMM_VARIANTS = frozenset({(128, 256, 64, 4)})
-SM100_ATTENTION_VARIANTS = frozenset({(128, 128, 3)})
+# (block_m, block_n, kv_stages): block_m 256 = two 128-row query tiles per CTA
+# with P kept in TMEM (B200TX_ATTN_PAIRED); block_m 128 = one query tile per
+# CTA with P staged through shared memory (B200TX_ATTN_SINGLE).
+SM100_ATTENTION_VARIANTS = frozenset({(256, 128, 3), (128, 128, 3)})
 SM100_NORM_ROWS_PER_CTA = frozenset({8})
 
 
@@ -190,7 +193,7 @@ class Sm100GemmParams:
 class Sm100AttentionParams:
     """Tile shape of the tcgen05 flash attention (csrc/attention_kernels.cuh)."""
 
-    block_m: int = 128
+    block_m: int = 256
     block_n: int = 128
     kv_stages: int = 3
 
@@ -205,6 +208,12 @@ class Sm100AttentionParams:
 
     def to_dict(self) -> dict[str, int]:
         return {"block_m": self.block_m, "block_n": self.block_n, "kv_stages": self.kv_stages}
+
+    @property
+    def kernel_variant(self) -> int:
+        """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE)."""
+
+        return 0 if self.block_m == 256 else 1
 
     @classmethod
     def from_dict(cls, payload: object) -> Sm100AttentionParams:

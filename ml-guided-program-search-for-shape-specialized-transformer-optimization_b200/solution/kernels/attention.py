@@ -45,6 +45,7 @@ def sm100_flash_attention(
     *,
     causal: bool = True,
     out: torch.Tensor | None = None,
+    variant: int = _native.ATTN_PAIRED,
 ) -> tuple[torch.Tensor, str]:
     """``softmax(q k^T / 8 [+ causal]) v`` per head; returns the ``[B, S, D]`` context."""
 
@@ -74,6 +75,7 @@ def sm100_flash_attention(
         HEAD_DIM,
         HEAD_DIM**-0.5,
         causal,
+        variant,
     )
     return result, SM100_FLASH_ATTENTION_BACKEND
 

@@ -544,6 +544,9 @@ class UserOptimizedTransformer(nn.Module):
         out_update = _DTYPES[plan.attention_output_update_dtype]
         ffn_update = _DTYPES[plan.ffn_output_update_dtype]
         n_layers = len(self.layers)
+        attention_variant = (
+            plan.attention_launch.kernel_variant if plan.attention_launch is not None else 0
+        )
 
         flat_in = value.reshape(rows, d_model)
         output = torch.empty((batch, seq, d_model), dtype=value.dtype, device=device)
@@ -597,7 +600,9 @@ class UserOptimizedTransformer(nn.Module):
                 planned_backend=plan.qkv_projection_backend.value,
             )
             token = rec.start("attention")
-            _, marker = sm100_flash_attention(qkv, heads, causal=causal, out=context)
+            _, marker = sm100_flash_attention(
+                qkv, heads, causal=causal, out=context, variant=attention_variant
+            )
             rec.stop(token)
             _strict_backend_marker(
                 marker,

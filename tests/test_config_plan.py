@@ -100,6 +100,8 @@ def test_launch_params_must_name_a_built_variant() -> None:
         Sm100GemmParams(tile_m=128, tile_n=128, tile_k=64, stages=4)
     with pytest.raises(ValueError):
         Sm100AttentionParams(block_m=64)
+    assert Sm100AttentionParams().kernel_variant == 0
+    assert Sm100AttentionParams(block_m=128).kernel_variant == 1
     with pytest.raises(ValueError):
         Sm100NormParams(rows_per_cta=4)
     with pytest.raises(ValueError):

@@ -194,6 +194,8 @@ def test_argument_errors_are_reported_before_any_launch() -> None:
     buf = ctypes.create_string_buffer(64)
     rc = lib.b200tx_attention(buf, buf, 1, 128, 1, 128, ctypes.c_float(0.125), 1, None)
     assert rc == -2 and b"head_dim" in lib.b200tx_last_error()
+    rc = lib.b200tx_attention_ex(buf, buf, 1, 128, 1, 64, ctypes.c_float(0.125), 1, 7, None)
+    assert rc == -1 and b"variant" in lib.b200tx_last_error()
     rc = lib.b200tx_linear(buf, buf, None, buf, 1, 16, 20, 64, 0, None)
     assert rc == -2 and b"multiples of 8" in lib.b200tx_last_error()
     rc = lib.b200tx_residual_layer_norm(buf, 5, None, 0, None, buf, 1, buf, buf, 4, 8, ctypes.c_float(1e-5), None)

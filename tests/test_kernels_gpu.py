@@ -148,17 +148,20 @@ def test_linear_three_dimensional_input() -> None:
     assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
 
 
-def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int) -> None:
+VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE]
+
+
+def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, variant: int) -> None:
     g = torch.Generator().manual_seed(seed)
     qkv = torch.randn(batch, seq, 3 * heads * 64, generator=g).to(torch.bfloat16)
     q, k, v = qkv.float().view(batch, seq, 3, heads, 64).permute(2, 0, 3, 1, 4).numpy()
     ref = attention_core(q, k, v, causal).transpose(0, 2, 1, 3).reshape(batch, seq, heads * 64)
     with torch.inference_mode():
-        out, marker = sm100_flash_attention(qkv.to(DEV), heads, causal=causal)
+        out, marker = sm100_flash_attention(qkv.to(DEV), heads, causal=causal, variant=variant)
     torch.cuda.synchronize()
     assert marker == "sm100_flash_attention"
     max_abs, rel = parity_errors(_bf16_np(out), ref)
-    assert rel < 1e-2 and max_abs < 2e-2, (batch, seq, heads, causal, max_abs, rel)
+    assert rel < 1e-2 and max_abs < 2e-2, (batch, seq, heads, causal, variant, max_abs, rel)
 
 
 @pytest.mark.parametrize(
@@ -174,28 +177,45 @@ def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int) -
         (1, 1, 1, False),
         (2, 200, 2, False),
         (1, 385, 1, False),
+        (2, 256, 3, True),  # even number of query tiles
+        (1, 384, 2, True),  # odd: the last pair has one tile
     ],
 )
-def test_attention_edges(batch: int, seq: int, heads: int, causal: bool) -> None:
-    _attention_case(batch, seq, heads, causal, seed=batch * 1000 + seq + heads)
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_attention_edges(batch: int, seq: int, heads: int, causal: bool, variant: int) -> None:
+    _attention_case(batch, seq, heads, causal, seed=batch * 1000 + seq + heads, variant=variant)
 
 
-def test_attention_long_sequence() -> None:
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_attention_long_sequence(variant: int) -> None:
     """Many KV tiles per query tile (64 on the last), running max moved repeatedly."""
 
-    _attention_case(1, 8192, 2, True, seed=77)
+    _attention_case(1, 8192, 2, True, seed=77, variant=variant)
 
 
-def test_attention_is_deterministic() -> None:
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_attention_is_deterministic(variant: int) -> None:
     g = torch.Generator().manual_seed(3)
     qkv = torch.randn(2, 700, 3 * 4 * 64, generator=g).to(torch.bfloat16).to(DEV)
     with torch.inference_mode():
-        a, _ = sm100_flash_attention(qkv, 4)
-        b, _ = sm100_flash_attention(qkv, 4)
+        a, _ = sm100_flash_attention(qkv, 4, variant=variant)
+        b, _ = sm100_flash_attention(qkv, 4, variant=variant)
     assert torch.equal(a, b)
 
 
-def test_attention_large_logits_stay_finite() -> None:
+def test_attention_variants_agree() -> None:
+    g = torch.Generator().manual_seed(13)
+    qkv = torch.randn(3, 1000, 3 * 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    with torch.inference_mode():
+        a, _ = sm100_flash_attention(qkv, 2, variant=_native.ATTN_PAIRED)
+        b, _ = sm100_flash_attention(qkv, 2, variant=_native.ATTN_SINGLE)
+    max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
+    # Two bf16 results of different summation orders: a few bf16 ulps apart.
+    assert rel < 5e-3 and max_abs < 4e-2
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_attention_large_logits_stay_finite(variant: int) -> None:
     """Scores of |s| ~ 100 exercise the stale-max threshold and rescaling."""
 
     g = torch.Generator().manual_seed(8)
@@ -203,7 +223,7 @@ def test_attention_large_logits_stay_finite() -> None:
     q, k, v = qkv.float().view(1, 512, 3, 1, 64).permute(2, 0, 3, 1, 4).numpy()
     ref = attention_core(q, k, v, True).transpose(0, 2, 1, 3).reshape(1, 512, 64)
     with torch.inference_mode():
-        out, _ = sm100_flash_attention(qkv.to(DEV), 1)
+        out, _ = sm100_flash_attention(qkv.to(DEV), 1, variant=variant)
     got = _bf16_np(out)
     assert np.isfinite(got).all()
     max_abs, rel = parity_errors(got, ref)
