@@ -416,6 +416,10 @@ def run_kernel(args: argparse.Namespace) -> None:
     _native.device_check()
     g = torch.Generator(device=device).manual_seed(0)
     b, s, d, h, f = (WORKLOAD[k] for k in ("batch_size", "seq_len", "d_model", "num_heads", "ffn_dim"))
+    if args.shape:
+        b, s, h = (int(v) for v in args.shape.split(","))
+        d = h * 64
+        f = 4 * d
     m = b * s
 
     def randn(*shape, scale=1.0, dtype=torch.bfloat16):
@@ -427,10 +431,14 @@ def run_kernel(args: argparse.Namespace) -> None:
         "ffn_in": (d, f, True),
         "ffn_out": (f, d, False),
     }
-    if args.kernel in ("attention", "attention_single"):
+    if args.kernel in ("attention", "attention_paired", "attention_single"):
         qkv = randn(b, s, 3 * d)
         out = torch.empty(b, s, d, device=device, dtype=torch.bfloat16)
-        variant = _native.ATTN_PAIRED if args.kernel == "attention" else _native.ATTN_SINGLE
+        variant = {
+            "attention": _native.ATTN_QUAD,
+            "attention_paired": _native.ATTN_PAIRED,
+            "attention_single": _native.ATTN_SINGLE,
+        }[args.kernel]
         launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
         work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
     elif args.kernel in gemm:
@@ -475,7 +483,9 @@ def run_kernel(args: argparse.Namespace) -> None:
         achieved = work / (ms / 1000.0) / 1e9
         peak = float(peaks["hbm_gbs"])
     print(json.dumps({
-        "kernel": args.kernel, "workload": WORKLOAD_NAME, "ms": ms, "achieved": achieved, "unit": unit,
+        "kernel": args.kernel,
+        "workload": WORKLOAD_NAME if not args.shape else f"B{b} S{s} H{h} D{d} F{f}",
+        "ms": ms, "achieved": achieved, "unit": unit,
         "bound": bound, "peak": peak, "peak_source": f"{source} burst", "frac": achieved / peak,
         "steps": args.steps,
     }), flush=True)
@@ -488,9 +498,19 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")
     parser.add_argument(
         "--kernel",
-        choices=("attention", "attention_single", "qkv", "out_proj", "ffn_in", "ffn_out", "residual_norm"),
+        choices=(
+            "attention",
+            "attention_paired",
+            "attention_single",
+            "qkv",
+            "out_proj",
+            "ffn_in",
+            "ffn_out",
+            "residual_norm",
+        ),
         default=None,
     )
     args = parser.parse_args()

@@ -42,6 +42,7 @@ extern "C" {
 /* Attention kernel variants (b200tx_attention_ex). */
 #define B200TX_ATTN_PAIRED 0 /* two 128-row query tiles per CTA, P kept in TMEM */
 #define B200TX_ATTN_SINGLE 1 /* one 128-row query tile per CTA, P through shared memory */
+#define B200TX_ATTN_QUAD 2   /* four 128-row query tiles per CTA, 64-row KV tiles, P in TMEM */
 
 /* Status codes. */
 #define B200TX_OK 0
@@ -119,8 +120,8 @@ int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int
                      int64_t head_dim, float scale, int causal, cudaStream_t stream);
 
 /*
- * b200tx_attention with an explicit kernel variant (B200TX_ATTN_PAIRED, the
- * default of b200tx_attention, or B200TX_ATTN_SINGLE).  Both compute the same
+ * b200tx_attention with an explicit kernel variant (B200TX_ATTN_QUAD, the
+ * default of b200tx_attention, B200TX_ATTN_PAIRED or B200TX_ATTN_SINGLE).  Both compute the same
  * function; the execution plan's attention launch record picks one.
  * Replaces the same reference operators as b200tx_attention; the variant is the
  * sm100 counterpart of the reference's attention launch parameters

@@ -669,4 +669,357 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Quad-tile variant: one CTA = four consecutive 128-row query tiles of one
+// (batch, head) against 64-row KV tiles; one CTA per SM, 576 threads.
+//   warp 0       TMA: Q0..Q3 once; K_j, V_j (64 x 64) through a 6-slot ring each
+//   warp 1       one thread issues, per query tile w, S_w = Q_w K_j^T
+//                (4 x 128x64x16 SS UMMAs) and O_w += P_w V_j (4 x 128x64x16 TS
+//                UMMAs, P read from TMEM), cycling over the four tiles
+//   warps 2..17  softmax: warps 2+4w .. 5+4w own query tile w, one row per
+//                thread, 64 scores per step
+// With four tiles in flight, the serial chain of one tile (softmax ->
+// P.V and next Q.K^T on the tensor core -> TMEM load) overlaps the exp2 work
+// of the other three, so the MUFU pipe, not latency, bounds the kernel.
+// TMEM (512 columns): S_w/P_w at 64w .. 64w+63 (P packed into the first 32),
+// O_w at 256 + 64w .. +63.
+// ---------------------------------------------------------------------------
+constexpr int kAttn4Tiles = 4;
+constexpr int kAttn4BN = 64;
+constexpr int kAttn4Ring = 6;
+constexpr int kAttn4Threads = 64 + kAttn4Tiles * 128;
+constexpr uint32_t kAttn4TmemCols = 512;
+constexpr uint32_t kAttn4KvBytes = kAttn4BN * kAttnDh * 2;  // 8 KB
+constexpr size_t kAttn4SmemBytes =
+    1024 + kAttn4Tiles * kAttnTileBytes + 2 * kAttn4Ring * kAttn4KvBytes;  // 161 KB
+constexpr float kAttn4MaxSlack = 8.0f;
+
+__global__ void __launch_bounds__(kAttn4Threads, 1)
+    attention_fwd_dh64_quad_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                                   const __grid_constant__ CUtensorMap tmap_kv, AttnArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t q_full_bar;
+  __shared__ uint64_t k_full_bar[kAttn4Ring];
+  __shared__ uint64_t k_empty_bar[kAttn4Ring];
+  __shared__ uint64_t v_full_bar[kAttn4Ring];
+  __shared__ uint64_t v_empty_bar[kAttn4Ring];
+  __shared__ uint64_t s_full_bar[kAttn4Tiles];
+  __shared__ uint64_t p_full_bar[kAttn4Tiles];
+  __shared__ uint64_t o_final_bar[kAttn4Tiles];
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* smem_q = smem;
+  uint8_t* smem_k = smem + kAttn4Tiles * kAttnTileBytes;
+  uint8_t* smem_v = smem_k + kAttn4Ring * kAttn4KvBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int num_quads = (args.num_q_tiles + kAttn4Tiles - 1) / kAttn4Tiles;
+  const int hb_count = args.heads * args.batch;
+  const int quad = num_quads - 1 - static_cast<int>(blockIdx.x / hb_count);  // longest first
+  const int hb = static_cast<int>(blockIdx.x % hb_count);
+  const int head = hb % args.heads;
+  const int batch = hb / args.heads;
+  const int kv_total = (args.seq + kAttn4BN - 1) / kAttn4BN;
+  const int q_tile0 = kAttn4Tiles * quad;
+  auto n_kv_of = [&](int w) -> int {
+    const int q = q_tile0 + w;
+    if (q >= args.num_q_tiles) return 0;
+    if (!args.causal) return kv_total;
+    const int n = 2 * q + 2;
+    return n < kv_total ? n : kv_total;
+  };
+  int n_kv = 0;
+#pragma unroll
+  for (int w = 0; w < kAttn4Tiles; ++w) n_kv = n_kv > n_kv_of(w) ? n_kv : n_kv_of(w);
+  const int d_model = args.heads * kAttnDh;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensor_map(&tmap_q);
+    prefetch_tensor_map(&tmap_kv);
+    mbar_init(&q_full_bar, 1);
+    for (int s = 0; s < kAttn4Ring; ++s) {
+      mbar_init(&k_full_bar[s], 1);
+      mbar_init(&k_empty_bar[s], 1);
+      mbar_init(&v_full_bar[s], 1);
+      mbar_init(&v_empty_bar[s], 1);
+    }
+    for (int w = 0; w < kAttn4Tiles; ++w) {
+      mbar_init(&s_full_bar[w], 1);
+      mbar_init(&p_full_bar[w], 128);
+      mbar_init(&o_final_bar[w], 1);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, kAttn4TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int active = 0;
+      for (int w = 0; w < kAttn4Tiles; ++w) active += n_kv_of(w) > 0 ? 1 : 0;
+      mbar_arrive_expect_tx(&q_full_bar, static_cast<uint32_t>(active) * kAttnTileBytes);
+      for (int w = 0; w < kAttn4Tiles; ++w) {
+        if (n_kv_of(w) > 0)
+          tma_load_3d(smem_q + w * kAttnTileBytes, &tmap_q, &q_full_bar, head * kAttnDh,
+                      (q_tile0 + w) * kAttnBM, batch);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int slot = j % kAttn4Ring;
+        const uint32_t ph = (j / kAttn4Ring) & 1;
+        if (!mbar_wait(&k_empty_bar[slot], ph ^ 1u, kErrAttnProducerWait, &abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full_bar[slot], kAttn4KvBytes);
+        tma_load_3d(smem_k + slot * kAttn4KvBytes, &tmap_kv, &k_full_bar[slot],
+                    d_model + head * kAttnDh, j * kAttn4BN, batch);
+        if (!mbar_wait(&v_empty_bar[slot], ph ^ 1u, kErrAttnProducerWait, &abort_flag)) {
+          ++issued;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full_bar[slot], kAttn4KvBytes);
+        tma_load_3d(smem_v + slot * kAttn4KvBytes, &tmap_kv, &v_full_bar[slot],
+                    2 * d_model + head * kAttnDh, j * kAttn4BN, batch);
+        ++issued;
+      }
+      volatile int no_abort = 0;
+      mbar_wait(&q_full_bar, 0, kErrAttnProducerWait, &no_abort);
+      const int first = issued > kAttn4Ring ? issued - kAttn4Ring : 0;
+      for (int j = first; j < issued; ++j) {
+        const uint32_t ph = (j / kAttn4Ring) & 1;
+        mbar_wait(&k_full_bar[j % kAttn4Ring], ph, kErrAttnProducerWait, &no_abort);
+        mbar_wait(&v_full_bar[j % kAttn4Ring], ph, kErrAttnProducerWait, &no_abort);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kAttnBM, kAttn4BN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kAttnBM, kAttnDh, false, true);
+      const uint32_t q_addr = smem_u32(smem_q);
+      int nk[kAttn4Tiles];
+#pragma unroll
+      for (int w = 0; w < kAttn4Tiles; ++w) nk[w] = n_kv_of(w);
+      bool issued_any = false;
+      // First / last tile (in issue order) that uses KV tile j.
+      auto first_user = [&](int j) -> int {
+#pragma unroll
+        for (int w = 0; w < kAttn4Tiles; ++w)
+          if (j < nk[w]) return w;
+        return kAttn4Tiles;
+      };
+      auto last_user = [&](int j) -> int {
+        int u = -1;
+#pragma unroll
+        for (int w = 0; w < kAttn4Tiles; ++w)
+          if (j < nk[w]) u = w;
+        return u;
+      };
+      auto issue_qk = [&](int w, int j) -> bool {
+        const int slot = j % kAttn4Ring;
+        if (w == first_user(j)) {
+          if (!mbar_wait(&k_full_bar[slot], (j / kAttn4Ring) & 1, kErrAttnMmaWait, &abort_flag))
+            return false;
+          tc_fence_after();
+        }
+        const uint32_t k_addr = smem_u32(smem_k + slot * kAttn4KvBytes);
+        const uint32_t qa = q_addr + w * kAttnTileBytes;
+        const uint32_t s_tmem = tmem_base + w * kAttn4BN;
+#pragma unroll
+        for (int k = 0; k < kAttnDh / 16; ++k) {
+          umma_bf16_ss(s_tmem, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(k_addr + k * 32, 16, 1024),
+                       idesc_qk, k != 0 ? 1u : 0u);
+        }
+        issued_any = true;
+        umma_commit(&s_full_bar[w]);
+        if (w == last_user(j)) umma_commit(&k_empty_bar[slot]);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full_bar, 0, kErrAttnMmaWait, &abort_flag);
+      if (ok) tc_fence_after();
+      for (int w = 0; ok && w < kAttn4Tiles; ++w)
+        if (nk[w] > 0) ok = issue_qk(w, 0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int slot = j % kAttn4Ring;
+        const int last = last_user(j);
+        bool v_ready = false;
+        for (int w = 0; ok && w < kAttn4Tiles; ++w) {
+          if (!(j < nk[w])) continue;
+          if (!mbar_wait(&p_full_bar[w], j & 1, kErrAttnMmaWait, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!v_ready) {
+            if (!mbar_wait(&v_full_bar[slot], (j / kAttn4Ring) & 1, kErrAttnMmaWait, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            v_ready = true;
+          }
+          const uint32_t v_addr = smem_u32(smem_v + slot * kAttn4KvBytes);
+          const uint32_t p_tmem = tmem_base + w * kAttn4BN;
+          const uint32_t o_tmem = tmem_base + kAttn4Tiles * kAttn4BN + w * kAttnDh;
+#pragma unroll
+          for (int k = 0; k < kAttn4BN / 16; ++k) {
+            umma_bf16_ts(o_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 16 * 128, kAttn4KvBytes, 1024),
+                         idesc_pv, (j | k) != 0 ? 1u : 0u);
+          }
+          if (w == last) umma_commit(&v_empty_bar[slot]);
+          if (j + 1 < nk[w]) {
+            ok = issue_qk(w, j + 1);
+          } else {
+            umma_commit(&o_final_bar[w]);
+          }
+        }
+      }
+      if (issued_any) {
+        umma_commit(&drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait(&drain_bar, 0, kErrAttnMmaWait, &no_abort);
+      }
+    }
+  } else {
+    const int w = (warp - 2) >> 2;
+    const int n_kv_mine = n_kv_of(w);
+    const int q_tile = q_tile0 + w;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q_idx = q_tile * kAttnBM + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem_base + lane_off + w * kAttn4BN;
+    const uint32_t o_tmem = tmem_base + lane_off + kAttn4Tiles * kAttn4BN + w * kAttnDh;
+    const float c = args.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = n_kv_mine > 0;
+    for (int j = 0; ok && j < n_kv_mine; ++j) {
+      ok = mbar_wait(&s_full_bar[w], j & 1, kErrAttnSoftmaxWait, &abort_flag);
+      if (__any_sync(0xffffffffu, !ok)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      uint32_t s[kAttn4BN];
+      tmem_ld_32cols(s_tmem + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_ld_32cols(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_wait_ld();
+      // Columns at or beyond `limit` are masked: above the diagonal, or past
+      // the sequence on a ragged non-causal tile.
+      int limit = kAttn4BN;
+      if (args.causal) {
+        const int lim = q_idx - j * kAttn4BN + 1;
+        limit = lim < kAttn4BN ? lim : kAttn4BN;
+      } else if ((j + 1) * kAttn4BN > args.seq) {
+        limit = args.seq - j * kAttn4BN;
+      }
+      if (limit < kAttn4BN) {
+#pragma unroll
+        for (int i = 0; i < kAttn4BN; ++i)
+          if (i >= limit) s[i] = __float_as_uint(-INFINITY);
+      }
+      float mp[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(s[k]);
+#pragma unroll
+      for (int i = 4; i < kAttn4BN - 8; i += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mp[k] = max3(mp[k], __uint_as_float(s[i + k]), __uint_as_float(s[i + 4 + k]));
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mp[k] = fmaxf(mp[k], __uint_as_float(s[kAttn4BN - 4 + k]));
+      const float mx = fmaxf(max3(mp[0], mp[1], mp[2]), mp[3]);
+      const float mx_scaled = mx * c;
+      // A fully masked row (the upper half of a diagonal block) has mx = -inf:
+      // it keeps its running max and contributes p = 0.
+      const bool need = mx_scaled > m_run + kAttn4MaxSlack;
+      const float m_new = need ? mx_scaled : m_run;
+      const float alpha = need ? fast_exp2(m_run - m_new) : 1.0f;  // 0 on the first tile
+      const uint64_t c2 = f32x2(c, c);
+      const uint64_t neg_m2 = f32x2(-m_new, -m_new);
+      uint64_t acc[2] = {0, 0};
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e = part * 32 + 2 * i;
+          const float2 x = unpack_f32x2(
+              fma_f32x2(f32x2(__uint_as_float(s[e]), __uint_as_float(s[e + 1])), c2, neg_m2));
+          const float p0 = fast_exp2(x.x);
+          const float p1 = fast_exp2(x.y);
+          packed[i] = pack_bf16x2(p0, p1);
+          acc[i & 1] = add_f32x2(acc[i & 1], f32x2(p0, p1));
+        }
+        tmem_st_16cols(s_tmem + part * 16, packed);
+      }
+      // O_w is idle here: the commit behind s_full also covers O_w += P_w(j-1) V.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(o_tmem + cc * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32cols(o_tmem + cc * 32, r);
+        }
+      }
+      const float2 a = unpack_f32x2(add_f32x2(acc[0], acc[1]));
+      tmem_wait_st();
+      l_run = l_run * alpha + (a.x + a.y);
+      m_run = m_new;
+      tc_fence_before();
+      mbar_arrive(&p_full_bar[w]);
+    }
+    if (ok) {
+      ok = mbar_wait(&o_final_bar[w], 0, kErrAttnSoftmaxWait, &abort_flag);
+      const bool all_ok = !__any_sync(0xffffffffu, !ok);
+      __syncwarp();
+      if (all_ok) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+        __nv_bfloat16* out_row =
+            args.out + (static_cast<int64_t>(batch) * args.seq + q_idx) * d_model + head * kAttnDh;
+#pragma unroll 1
+        for (int cc = 0; cc < kAttnDh / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32cols(o_tmem + cc * 32, r);
+          tmem_wait_ld();
+          if (q_idx < args.seq) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              st_global_v4(out_row + cc * 32 + i,
+                           pack_bf16x2(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l),
+                           pack_bf16x2(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l));
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAttn4TmemCols);
+  }
+}
+
 }  // namespace b200tx

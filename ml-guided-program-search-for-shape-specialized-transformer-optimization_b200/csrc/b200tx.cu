@@ -47,7 +47,7 @@ struct DeviceState {
   int cc_major = 0;
   int cc_minor = 0;
   bool gemm_attr[4] = {false, false, false, false};
-  bool attn_attr[2] = {false, false};
+  bool attn_attr[3] = {false, false, false};
 };
 
 std::mutex g_mutex;
@@ -336,13 +336,15 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
   if (head_dim != b200tx::kAttnDh)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: head_dim %lld (only 64 is built)",
                 (long long)head_dim);
-  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE)
+  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE && variant != B200TX_ATTN_QUAD)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: variant %d", variant);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
   const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
-  const int64_t units = variant == B200TX_ATTN_PAIRED ? (q_tiles + 1) / 2 : q_tiles;
+  const int64_t units = variant == B200TX_ATTN_PAIRED ? (q_tiles + 1) / 2
+                        : variant == B200TX_ATTN_QUAD ? (q_tiles + 3) / 4
+                                                      : q_tiles;
   const int64_t blocks = units * heads * batch;
   if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: problem too large for one launch");
@@ -369,6 +371,31 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
   args.num_q_tiles = static_cast<int>(q_tiles);
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
+  if (variant == B200TX_ATTN_QUAD) {
+    CUtensorMap map_kv;
+    const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(3 * d_model) * 2,
+                                 static_cast<uint64_t>(3 * d_model) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t box[3] = {b200tx::kAttnDh, b200tx::kAttn4BN, 1};
+    rc = encode_bf16_map(&map_kv, qkv, 3, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (!dev->attn_attr[variant]) {
+        cudaError_t err = cudaFuncSetAttribute(b200tx::attention_fwd_dh64_quad_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(b200tx::kAttn4SmemBytes));
+        if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
+        dev->attn_attr[variant] = true;
+      }
+    }
+    b200tx::attention_fwd_dh64_quad_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttn4Threads,
+                                             b200tx::kAttn4SmemBytes, stream>>>(map_qkv, map_kv, args);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+    return B200TX_OK;
+  }
   using KernelFn = void (*)(CUtensorMap, b200tx::AttnArgs);
   const KernelFn kernel = variant == B200TX_ATTN_PAIRED ? b200tx::attention_fwd_dh64_pair_kernel
                                                         : b200tx::attention_fwd_dh64_kernel;
@@ -392,7 +419,7 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
 int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
                      int64_t head_dim, float scale, int causal, cudaStream_t stream) {
   return b200tx_attention_ex(qkv, out, batch, seq, heads, head_dim, scale, causal,
-                             B200TX_ATTN_PAIRED, stream);
+                             B200TX_ATTN_QUAD, stream);
 }
 
 }  // extern "C"

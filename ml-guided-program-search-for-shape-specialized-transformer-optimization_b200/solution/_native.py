@@ -23,6 +23,7 @@ EPI_BIAS = 0
 EPI_BIAS_GELU = 1
 ATTN_PAIRED = 0
 ATTN_SINGLE = 1
+ATTN_QUAD = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -258,7 +259,7 @@ def attention(
     head_dim: int,
     scale: float,
     causal: bool,
-    variant: int = ATTN_PAIRED,
+    variant: int = ATTN_QUAD,
 ) -> None:
     """Launch b200tx_attention_ex over a packed [B, S, 3D] projection."""
 
@@ -283,6 +284,7 @@ def attention(
 __all__ = [
     "ABI_VERSION",
     "ATTN_PAIRED",
+    "ATTN_QUAD",
     "ATTN_SINGLE",
     "BF16",
     "EPI_BIAS",

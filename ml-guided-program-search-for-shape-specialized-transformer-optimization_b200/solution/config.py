@@ -149,10 +149,11 @@ def _exact_fields(value: dict[str, Any], expected: frozenset[str], *, field: str
 # sets are rejected by the dataclasses, so a search never proposes a variant
 # that does not exist.
 SM100_GEMM_VARIANTS = frozenset({(128, 256, 64, 4)})
-# (block_m, block_n, kv_stages): block_m 256 = two 128-row query tiles per CTA
-# with P kept in TMEM (B200TX_ATTN_PAIRED); block_m 128 = one query tile per
-# CTA with P staged through shared memory (B200TX_ATTN_SINGLE).
-SM100_ATTENTION_VARIANTS = frozenset({(256, 128, 3), (128, 128, 3)})
+# (block_m, block_n, kv_stages) -> libb200tx attention variant:
+#   (256, 128, 3): two 128-row query tiles per CTA, P kept in TMEM (B200TX_ATTN_PAIRED)
+#   (128, 128, 3): one query tile per CTA, P staged through shared memory (B200TX_ATTN_SINGLE)
+#   (512, 64, 6):  four query tiles per CTA, 64-row KV tiles, P in TMEM (B200TX_ATTN_QUAD)
+SM100_ATTENTION_VARIANTS = {(256, 128, 3): 0, (128, 128, 3): 1, (512, 64, 6): 2}
 SM100_NORM_ROWS_PER_CTA = frozenset({8})
 
 
@@ -193,9 +194,9 @@ class Sm100GemmParams:
 class Sm100AttentionParams:
     """Tile shape of the tcgen05 flash attention (csrc/attention_kernels.cuh)."""
 
-    block_m: int = 256
-    block_n: int = 128
-    kv_stages: int = 3
+    block_m: int = 512
+    block_n: int = 64
+    kv_stages: int = 6
 
     _FIELDS: ClassVar[frozenset[str]] = frozenset({"block_m", "block_n", "kv_stages"})
 
@@ -213,7 +214,7 @@ class Sm100AttentionParams:
     def kernel_variant(self) -> int:
         """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE)."""
 
-        return 0 if self.block_m == 256 else 1
+        return SM100_ATTENTION_VARIANTS[(self.block_m, self.block_n, self.kv_stages)]
 
     @classmethod
     def from_dict(cls, payload: object) -> Sm100AttentionParams:

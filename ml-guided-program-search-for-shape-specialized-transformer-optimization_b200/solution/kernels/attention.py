@@ -45,7 +45,7 @@ def sm100_flash_attention(
     *,
     causal: bool = True,
     out: torch.Tensor | None = None,
-    variant: int = _native.ATTN_PAIRED,
+    variant: int = _native.ATTN_QUAD,
 ) -> tuple[torch.Tensor, str]:
     """``softmax(q k^T / 8 [+ causal]) v`` per head; returns the ``[B, S, D]`` context."""
 

@@ -100,8 +100,12 @@ def test_launch_params_must_name_a_built_variant() -> None:
         Sm100GemmParams(tile_m=128, tile_n=128, tile_k=64, stages=4)
     with pytest.raises(ValueError):
         Sm100AttentionParams(block_m=64)
-    assert Sm100AttentionParams().kernel_variant == 0
-    assert Sm100AttentionParams(block_m=128).kernel_variant == 1
+    with pytest.raises(ValueError):
+        Sm100AttentionParams(block_m=512, block_n=128, kv_stages=6)
+    assert Sm100AttentionParams().kernel_variant == 2
+    assert Sm100AttentionParams(block_m=256, block_n=128, kv_stages=3).kernel_variant == 0
+    assert Sm100AttentionParams(block_m=128, block_n=128, kv_stages=3).kernel_variant == 1
+    assert Sm100AttentionParams(block_m=512, block_n=64, kv_stages=6).kernel_variant == 2
     with pytest.raises(ValueError):
         Sm100NormParams(rows_per_cta=4)
     with pytest.raises(ValueError):

@@ -148,7 +148,7 @@ def test_linear_three_dimensional_input() -> None:
     assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
 
 
-VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE]
+VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD]
 
 
 def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, variant: int) -> None:
@@ -179,6 +179,8 @@ def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, v
         (1, 385, 1, False),
         (2, 256, 3, True),  # even number of query tiles
         (1, 384, 2, True),  # odd: the last pair has one tile
+        (1, 640, 2, True),  # five query tiles: the last quad has one
+        (2, 1500, 1, False),
     ],
 )
 @pytest.mark.parametrize("variant", VARIANTS)
@@ -203,15 +205,17 @@ def test_attention_is_deterministic(variant: int) -> None:
     assert torch.equal(a, b)
 
 
-def test_attention_variants_agree() -> None:
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_variants_agree(causal: bool) -> None:
     g = torch.Generator().manual_seed(13)
     qkv = torch.randn(3, 1000, 3 * 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
     with torch.inference_mode():
-        a, _ = sm100_flash_attention(qkv, 2, variant=_native.ATTN_PAIRED)
-        b, _ = sm100_flash_attention(qkv, 2, variant=_native.ATTN_SINGLE)
-    max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
-    # Two bf16 results of different summation orders: a few bf16 ulps apart.
-    assert rel < 5e-3 and max_abs < 4e-2
+        a, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=_native.ATTN_PAIRED)
+        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD):
+            b, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=other)
+            max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
+            # Two bf16 results of different summation orders: a few bf16 ulps apart.
+            assert rel < 5e-3 and max_abs < 4e-2, (other, max_abs, rel)
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
