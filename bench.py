@@ -48,6 +48,16 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 WORKLOAD = dict(batch_size=8, seq_len=2048, d_model=1024, num_heads=16, ffn_dim=4096, num_layers=2, causal=True)
+# BASELINE.json configs run by --workload (c2 is the default bench line).
+WORKLOADS = {
+    "c2": (WORKLOAD, 1, "C2 resident mid shape: B8 S2048 D1024 H16(Dh64) F4096 L2 causal"),
+    "c3": (dict(batch_size=64, seq_len=256, d_model=768, num_heads=12, ffn_dim=3072, num_layers=4, causal=True), 2,
+           "C3 short-sequence large-batch: B64 S256 D768 H12(Dh64) F3072 L4 causal"),
+    "c4": (dict(batch_size=4, seq_len=16384, d_model=2048, num_heads=32, ffn_dim=8192, num_layers=2, causal=True), 3,
+           "C4 long-context: B4 S16384 D2048 H32(Dh64) F8192 L2 causal"),
+    "c5": (dict(batch_size=32, seq_len=100000, d_model=1024, num_heads=16, ffn_dim=4096, num_layers=2, causal=True), 4,
+           "C5 streamed capacity: B32 S100000 D1024 H16(Dh64) F4096 L2 causal"),
+}
 INPUT_SEED = 1
 WEIGHT_SEED = 0
 METRIC = "fwd tokens/s"
@@ -99,7 +109,7 @@ class ClockSampler:
         0x80: "hw_power_brake_slowdown",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.1) -> None:
+    def __init__(self, device_index: int, period_s: float = 0.005) -> None:
         self.device_index = device_index
         self.period_s = period_s
         self.samples: list[int] = []
@@ -227,14 +237,35 @@ def run_reference(args: argparse.Namespace) -> None:
 
 
 # ---------------------------------------------------------------- GPU arm
-def build_model(device: torch.device):
+def build_model(device: torch.device, spec: dict | None = None):
     from oracle import OfficialConfig, official_state_dict
     from solution.transformer import UserOptimizedTransformer, copy_model_weights
 
-    cfg = SimpleNamespace(**WORKLOAD)
-    model = UserOptimizedTransformer(cfg)
-    copy_model_weights(official_state_dict(OfficialConfig(**WORKLOAD), seed=WEIGHT_SEED), model)
+    spec = spec or WORKLOAD
+    model = UserOptimizedTransformer(SimpleNamespace(**spec))
+    copy_model_weights(official_state_dict(OfficialConfig(**spec), seed=WEIGHT_SEED), model)
     return model.to(device).eval()
+
+
+def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, world: int):
+    """This rank's input rows and the parallel mode of the workload."""
+
+    from oracle import OfficialConfig, official_input
+    from oracle.weights import per_row_input
+    from solution.runtimes.sharded import batch_shard_bounds
+
+    cfg = OfficialConfig(**spec)
+    if args.workload == "c4" and world > 1:
+        # Head-sharded tensor parallel: every rank holds the whole batch.
+        return official_input(cfg, seed), "heads", "strong", cfg.batch_size * cfg.seq_len
+    if args.workload == "c5":
+        # Batch-sharded capacity run: the 32 rows (seed 4 + row) split over ranks.
+        start, stop = batch_shard_bounds(cfg.batch_size, rank, world)
+        rows = [per_row_input(cfg, seed, r) for r in range(start, stop)]
+        x = torch.cat(rows, dim=0)
+        return x, "batch", "strong", cfg.batch_size * cfg.seq_len
+    # c2 / c3: every rank runs its own full batch (rank r: seed + r).
+    return official_input(cfg, seed + rank), "batch", "weak", world * cfg.batch_size * cfg.seq_len
 
 
 def run_gpu(args: argparse.Namespace) -> None:
@@ -254,18 +285,23 @@ def run_gpu(args: argparse.Namespace) -> None:
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         dist = dist_mod
 
-    from oracle import OfficialConfig, official_input
+    from oracle import OfficialConfig
     from solution import _native
+    from solution.runtimes.sharded import TensorParallelTransformer
     from solution.transformer import KernelEventRecorder
 
     _native.device_check()
-    cfg = OfficialConfig(**WORKLOAD)
-    model = build_model(device)
-    # Each rank owns its own C2 batch; rank r uses seed 1 + r (rank 0 = the BASELINE input).
-    x_host = official_input(cfg, INPUT_SEED + rank).pin_memory()
+    spec, seed, workload_name = WORKLOADS[args.workload]
+    cfg = OfficialConfig(**spec)
+    model = build_model(device, spec)
+    x_cpu, parallel, scaling, total_tokens = _workload_input(args, spec, seed, rank, world)
+    runner = TensorParallelTransformer(model) if parallel == "heads" else model
+    x_host = x_cpu.pin_memory()
+    del x_cpu
     x_dev = x_host.to(device)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-    tokens_per_rank = cfg.batch_size * cfg.seq_len
+    big_input = x_dev.numel() * x_dev.element_size() > 2 * L2_FLUSH_BYTES
+    flush = None if big_input else torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    torch.cuda.reset_peak_memory_stats(device)
 
     def barrier() -> None:
         if dist is not None:
@@ -274,90 +310,97 @@ def run_gpu(args: argparse.Namespace) -> None:
 
     with torch.inference_mode():
         for _ in range(max(3, args.warmup)):
-            model(x_dev)
+            runner(x_dev)
         torch.cuda.synchronize()
 
         recorder = KernelEventRecorder()
-        model.kernel_events = recorder
+        if runner is model:
+            model.kernel_events = recorder
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
         with ClockSampler(local_rank) as clocks:
             for i in range(args.steps):
-                flush.zero_()
+                if flush is not None:
+                    flush.zero_()
                 starts[i].record()
-                model(x_dev)
+                runner(x_dev)
                 ends[i].record()
             barrier()
         model.kernel_events = None
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         kernel_ms = recorder.durations_ms()
 
-        # End to end through the public API from pinned host memory.
+        # End to end through the public call from pinned host memory: H2D of
+        # the input and D2H of the whole output inside every step.
         out_host = torch.empty(x_host.shape, dtype=torch.float32).pin_memory()
         for _ in range(2):
-            out_host.copy_(model(x_host.to(device, non_blocking=True)), non_blocking=True)
+            out_host.copy_(runner(x_host.to(device, non_blocking=True)), non_blocking=True)
         torch.cuda.synchronize()
         barrier()
         e2e_start = torch.cuda.Event(enable_timing=True)
         e2e_end = torch.cuda.Event(enable_timing=True)
         e2e_start.record()
         for _ in range(args.steps):
-            y = model(x_host.to(device, non_blocking=True))
+            y = runner(x_host.to(device, non_blocking=True))
             out_host.copy_(y, non_blocking=True)
         e2e_end.record()
         barrier()
         e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
+    peak_gb = torch.cuda.max_memory_allocated(device) / 2**30
 
     total_ms = sum(step_ms)
-    stats = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    stats = torch.tensor([total_ms, e2e_ms, peak_gb], dtype=torch.float64, device=device)
     if dist is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    total_ms_max, e2e_ms_max = stats.tolist()
+    total_ms_max, e2e_ms_max, peak_gb_max = stats.tolist()
     ms_per_step = total_ms_max / args.steps
-    value = world * tokens_per_rank * args.steps / (total_ms_max / 1000.0)
-    e2e_value = world * tokens_per_rank / (e2e_ms_max / 1000.0)
+    value = total_tokens * args.steps / (total_ms_max / 1000.0)
+    e2e_value = total_tokens / (e2e_ms_max / 1000.0)
 
-    # Dominant kernel of the step and its roofline.
-    per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
-    launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
-    dominant = max(per_role, key=per_role.get)
-    peaks, peak_source = _peaks()
-    b, s, d, f, layers = cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
-    m = b * s
+    b_loc = x_dev.shape[0]
+    s, d, f, layers = cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
+    m = b_loc * s
+    heads_frac = 1.0 / world if parallel == "heads" else 1.0
     flops_per_launch = {
-        "attention": 2.0 * b * s * s * d,  # causal, counted as 2BS^2D like the reference
-        "qkv_projection": 2.0 * m * 3 * d * d,
-        "attention_output_projection": 2.0 * m * d * d,
-        "ffn_input_projection": 2.0 * m * f * d,
-        "ffn_output_projection": 2.0 * m * d * f,
+        "attention": 2.0 * b_loc * s * s * d * heads_frac,  # causal, counted as 2BS^2D like the reference
+        "qkv_projection": 2.0 * m * 3 * d * d * heads_frac,
+        "attention_output_projection": 2.0 * m * d * d * heads_frac,
+        "ffn_input_projection": 2.0 * m * f * d * heads_frac,
+        "ffn_output_projection": 2.0 * m * d * f * heads_frac,
     }
     bytes_per_launch = {"residual_norm": 12.0 * m * d, "initial_norm": 6.0 * m * d}
-    avg_launch_ms = per_role[dominant] / max(1, launches[dominant])
-    if dominant in flops_per_launch:
-        achieved = flops_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e12
-        peak = float(peaks["bf16_tflops_sustained"])
-        roofline = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dominant,
-                    "algorithmic_per_launch": flops_per_launch[dominant]}
-    else:
-        achieved = bytes_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e9
-        peak = float(peaks["hbm_gbs"])
-        roofline = {"bound": "hbm", "unit": "GB/s", "kernel": dominant,
-                    "algorithmic_per_launch": bytes_per_launch[dominant]}
-    roofline.update(
-        achieved=achieved,
-        peak=peak,
-        peak_source=f"{peak_source} ({'bf16_tflops_sustained' if roofline['bound'] == 'tensor' else 'hbm_gbs'})",
-        frac=achieved / peak,
-        traffic=_profile_traffic(dominant),
-        avg_launch_ms=avg_launch_ms,
-    )
+    per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
+    launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
+    roofline = None
+    if per_role:
+        dominant = max(per_role, key=per_role.get)
+        peaks, peak_source = _peaks()
+        avg_launch_ms = per_role[dominant] / max(1, launches[dominant])
+        if dominant in flops_per_launch:
+            achieved = flops_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e12
+            peak = float(peaks["bf16_tflops_sustained"])
+            roofline = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dominant,
+                        "algorithmic_per_launch": flops_per_launch[dominant]}
+        else:
+            achieved = bytes_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e9
+            peak = float(peaks["hbm_gbs"])
+            roofline = {"bound": "hbm", "unit": "GB/s", "kernel": dominant,
+                        "algorithmic_per_launch": bytes_per_launch[dominant]}
+        roofline.update(
+            achieved=achieved,
+            peak=peak,
+            peak_source=f"{peak_source} ({'bf16_tflops_sustained' if roofline['bound'] == 'tensor' else 'hbm_gbs'})",
+            frac=achieved / peak,
+            traffic=_profile_traffic(dominant) if args.workload == "c2" else None,
+            avg_launch_ms=avg_launch_ms,
+        )
     attention_ms = per_role.get("attention", 0.0) / max(1, launches.get("attention", 1))
     kernel_table = {
         role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]} for role in sorted(per_role)
     }
-    model_flops = layers * (2.0 * b * s * s * d + 8.0 * b * s * d * d + 4.0 * b * s * d * f)
-
+    model_flops = (total_tokens / cfg.seq_len) * layers * (2.0 * s * s * d + 8.0 * s * d * d + 4.0 * s * d * f)
+    launches_per_step = 1 + 7 * layers
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -369,21 +412,26 @@ def run_gpu(args: argparse.Namespace) -> None:
             "ms_per_step": ms_per_step,
             "p50_latency_ms": statistics.median(step_ms),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic: x ~ N(0,1) seed 1+rank (CPU generator), reference default-init weights seed 0",
+            "data": "synthetic: x ~ N(0,1) from the BASELINE seeds (CPU generator), reference default-init weights seed 0",
             "config": {
-                "workload": WORKLOAD_NAME,
-                "global_batch": cfg.batch_size * world,
+                "workload": workload_name,
+                "global_batch": cfg.batch_size * (world if scaling == "weak" else 1),
                 "seq_len": cfg.seq_len,
-                "parallelism": f"dp{world} (batch-sharded, no collective)",
+                "parallelism": (
+                    f"tp{world} (head-sharded, NCCL all-reduce after out-proj and FFN-down)"
+                    if parallel == "heads"
+                    else f"dp{world} (batch-sharded, no collective)"
+                ),
                 "io_dtype": "float32 in/out, bf16 GEMM/attention operands, fp32 accumulation and residual",
-                "l2": "flushed (256 MB write) before every timed step",
+                "l2": "inputs larger than L2" if big_input else "flushed (256 MB write) before every timed step",
                 "runtime": model.active_config.schedule.runtime.value,
             },
             "attention_tflops": flops_per_launch["attention"] / (attention_ms / 1000.0) / 1e12 if attention_ms else None,
             "model_tflops": model_flops / (ms_per_step / 1000.0) / 1e12,
+            "peak_memory_gb_per_gpu": peak_gb_max,
             "kernels": kernel_table,
             "roofline": roofline,
             "e2e": {
@@ -393,14 +441,15 @@ def run_gpu(args: argparse.Namespace) -> None:
                 "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
                 "ms_per_step": e2e_ms_max,
             },
-            "gpu_launches": int(sum(len(v) for v in kernel_ms.values())),
+            "gpu_launches": int(sum(len(v) for v in kernel_ms.values())) or launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
-        if world == 1 and not args.skip_cpu_baseline:
+        if world == 1 and args.workload == "c2" and not args.skip_cpu_baseline:
             line["cpu_baseline"] = {
                 k: v for k, v in cpu_baseline(steps=1).items() if k in ("value", "unit", "cores", "kind", "sample")
             }
         print(json.dumps(line), flush=True)
+    del runner
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -498,6 +547,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="c2",
+                        help="BASELINE config to run (c2 is the bench line the driver records)")
     parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")
     parser.add_argument(
         "--kernel",

@@ -1,0 +1,187 @@
+"""Multi-process sharding: batch partition, head-sharded tensor-parallel math
+and its collective plumbing.
+
+CPU tests run the tensor-parallel composition with gloo ranks (world size 2)
+and numpy/torch CPU arithmetic on the very shards ``shard_layer`` produces,
+against the single-process oracle.  The GPU test (two or more GPUs) runs
+``TensorParallelTransformer`` over NCCL against the single-GPU model.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import OfficialConfig, official_input, official_state_dict, transformer_forward
+from oracle.reference_forward import gelu_erf, layer_norm
+from oracle.weights import state_to_numpy
+from solution.runtimes.sharded import batch_shard_bounds, shard_layer
+
+CFG = OfficialConfig(2, 24, 256, 4, 512, 2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_batch_shard_bounds_partition() -> None:
+    for batch in (1, 4, 7, 8, 32):
+        for world in (1, 2, 3, 8):
+            spans = [batch_shard_bounds(batch, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == batch
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        batch_shard_bounds(4, 2, 2)
+
+
+def _packed_layer(state: dict[str, torch.Tensor], i: int) -> tuple[torch.Tensor, ...]:
+    p = f"layers.{i}"
+    w_qkv = torch.cat([state[f"{p}.attention.{n}_proj.weight"] for n in "qkv"], dim=0)
+    b_qkv = torch.cat([state[f"{p}.attention.{n}_proj.bias"] for n in "qkv"], dim=0)
+    return (
+        w_qkv,
+        b_qkv,
+        state[f"{p}.attention.out_proj.weight"],
+        state[f"{p}.attention.out_proj.bias"],
+        state[f"{p}.ffn_in.weight"],
+        state[f"{p}.ffn_in.bias"],
+        state[f"{p}.ffn_out.weight"],
+        state[f"{p}.ffn_out.bias"],
+    )
+
+
+def test_shards_reassemble_the_full_projections() -> None:
+    state = official_state_dict(CFG, seed=0)
+    full = _packed_layer(state, 0)
+    world = 4
+    shards = [shard_layer(*full, num_heads=CFG.num_heads, rank=r, world=world) for r in range(world)]
+    x = torch.randn(5, CFG.d_model, dtype=torch.float64)
+    ctx = torch.randn(5, CFG.d_model, dtype=torch.float64)
+    h = torch.randn(5, CFG.ffn_dim, dtype=torch.float64)
+    d_local = CFG.d_model // world
+    f_local = CFG.ffn_dim // world
+    # Column-parallel QKV: each rank's outputs are its heads' q, k, v columns.
+    qkv_full = x @ full[0].double().T + full[1].double()
+    for r, sh in enumerate(shards):
+        local = x @ sh.w_qkv.double().T + sh.b_qkv.double()
+        for which in range(3):
+            cols = slice(which * CFG.d_model + r * d_local, which * CFG.d_model + (r + 1) * d_local)
+            np.testing.assert_allclose(local[:, which * d_local : (which + 1) * d_local], qkv_full[:, cols])
+    # Row-parallel out-proj and FFN-down: partial sums add up to the full map.
+    o_sum = sum(ctx[:, r * d_local : (r + 1) * d_local] @ sh.w_o.double().T + sh.b_o.double() for r, sh in enumerate(shards))
+    np.testing.assert_allclose(o_sum, ctx @ full[2].double().T + full[3].double(), atol=1e-10)
+    f_sum = sum(h[:, r * f_local : (r + 1) * f_local] @ sh.w_2.double().T + sh.b_2.double() for r, sh in enumerate(shards))
+    np.testing.assert_allclose(f_sum, h @ full[6].double().T + full[7].double(), atol=1e-10)
+    with pytest.raises(ValueError):
+        shard_layer(*full, num_heads=CFG.num_heads, rank=0, world=3)
+
+
+def _tp_forward_cpu(x: np.ndarray, state: dict[str, torch.Tensor], rank: int, world: int) -> np.ndarray:
+    """The tensor-parallel composition on CPU: local shards + gloo all-reduce."""
+
+    ns = state_to_numpy(state)
+    batch, seq, d = x.shape
+    heads_local = CFG.num_heads // world
+    d_local = d // world
+    out = x.astype(np.float32).copy()
+    for i in range(CFG.num_layers):
+        sh = shard_layer(*_packed_layer(state, i), num_heads=CFG.num_heads, rank=rank, world=world)
+        p = f"layers.{i}"
+        n = layer_norm(out, ns[f"{p}.norm1.weight"], ns[f"{p}.norm1.bias"])
+        qkv = n @ sh.w_qkv.numpy().T + sh.b_qkv.numpy()
+        q, k, v = (qkv[..., j * d_local : (j + 1) * d_local].reshape(batch, seq, heads_local, 64).transpose(0, 2, 1, 3) for j in range(3))
+        scores = q @ k.transpose(0, 1, 3, 2) / 8.0
+        scores = np.where(np.triu(np.ones((seq, seq), bool), 1)[None, None], -np.inf, scores)
+        probs = np.exp(scores - scores.max(-1, keepdims=True))
+        probs /= probs.sum(-1, keepdims=True)
+        ctx = (probs @ v).transpose(0, 2, 1, 3).reshape(batch, seq, d_local)
+        partial = torch.from_numpy((ctx @ sh.w_o.numpy().T + sh.b_o.numpy()).astype(np.float32))
+        dist.all_reduce(partial)
+        out = out + partial.numpy()
+        n = layer_norm(out, ns[f"{p}.norm2.weight"], ns[f"{p}.norm2.bias"])
+        h = gelu_erf(n @ sh.w_1.numpy().T + sh.b_1.numpy())
+        partial = torch.from_numpy((h @ sh.w_2.numpy().T + sh.b_2.numpy()).astype(np.float32))
+        dist.all_reduce(partial)
+        out = out + partial.numpy()
+    return layer_norm(out, ns["final_norm.weight"], ns["final_norm.bias"])
+
+
+def _gloo_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        state = official_state_dict(CFG, seed=0)
+        x = official_input(CFG, 3).numpy()
+        y = _tp_forward_cpu(x, state, rank, world)
+        np.save(os.path.join(result_dir, f"rank{rank}.npy"), y)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_composition_over_gloo() -> None:
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_gloo_worker, args=(world, _free_port(), tmp), nprocs=world, start_method="spawn")
+        outs = [np.load(os.path.join(tmp, f"rank{r}.npy")) for r in range(world)]
+    state = state_to_numpy(official_state_dict(CFG, seed=0))
+    ref = transformer_forward(official_input(CFG, 3).numpy(), state, num_heads=CFG.num_heads, num_layers=CFG.num_layers)
+    for y in outs:
+        np.testing.assert_allclose(y, ref, rtol=1e-4, atol=1e-4)
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    import datetime
+
+    from solution.runtimes.sharded import TensorParallelTransformer
+    from solution.transformer import UserOptimizedTransformer, copy_model_weights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        cfg = OfficialConfig(2, 640, 512, 8, 1024, 2)
+        model = UserOptimizedTransformer(SimpleNamespace(**cfg.__dict__))
+        copy_model_weights(official_state_dict(cfg, seed=0), model)
+        model = model.to(f"cuda:{rank}").eval()
+        tp = TensorParallelTransformer(model)
+        x = official_input(cfg, 5).to(f"cuda:{rank}")
+        y_tp = tp(x)
+        with torch.inference_mode():
+            y_single = model(x)
+        torch.cuda.synchronize()
+        np.save(os.path.join(result_dir, f"tp{rank}.npy"), y_tp.cpu().numpy())
+        np.save(os.path.join(result_dir, f"single{rank}.npy"), y_single.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_tensor_parallel_matches_single_gpu() -> None:
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_nccl_worker, args=(world, _free_port(), tmp), nprocs=world, start_method="spawn")
+        tp = [np.load(os.path.join(tmp, f"tp{r}.npy")) for r in range(world)]
+        single = np.load(os.path.join(tmp, "single0.npy"))
+    np.testing.assert_array_equal(tp[0], tp[1])
+    diff = tp[0].astype(np.float64) - single
+    assert np.abs(diff).max() < 2e-2
+    assert np.linalg.norm(diff) / np.linalg.norm(single) < 5e-3
