@@ -331,6 +331,48 @@ __device__ __forceinline__ float2 unpack_f32x2(uint64_t v) {
   return r;
 }
 
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair of fp32 values on the FMA pipe instead of MUFU, so that the
+// softmax can split its exponentials between the two pipes.
+// Method: Cody-Waite style range reduction x = n + f with n = round(x) and
+// f in [-1/2, 1/2], then 2^f from a degree-3 polynomial and 2^n by adding n
+// to the exponent field.  n is found with the round-to-nearest "magic number"
+// addition: 1.5 * 2^23 + x holds round(x) in its low mantissa bits, so
+// (bits << 23) is n << 23 modulo 2^32.  The polynomial
+//     p(f) = 1 + f (c1 + f (c2 + f c3))
+// is a relative-error minimax fit of 2^f on [-1/2, 1/2] with p(0) = 1 exactly
+// (coefficients fitted for this library; max relative error 1.0e-4, well
+// under the bf16 rounding of P).  Inputs are clamped to [-127, inf): at -127
+// the result is exactly +0 (p(0) = 1 and n = -127 cancel the exponent bias),
+// so masked (-inf) scores give p = 0 as with ex2; above -127 every result is
+// a non-negative finite float.  Callers keep x <= 8 (the softmax slack).
+__device__ __forceinline__ void exp2_poly_f32x2(uint64_t x2, float& r0, float& r1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC1 = 0.6932829022407532f;
+  constexpr float kC2 = 0.24221037328243256f;
+  constexpr float kC3 = 0.05500858277082443f;
+  const float2 xv = unpack_f32x2(x2);
+  const uint64_t x = f32x2(fmaxf(xv.x, -127.0f), fmaxf(xv.y, -127.0f));
+  const uint64_t t = add_f32x2(x, f32x2(kMagic, kMagic));
+  const uint64_t n = sub_f32x2(t, f32x2(kMagic, kMagic));
+  const uint64_t f = sub_f32x2(x, n);
+  uint64_t p = fma_f32x2(f32x2(kC3, kC3), f, f32x2(kC2, kC2));
+  p = fma_f32x2(p, f, f32x2(kC1, kC1));
+  p = fma_f32x2(p, f, f32x2(1.0f, 1.0f));
+  const float2 tv = unpack_f32x2(t);
+  const float2 pv = unpack_f32x2(p);
+  uint32_t b0, b1;
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(b0) : "r"(__float_as_uint(tv.x)), "r"(__float_as_uint(pv.x)));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(b1) : "r"(__float_as_uint(tv.y)), "r"(__float_as_uint(pv.y)));
+  r0 = __uint_as_float(b0);
+  r1 = __uint_as_float(b1);
+}
+
 // exp2 of two fp32 values, rounded to bf16 on the way in and computed by one
 // MUFU operation for the pair; returns the packed bf16x2 (lo in bits 0..15).
 __device__ __forceinline__ uint32_t exp2_bf16x2(uint64_t x) {
