@@ -340,7 +340,7 @@ def run_gpu(args: argparse.Namespace) -> None:
         # to after the last copy-out.
         from solution.runtimes.host_pipeline import HostPipeline
 
-        pipe = HostPipeline(runner, device, depth=2)
+        pipe = HostPipeline(runner, device, depth=3)
         outs_host = [torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory() for _ in range(2)]
         for i in range(3):
             pipe.submit(x_host, outs_host[i % 2])
