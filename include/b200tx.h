@@ -87,6 +87,26 @@ int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void
                                int out_dtype, const float* gamma, const float* beta,
                                int64_t rows, int64_t cols, float eps, cudaStream_t stream);
 
+/* mask_mode bits of b200tx_residual_layer_norm_masked, applied to rows whose
+ * row_valid flag is 0 (the reference's masked_fill of padding tokens,
+ * official/torch_transformer_benchmark.py:119-121, 143-144, 170-171). */
+#define B200TX_MASK_DROP_UPDATE 1   /* r = residual_in: the update is ignored */
+#define B200TX_MASK_ZERO_RESIDUAL 2 /* r = 0 (residual_out, and the LN input) */
+#define B200TX_MASK_ZERO_NORMED 4   /* normed = 0 */
+
+/*
+ * b200tx_residual_layer_norm with a padding mask: row_valid [rows] uint8
+ * (0 = padding token, non-null); mask_mode is a combination of B200TX_MASK_*
+ * bits.  Replaces the masked LayerNorm path of the reference
+ * (solution/kernels/norm/triton_masked.py:47-118) and the masked_fill calls
+ * of official/torch_transformer_benchmark.py:119-121, 143-144, 170-171.
+ */
+int b200tx_residual_layer_norm_masked(const void* residual_in, int in_dtype, const void* update,
+                                      int update_dtype, float* residual_out, void* normed,
+                                      int out_dtype, const float* gamma, const float* beta,
+                                      const uint8_t* row_valid, int mask_mode, int64_t rows,
+                                      int64_t cols, float eps, cudaStream_t stream);
+
 /*
  * out[M, N] = epilogue(a[M, K] . w[N, K]^T + bias[N]) on the tcgen05 tensor
  * cores, bf16 inputs, fp32 accumulation, output F32 or BF16.
@@ -130,6 +150,17 @@ int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int
 int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
                         int64_t head_dim, float scale, int causal, int variant,
                         cudaStream_t stream);
+
+/*
+ * b200tx_attention_ex with a key padding mask: key_valid [batch, seq] uint8
+ * (non-null), 0 = padding key, whose scores are -inf for every query (the
+ * reference's invalid_keys masked_fill, official/torch_transformer_benchmark.py:
+ * 105-108).  A query that sees no valid key gets a zero context row.  Built
+ * into B200TX_ATTN_QUAD only; other variants return B200TX_ERR_UNSUPPORTED.
+ */
+int b200tx_attention_masked(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                            int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                            int variant, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

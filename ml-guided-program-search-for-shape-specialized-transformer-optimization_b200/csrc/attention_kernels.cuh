@@ -45,6 +45,9 @@ constexpr size_t kAttnSmemBytes =
 
 struct AttnArgs {
   __nv_bfloat16* out;  // [B, S, H*64]
+  // [B, S] 0/1 padding mask of the keys (official/torch_transformer_benchmark.py:
+  // 105-108), or null when every key is valid.  Read by the masked quad build.
+  const uint8_t* key_valid;
   int batch;
   int seq;
   int heads;
@@ -694,6 +697,9 @@ constexpr size_t kAttn4SmemBytes =
     1024 + kAttn4Tiles * kAttnTileBytes + 2 * kAttn4Ring * kAttn4KvBytes;  // 161 KB
 constexpr float kAttn4MaxSlack = 8.0f;
 
+// kMasked: the build that reads args.key_valid (padding masks); the unmasked
+// build carries none of that code.
+template <bool kMasked>
 __global__ void __launch_bounds__(kAttn4Threads, 1)
     attention_fwd_dh64_quad_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                    const __grid_constant__ CUtensorMap tmap_kv, AttnArgs args) {
@@ -904,7 +910,17 @@ __global__ void __launch_bounds__(kAttn4Threads, 1)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = n_kv_mine > 0;
+    const uint8_t* key_valid =
+        kMasked ? args.key_valid + static_cast<int64_t>(batch) * args.seq : nullptr;
     for (int j = 0; ok && j < n_kv_mine; ++j) {
+      // Padding flags of this KV tile's 64 keys (two per lane), loaded before
+      // the wait so that their latency overlaps it.
+      bool kv0 = true, kv1 = true;
+      if (kMasked) {
+        const int c0 = j * kAttn4BN + lane;
+        kv0 = c0 < args.seq && key_valid[c0] != 0;
+        kv1 = c0 + 32 < args.seq && key_valid[c0 + 32] != 0;
+      }
       ok = mbar_wait(&s_full_bar[w], j & 1, kErrAttnSoftmaxWait, &abort_flag);
       if (__any_sync(0xffffffffu, !ok)) {
         ok = false;
@@ -930,6 +946,15 @@ __global__ void __launch_bounds__(kAttn4Threads, 1)
         for (int i = 0; i < kAttn4BN; ++i)
           if (i >= limit) s[i] = __float_as_uint(-INFINITY);
       }
+      if (kMasked) {
+        const uint32_t lo = __ballot_sync(0xffffffffu, kv0);
+        const uint32_t hi = __ballot_sync(0xffffffffu, kv1);
+        if ((lo & hi) != 0xffffffffu) {
+#pragma unroll
+          for (int i = 0; i < kAttn4BN; ++i)
+            if (!(((i < 32 ? lo : hi) >> (i & 31)) & 1u)) s[i] = __float_as_uint(-INFINITY);
+        }
+      }
       float mp[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(s[k]);
@@ -947,8 +972,11 @@ __global__ void __launch_bounds__(kAttn4Threads, 1)
       const bool need = mx_scaled > m_run + kAttn4MaxSlack;
       const float m_new = need ? mx_scaled : m_run;
       const float alpha = need ? fast_exp2(m_run - m_new) : 1.0f;  // 0 on the first tile
+      // A row that has seen no valid key yet (padding) keeps m = -inf; its
+      // scores are all -inf, so any finite offset gives p = 0 without NaN.
+      const float m_use = (kMasked && m_new == -INFINITY) ? 0.0f : m_new;
       const uint64_t c2 = f32x2(c, c);
-      const uint64_t neg_m2 = f32x2(-m_new, -m_new);
+      const uint64_t neg_m2 = f32x2(-m_use, -m_use);
       uint64_t acc[2] = {0, 0};
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
@@ -990,7 +1018,8 @@ __global__ void __launch_bounds__(kAttn4Threads, 1)
       __syncwarp();
       if (all_ok) {
         tc_fence_after();
-        const float inv_l = 1.0f / l_run;
+        // l = 0 only for a padding query that sees no valid key: zero row.
+        const float inv_l = (!kMasked || l_run > 0.0f) ? 1.0f / l_run : 0.0f;
         __nv_bfloat16* out_row =
             args.out + (static_cast<int64_t>(batch) * args.seq + q_idx) * d_model + head * kAttnDh;
 #pragma unroll 1

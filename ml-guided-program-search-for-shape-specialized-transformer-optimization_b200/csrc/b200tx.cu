@@ -47,7 +47,7 @@ struct DeviceState {
   int cc_major = 0;
   int cc_minor = 0;
   bool gemm_attr[4] = {false, false, false, false};
-  bool attn_attr[3] = {false, false, false};
+  bool attn_attr[4] = {false, false, false, false};  // variants 0-2, masked quad
 };
 
 std::mutex g_mutex;
@@ -200,10 +200,17 @@ int b200tx_device_error(int clear, unsigned int* code_out) {
   return B200TX_OK;
 }
 
-int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void* update,
-                               int update_dtype, float* residual_out, void* normed,
-                               int out_dtype, const float* gamma, const float* beta,
-                               int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int residual_layer_norm_impl(const void* residual_in, int in_dtype, const void* update,
+                             int update_dtype, float* residual_out, void* normed, int out_dtype,
+                             const float* gamma, const float* beta, const uint8_t* row_valid,
+                             int mask_mode, int64_t rows, int64_t cols, float eps,
+                             cudaStream_t stream) {
+  if (mask_mode < 0 || mask_mode > 7)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: mask_mode %d", mask_mode);
   if (residual_in == nullptr || normed == nullptr || gamma == nullptr || beta == nullptr)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm: null tensor pointer");
   if (rows <= 0 || cols <= 0 || cols > (1 << 20))
@@ -228,6 +235,8 @@ int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void
   a.normed = normed;
   a.gamma = gamma;
   a.beta = beta;
+  a.row_valid = row_valid;
+  a.mask_mode = row_valid != nullptr ? mask_mode : 0;
   a.rows = rows;
   a.cols = static_cast<int>(cols);
   a.eps = eps;
@@ -252,6 +261,30 @@ int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void
   }
   if (err != cudaSuccess) return cuda_fail(err, "residual_layer_norm launch");
   return B200TX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200tx_residual_layer_norm(const void* residual_in, int in_dtype, const void* update,
+                               int update_dtype, float* residual_out, void* normed,
+                               int out_dtype, const float* gamma, const float* beta,
+                               int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  return residual_layer_norm_impl(residual_in, in_dtype, update, update_dtype, residual_out, normed,
+                                  out_dtype, gamma, beta, nullptr, 0, rows, cols, eps, stream);
+}
+
+int b200tx_residual_layer_norm_masked(const void* residual_in, int in_dtype, const void* update,
+                                      int update_dtype, float* residual_out, void* normed,
+                                      int out_dtype, const float* gamma, const float* beta,
+                                      const uint8_t* row_valid, int mask_mode, int64_t rows,
+                                      int64_t cols, float eps, cudaStream_t stream) {
+  if (row_valid == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_masked: null row_valid");
+  return residual_layer_norm_impl(residual_in, in_dtype, update, update_dtype, residual_out, normed,
+                                  out_dtype, gamma, beta, row_valid, mask_mode, rows, cols, eps,
+                                  stream);
 }
 
 int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
@@ -326,8 +359,13 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
   return B200TX_OK;
 }
 
-int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
-                        int64_t head_dim, float scale, int causal, int variant, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                   int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                   int variant, cudaStream_t stream) {
   if (qkv == nullptr || out == nullptr)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: null tensor pointer");
   if (batch <= 0 || seq <= 0 || heads <= 0)
@@ -340,6 +378,10 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: variant %d", variant);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
+  if (key_valid != nullptr && variant != B200TX_ATTN_QUAD)
+    return fail(B200TX_ERR_UNSUPPORTED,
+                "attention: padding masks are built into the QUAD variant only (variant %d)",
+                variant);
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
   const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
   const int64_t units = variant == B200TX_ATTN_PAIRED ? (q_tiles + 1) / 2
@@ -365,6 +407,7 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
   }
   b200tx::AttnArgs args;
   args.out = static_cast<__nv_bfloat16*>(out);
+  args.key_valid = key_valid;
   args.batch = static_cast<int>(batch);
   args.seq = static_cast<int>(seq);
   args.heads = static_cast<int>(heads);
@@ -380,18 +423,22 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
     const uint32_t box[3] = {b200tx::kAttnDh, b200tx::kAttn4BN, 1};
     rc = encode_bf16_map(&map_kv, qkv, 3, dims, strides, box);
     if (rc != B200TX_OK) return rc;
+    using QuadFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
+    const QuadFn quad_kernel = key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true>
+                                                    : b200tx::attention_fwd_dh64_quad_kernel<false>;
+    const int attr_slot = key_valid != nullptr ? 3 : variant;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
-      if (!dev->attn_attr[variant]) {
-        cudaError_t err = cudaFuncSetAttribute(b200tx::attention_fwd_dh64_quad_kernel,
+      if (!dev->attn_attr[attr_slot]) {
+        cudaError_t err = cudaFuncSetAttribute(quad_kernel,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(b200tx::kAttn4SmemBytes));
         if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
-        dev->attn_attr[variant] = true;
+        dev->attn_attr[attr_slot] = true;
       }
     }
-    b200tx::attention_fwd_dh64_quad_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttn4Threads,
-                                             b200tx::kAttn4SmemBytes, stream>>>(map_qkv, map_kv, args);
+    quad_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttn4Threads, b200tx::kAttn4SmemBytes,
+                  stream>>>(map_qkv, map_kv, args);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
@@ -414,6 +461,25 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "attention launch");
   return B200TX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,
+                        int64_t head_dim, float scale, int causal, int variant, cudaStream_t stream) {
+  return attention_impl(qkv, nullptr, out, batch, seq, heads, head_dim, scale, causal, variant,
+                        stream);
+}
+
+int b200tx_attention_masked(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                            int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                            int variant, cudaStream_t stream) {
+  if (key_valid == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_masked: null key_valid");
+  return attention_impl(qkv, key_valid, out, batch, seq, heads, head_dim, scale, causal, variant,
+                        stream);
 }
 
 int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,

@@ -9,6 +9,13 @@
 //   n = (r - mean(r)) * rsqrt(var(r) + eps) * gamma + beta
 // with the biased variance over the row, computed two-pass in registers.
 //
+// Padding masks (official/torch_transformer_benchmark.py:119-121, 143-144,
+// 170-171): with `row_valid`, a row whose flag is 0 follows `mask_mode`:
+//   kNormMaskDropUpdate   r = residual_in           (attention output zeroed)
+//   kNormMaskZeroResidual r = 0                     (block output zeroed)
+//   kNormMaskZeroNormed   normed = 0                (final output zeroed)
+// The branch is per row, so uniform across the row's warp.
+//
 // Layout: row-major [rows, cols].  For cols % 128 == 0 (every BASELINE width)
 // each lane owns cols/128 groups of four consecutive columns, so each warp
 // instruction touches 512 contiguous bytes of fp32 (256 of bf16): 128-bit
@@ -19,6 +26,10 @@
 
 namespace b200tx {
 
+constexpr int kNormMaskDropUpdate = 1;
+constexpr int kNormMaskZeroResidual = 2;
+constexpr int kNormMaskZeroNormed = 4;
+
 struct NormArgs {
   const void* residual_in;  // [rows, cols] fp32 or bf16
   const void* update;       // [rows, cols] bf16 or fp32; null for a plain LayerNorm
@@ -26,10 +37,28 @@ struct NormArgs {
   void* normed;             // [rows, cols] bf16 or fp32
   const float* gamma;       // [cols]
   const float* beta;        // [cols]
+  const uint8_t* row_valid; // [rows] 0/1 or null (every row valid)
+  int mask_mode;            // kNormMask* bits applied to rows whose flag is 0
   int64_t rows;
   int cols;
   float eps;
 };
+
+// Which of the masked behaviours apply to this row.
+struct RowMask {
+  bool add_update;
+  bool zero_residual;
+  bool zero_normed;
+};
+
+__device__ __forceinline__ RowMask row_mask(const NormArgs& a, int64_t row) {
+  const bool valid = a.row_valid == nullptr || a.row_valid[row] != 0;
+  RowMask m;
+  m.add_update = valid || !(a.mask_mode & kNormMaskDropUpdate);
+  m.zero_residual = !valid && (a.mask_mode & kNormMaskZeroResidual);
+  m.zero_normed = !valid && (a.mask_mode & kNormMaskZeroNormed);
+  return m;
+}
 
 template <typename T>
 __device__ __forceinline__ float4 load4(const T* base, int64_t idx);
@@ -106,18 +135,26 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
   const int64_t base = row * cols;
   const InT* rin = static_cast<const InT*>(args.residual_in);
 
+  const RowMask mask = row_mask(args, row);
   float4 v[NV];
+  if (mask.zero_residual) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) v[i] = load4<InT>(rin, base + (i * 32 + lane) * 4);
-  if constexpr (!std::is_same<UpdT, void>::value) {
-    const UpdT* upd = static_cast<const UpdT*>(args.update);
+    for (int i = 0; i < NV; ++i) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const float4 u = load4<UpdT>(upd, base + (i * 32 + lane) * 4);
-      v[i].x += u.x;
-      v[i].y += u.y;
-      v[i].z += u.z;
-      v[i].w += u.w;
+    for (int i = 0; i < NV; ++i) v[i] = load4<InT>(rin, base + (i * 32 + lane) * 4);
+    if constexpr (!std::is_same<UpdT, void>::value) {
+      if (mask.add_update) {
+        const UpdT* upd = static_cast<const UpdT*>(args.update);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const float4 u = load4<UpdT>(upd, base + (i * 32 + lane) * 4);
+          v[i].x += u.x;
+          v[i].y += u.y;
+          v[i].z += u.z;
+          v[i].w += u.w;
+        }
+      }
     }
   }
   if (args.residual_out != nullptr) {
@@ -149,6 +186,7 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
     o.y = (v[i].y - mean) * rstd * g.y + b.y;
     o.z = (v[i].z - mean) * rstd * g.z + b.z;
     o.w = (v[i].w - mean) * rstd * g.w + b.w;
+    if (mask.zero_normed) o = make_float4(0.f, 0.f, 0.f, 0.f);
     store4<OutT>(out, base + c, o);
   }
 }
@@ -165,9 +203,13 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
   const int64_t base = row * cols;
   const InT* rin = static_cast<const InT*>(args.residual_in);
   const UpdT* upd = static_cast<const UpdT*>(args.update);
+  const RowMask mask = row_mask(args, row);
   auto value_at = [&](int c) -> float {
+    if (mask.zero_residual) return 0.f;
     float x = load1<InT>(rin, base + c);
-    if constexpr (!std::is_same<UpdT, void>::value) x += load1<UpdT>(upd, base + c);
+    if constexpr (!std::is_same<UpdT, void>::value) {
+      if (mask.add_update) x += load1<UpdT>(upd, base + c);
+    }
     return x;
   };
   float s = 0.f;
@@ -185,7 +227,8 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
     // Every lane reads its own columns before writing them, so an in-place
     // residual update (residual_out == residual_in) stays exact.
     if (args.residual_out != nullptr) args.residual_out[base + c] = x;
-    store1<OutT>(out, base + c, (x - mean) * rstd * args.gamma[c] + args.beta[c]);
+    store1<OutT>(out, base + c,
+                 mask.zero_normed ? 0.f : (x - mean) * rstd * args.gamma[c] + args.beta[c]);
   }
 }
 

@@ -24,6 +24,9 @@ EPI_BIAS_GELU = 1
 ATTN_PAIRED = 0
 ATTN_SINGLE = 1
 ATTN_QUAD = 2
+MASK_DROP_UPDATE = 1
+MASK_ZERO_RESIDUAL = 2
+MASK_ZERO_NORMED = 4
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -62,6 +65,24 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_float,  # eps
         _c_void_p,  # stream
     ]
+    lib.b200tx_residual_layer_norm_masked.restype = ctypes.c_int
+    lib.b200tx_residual_layer_norm_masked.argtypes = [
+        _c_void_p,  # residual_in
+        ctypes.c_int,  # in_dtype
+        _c_void_p,  # update
+        ctypes.c_int,  # update_dtype
+        _c_void_p,  # residual_out
+        _c_void_p,  # normed
+        ctypes.c_int,  # out_dtype
+        _c_void_p,  # gamma
+        _c_void_p,  # beta
+        _c_void_p,  # row_valid
+        ctypes.c_int,  # mask_mode
+        _c_int64,  # rows
+        _c_int64,  # cols
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
     lib.b200tx_linear.restype = ctypes.c_int
     lib.b200tx_linear.argtypes = [
         _c_void_p,  # a
@@ -90,6 +111,20 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b200tx_attention_ex.restype = ctypes.c_int
     lib.b200tx_attention_ex.argtypes = [
         _c_void_p,  # qkv
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # heads
+        _c_int64,  # head_dim
+        ctypes.c_float,  # scale
+        ctypes.c_int,  # causal
+        ctypes.c_int,  # variant
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_attention_masked.restype = ctypes.c_int
+    lib.b200tx_attention_masked.argtypes = [
+        _c_void_p,  # qkv
+        _c_void_p,  # key_valid
         _c_void_p,  # out
         _c_int64,  # batch
         _c_int64,  # seq
@@ -194,29 +229,39 @@ def residual_layer_norm(
     gamma: torch.Tensor,
     beta: torch.Tensor,
     eps: float,
+    row_valid: torch.Tensor | None = None,
+    mask_mode: int = 0,
 ) -> None:
-    """Launch b200tx_residual_layer_norm on the current stream (no checks beyond the C side)."""
+    """Launch b200tx_residual_layer_norm (or its _masked form when ``row_valid``
+    is given: uint8 [rows] flags, 0 = padding row, handled per ``mask_mode``)
+    on the current stream (no checks beyond the C side)."""
 
     cols = residual_in.shape[-1]
     rows = residual_in.numel() // cols
     lib = load()
+    common = (
+        residual_in.data_ptr(),
+        dtype_code(residual_in.dtype),
+        None if update is None else update.data_ptr(),
+        F32 if update is None else dtype_code(update.dtype),
+        None if residual_out is None else residual_out.data_ptr(),
+        normed.data_ptr(),
+        dtype_code(normed.dtype),
+        gamma.data_ptr(),
+        beta.data_ptr(),
+    )
+    stream = _stream(residual_in.device)
+    if row_valid is None:
+        _check(
+            lib.b200tx_residual_layer_norm(*common, rows, cols, float(eps), stream),
+            "b200tx_residual_layer_norm",
+        )
+        return
     _check(
-        lib.b200tx_residual_layer_norm(
-            residual_in.data_ptr(),
-            dtype_code(residual_in.dtype),
-            None if update is None else update.data_ptr(),
-            F32 if update is None else dtype_code(update.dtype),
-            None if residual_out is None else residual_out.data_ptr(),
-            normed.data_ptr(),
-            dtype_code(normed.dtype),
-            gamma.data_ptr(),
-            beta.data_ptr(),
-            rows,
-            cols,
-            float(eps),
-            _stream(residual_in.device),
+        lib.b200tx_residual_layer_norm_masked(
+            *common, row_valid.data_ptr(), int(mask_mode), rows, cols, float(eps), stream
         ),
-        "b200tx_residual_layer_norm",
+        "b200tx_residual_layer_norm_masked",
     )
 
 
@@ -260,24 +305,25 @@ def attention(
     scale: float,
     causal: bool,
     variant: int = ATTN_QUAD,
+    key_valid: torch.Tensor | None = None,
 ) -> None:
-    """Launch b200tx_attention_ex over a packed [B, S, 3D] projection."""
+    """Launch b200tx_attention_ex over a packed [B, S, 3D] projection, or
+    b200tx_attention_masked when ``key_valid`` (uint8 [B, S], 0 = padding key)
+    is given."""
 
     lib = load()
+    shape = (int(batch), int(seq), int(heads), int(head_dim), float(scale), int(bool(causal)), int(variant))
+    if key_valid is None:
+        _check(
+            lib.b200tx_attention_ex(qkv.data_ptr(), out.data_ptr(), *shape, _stream(qkv.device)),
+            "b200tx_attention_ex",
+        )
+        return
     _check(
-        lib.b200tx_attention_ex(
-            qkv.data_ptr(),
-            out.data_ptr(),
-            int(batch),
-            int(seq),
-            int(heads),
-            int(head_dim),
-            float(scale),
-            int(bool(causal)),
-            int(variant),
-            _stream(qkv.device),
+        lib.b200tx_attention_masked(
+            qkv.data_ptr(), key_valid.data_ptr(), out.data_ptr(), *shape, _stream(qkv.device)
         ),
-        "b200tx_attention_ex",
+        "b200tx_attention_masked",
     )
 
 
@@ -290,6 +336,9 @@ __all__ = [
     "EPI_BIAS",
     "EPI_BIAS_GELU",
     "F32",
+    "MASK_DROP_UPDATE",
+    "MASK_ZERO_NORMED",
+    "MASK_ZERO_RESIDUAL",
     "attention",
     "device_check",
     "device_error",

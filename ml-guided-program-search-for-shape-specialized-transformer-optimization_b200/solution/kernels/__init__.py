@@ -17,6 +17,9 @@ from .attention import (
     sm100_flash_attention_available,
 )
 from .norm import (
+    MASK_DROP_UPDATE,
+    MASK_ZERO_NORMED,
+    MASK_ZERO_RESIDUAL,
     SM100_INITIAL_LAYER_NORM_BACKEND,
     SM100_RESIDUAL_LAYER_NORM_BACKEND,
     can_use_sm100_residual_layer_norm,
@@ -33,6 +36,9 @@ from .projection import (
 )
 
 __all__ = [
+    "MASK_DROP_UPDATE",
+    "MASK_ZERO_NORMED",
+    "MASK_ZERO_RESIDUAL",
     "SM100_FLASH_ATTENTION_BACKEND",
     "SM100_INITIAL_LAYER_NORM_BACKEND",
     "SM100_LINEAR_BACKEND",

@@ -7,6 +7,8 @@ query-blocked reference operators (solution/operators/attention/sdpa.py:76-170)
 and ``split_qkv`` (solution/operators/projection/qkv_layout.py:22-50): the
 kernel reads Q/K/V head tiles straight out of the packed ``[B, S, 3D]`` QKV
 projection and writes the ``[B, S, D]`` context the out-projection consumes.
+A ``key_valid`` padding mask (uint8 ``[B, S]``) masks padding keys with -inf
+as the official block does (official/torch_transformer_benchmark.py:105-108).
 """
 
 from __future__ import annotations
@@ -46,8 +48,11 @@ def sm100_flash_attention(
     causal: bool = True,
     out: torch.Tensor | None = None,
     variant: int = _native.ATTN_QUAD,
+    key_valid: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, str]:
-    """``softmax(q k^T / 8 [+ causal]) v`` per head; returns the ``[B, S, D]`` context."""
+    """``softmax(q k^T / 8 [+ causal] [+ key padding]) v`` per head; returns
+    the ``[B, S, D]`` context.  With ``key_valid`` only the QUAD variant is
+    built; a query that sees no valid key gets a zero row."""
 
     if not can_use_sm100_flash_attention(qkv, num_heads):
         raise RuntimeError("sm100 flash attention is ineligible for the requested inputs")
@@ -65,6 +70,15 @@ def sm100_flash_attention(
         and result.data_ptr() % 16 == 0,
         "out must be a contiguous, 16-byte aligned bf16 [B, S, D] tensor",
     )
+    if key_valid is not None:
+        require(
+            key_valid.dtype == torch.uint8
+            and key_valid.device == qkv.device
+            and key_valid.is_contiguous()
+            and tuple(key_valid.shape) == (batch, seq),
+            "key_valid must be a contiguous uint8 [B, S] tensor on the qkv device",
+        )
+        require(variant == _native.ATTN_QUAD, "padding masks are built into the QUAD variant only")
     launch(
         _native.attention,
         qkv,
@@ -76,6 +90,7 @@ def sm100_flash_attention(
         HEAD_DIM**-0.5,
         causal,
         variant,
+        key_valid,
     )
     return result, SM100_FLASH_ATTENTION_BACKEND
 

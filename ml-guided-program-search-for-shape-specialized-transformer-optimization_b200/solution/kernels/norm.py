@@ -5,7 +5,11 @@ Replaces the reference's ``triton_initial_fp16_layer_norm``
 (solution/kernels/norm/triton_residual.py:38-73) and
 ``triton_mixed_residual_layer_norm``
 (solution/kernels/norm/triton_mixed_residual.py:40-160): fp32 residual stream,
-bf16 normalised output, fp32 output at the final boundary.
+bf16 normalised output, fp32 output at the final boundary.  With a padding
+mask (``row_valid``, uint8 per row) the kernel also applies the reference's
+``masked_fill`` of padding rows (official/torch_transformer_benchmark.py:
+119-121, 143-144, 170-171; masked LayerNorm solution/kernels/norm/
+triton_masked.py:47-118) per ``mask_mode``.
 """
 
 from __future__ import annotations
@@ -20,6 +24,23 @@ SM100_RESIDUAL_LAYER_NORM_BACKEND = "sm100_residual_layer_norm"
 SM100_INITIAL_LAYER_NORM_BACKEND = "sm100_initial_layer_norm"
 
 _IO = (torch.float32, torch.bfloat16)
+
+MASK_DROP_UPDATE = _native.MASK_DROP_UPDATE
+MASK_ZERO_RESIDUAL = _native.MASK_ZERO_RESIDUAL
+MASK_ZERO_NORMED = _native.MASK_ZERO_NORMED
+
+
+def _check_row_valid(row_valid: torch.Tensor | None, value: torch.Tensor) -> None:
+    if row_valid is None:
+        return
+    rows = value.numel() // value.shape[-1]
+    require(
+        row_valid.dtype == torch.uint8
+        and row_valid.device == value.device
+        and row_valid.is_contiguous()
+        and row_valid.numel() == rows,
+        f"row_valid must be a contiguous uint8 tensor of {rows} flags on {value.device}",
+    )
 
 
 def sm100_layer_norm_available() -> bool:
@@ -68,13 +89,16 @@ def sm100_residual_layer_norm(
     out_dtype: torch.dtype | None = None,
     residual_out: torch.Tensor | None = None,
     normalized_out: torch.Tensor | None = None,
+    row_valid: torch.Tensor | None = None,
+    mask_mode: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor, str]:
     """``r = value + update`` (fp32) and ``LN(r)``.
 
     The normalised output is bf16 for an inner boundary and fp32 at the final
     boundary unless ``out_dtype`` says otherwise (the model passes its input
     dtype there).  ``residual_out`` may be ``value`` itself for an in-place
-    update of an fp32 residual stream.
+    update of an fp32 residual stream.  ``row_valid`` / ``mask_mode`` apply
+    the padding-mask behaviours (MASK_* bits) to rows whose flag is 0.
     """
 
     if not can_use_sm100_residual_layer_norm(value, update, layer_norm):
@@ -98,6 +122,7 @@ def sm100_residual_layer_norm(
         normalized.shape == value.shape and normalized.dtype == out_dtype,
         f"normalized_out must be {out_dtype} of shape {tuple(value.shape)}",
     )
+    _check_row_valid(row_valid, value)
     launch(
         _native.residual_layer_norm,
         value,
@@ -107,6 +132,8 @@ def sm100_residual_layer_norm(
         layer_norm.weight,
         layer_norm.bias,
         layer_norm.eps,
+        row_valid,
+        mask_mode,
     )
     return residual, normalized, SM100_RESIDUAL_LAYER_NORM_BACKEND
 
@@ -146,6 +173,9 @@ def sm100_initial_layer_norm(
 
 
 __all__ = [
+    "MASK_DROP_UPDATE",
+    "MASK_ZERO_NORMED",
+    "MASK_ZERO_RESIDUAL",
     "SM100_INITIAL_LAYER_NORM_BACKEND",
     "SM100_RESIDUAL_LAYER_NORM_BACKEND",
     "can_use_sm100_residual_layer_norm",

@@ -32,6 +32,8 @@ from .plan import ExecutionContext, ExecutionPlan, ExpectedExecutionTrace
 Reject = Callable[[str, str, str], None]
 
 SUPPORTED_HEAD_DIMS = frozenset({64})
+# The attention variant that reads a key padding mask (B200TX_ATTN_QUAD).
+SM100_QUAD_ATTENTION_VARIANT = 2
 SUPPORTED_IO_DTYPES = frozenset({torch.float32, torch.bfloat16})
 _INT32_MAX = 2**31 - 1
 
@@ -240,13 +242,6 @@ class PlanBuilder:
             )
         if not context.input_contiguous:
             reject("requires_contiguous_input", "input", "input must be contiguous")
-        if context.has_valid_token_mask:
-            reject(
-                "mask_not_supported",
-                "valid_token_mask",
-                "padding masks are not implemented by the sm100 kernels; "
-                "all-valid masks are collapsed before planning",
-            )
 
     @staticmethod
     def _validate_runtime(
@@ -274,6 +269,18 @@ class PlanBuilder:
     @staticmethod
     def _validate_shapes(config: ConfigSpec, context: ExecutionContext, reject: Reject) -> None:
         head_dim = context.head_dim
+        launch = config.schedule.attention_launch
+        if (
+            context.has_valid_token_mask
+            and launch is not None
+            and launch.kernel_variant != SM100_QUAD_ATTENTION_VARIANT
+        ):
+            reject(
+                "mask_not_supported",
+                "schedule.attention_launch",
+                "padding masks are built into the quad attention variant "
+                "(block_m 512, block_n 64, kv_stages 6) only",
+            )
         if config.program.attention is AttentionBackend.SM100_FLASH:
             if head_dim is not None and head_dim not in SUPPORTED_HEAD_DIMS:
                 reject(

@@ -31,6 +31,9 @@ from torch import nn
 
 from .config import ConfigSpec, RuntimeBackend, portable_config
 from .kernels import (
+    MASK_DROP_UPDATE,
+    MASK_ZERO_NORMED,
+    MASK_ZERO_RESIDUAL,
     SM100_FLASH_ATTENTION_BACKEND,
     SM100_INITIAL_LAYER_NORM_BACKEND,
     SM100_LINEAR_BACKEND,
@@ -529,8 +532,6 @@ class UserOptimizedTransformer(nn.Module):
     ) -> torch.Tensor:
         """One pass of the planned program over ``value`` ([B, S, D], contiguous)."""
 
-        if valid_token_mask is not None:
-            raise RuntimeError("the sm100 program has no padding-mask path (plan should reject)")
         observation = (
             _ExecutionObservation(config_id=plan.config_id)
             if observe and self._execution_observation_enabled
@@ -550,13 +551,35 @@ class UserOptimizedTransformer(nn.Module):
 
         flat_in = value.reshape(rows, d_model)
         output = torch.empty((batch, seq, d_model), dtype=value.dtype, device=device)
+        # Padding mask (official/torch_transformer_benchmark.py:105-121,
+        # 143-144, 170-171): keys of padding tokens are masked in attention,
+        # their attention output is dropped, each block's output rows and the
+        # final output rows are zeroed.  The bool mask is read as uint8 flags
+        # in place (no copy for a contiguous mask).
+        key_valid = None
+        row_valid = None
+        if valid_token_mask is not None:
+            key_valid = valid_token_mask.contiguous().view(torch.uint8)
+            row_valid = key_valid.view(rows)
         if n_layers == 0:
-            sm100_initial_layer_norm(
-                flat_in,
-                self.final_norm.kernel_norm(),
-                out_dtype=value.dtype,
-                normalized_out=output.view(rows, d_model),
-            )
+            if row_valid is None:
+                sm100_initial_layer_norm(
+                    flat_in,
+                    self.final_norm.kernel_norm(),
+                    out_dtype=value.dtype,
+                    normalized_out=output.view(rows, d_model),
+                )
+            else:
+                sm100_residual_layer_norm(
+                    flat_in,
+                    None,
+                    self.final_norm.kernel_norm(),
+                    final_boundary=True,
+                    out_dtype=value.dtype,
+                    normalized_out=output.view(rows, d_model),
+                    row_valid=row_valid,
+                    mask_mode=MASK_ZERO_NORMED,
+                )
             return output
 
         residual = torch.empty((rows, d_model), dtype=torch.float32, device=device)
@@ -601,7 +624,7 @@ class UserOptimizedTransformer(nn.Module):
             )
             token = rec.start("attention")
             _, marker = sm100_flash_attention(
-                qkv, heads, causal=causal, out=context, variant=attention_variant
+                qkv, heads, causal=causal, out=context, variant=attention_variant, key_valid=key_valid
             )
             rec.stop(token)
             _strict_backend_marker(
@@ -626,6 +649,8 @@ class UserOptimizedTransformer(nn.Module):
                 final_boundary=False,
                 residual_out=residual,
                 normalized_out=normalized,
+                row_valid=row_valid,
+                mask_mode=MASK_DROP_UPDATE,
             )
             rec.stop(token)
             _strict_backend_marker(
@@ -663,6 +688,8 @@ class UserOptimizedTransformer(nn.Module):
                 out_dtype=value.dtype if last else torch.bfloat16,
                 residual_out=residual,
                 normalized_out=output.view(rows, d_model) if last else normalized,
+                row_valid=row_valid,
+                mask_mode=MASK_ZERO_RESIDUAL | (MASK_ZERO_NORMED if last else 0),
             )
             rec.stop(token)
             _strict_backend_marker(

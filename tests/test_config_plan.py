@@ -168,7 +168,6 @@ def test_precision_plan_sets_update_dtypes() -> None:
         ({"grad_enabled": True}, B200, "requires_inference"),
         ({"dtype": torch.float16}, B200, "unsupported_dtype"),
         ({"input_contiguous": False}, B200, "requires_contiguous_input"),
-        ({"has_valid_token_mask": True}, B200, "mask_not_supported"),
         ({"d_model": 256, "num_heads": 2}, B200, "unsupported_shape"),  # head_dim 128
         ({"d_model": 250, "num_heads": 5}, B200, "unsupported_shape"),
         ({"ffn_dim": 1020}, B200, "unsupported_shape"),
@@ -182,6 +181,21 @@ def test_structured_rejections(overrides: dict, hardware: HardwareCapabilities, 
     assert code in _codes(result)
     with pytest.raises(ConfigRejectedError):
         result.require_plan()
+
+
+def test_padding_masks_need_the_quad_attention_variant() -> None:
+    masked = _context(has_valid_token_mask=True)
+    plan = PlanBuilder().build(portable_config(), masked, B200)
+    assert plan.describe()["valid_token_mask"] == "direct_key_mask"
+    paired = ConfigSpec(
+        program=default_program(),
+        schedule=replace(
+            default_schedule(), attention_launch=Sm100AttentionParams(block_m=256, block_n=128, kv_stages=3)
+        ),
+    )
+    assert PlanBuilder().evaluate(paired, _context(), B200).accepted
+    result = PlanBuilder().evaluate(paired, masked, B200)
+    assert "mask_not_supported" in _codes(result)
 
 
 def test_runtime_rules() -> None:

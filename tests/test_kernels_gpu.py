@@ -232,3 +232,114 @@ def test_attention_large_logits_stay_finite(variant: int) -> None:
     assert np.isfinite(got).all()
     max_abs, rel = parity_errors(got, ref)
     assert rel < 2e-2, rel
+
+
+# ---------------------------------------------------------------- padding masks
+def _masked_attention_reference(
+    q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool, key_valid: np.ndarray
+) -> np.ndarray:
+    """Official scores with causal and key-padding -inf (official :97-112); a
+    query with no valid key gets a zero row (the kernel's convention; the
+    reference's NaN row there is zeroed by the caller's masked_fill)."""
+
+    seq = q.shape[2]
+    scores = np.matmul(q, k.transpose(0, 1, 3, 2)) * np.float32(q.shape[-1] ** -0.5)
+    if causal:
+        scores = np.where(np.triu(np.ones((seq, seq), bool), 1)[None, None], np.float32(-np.inf), scores)
+    scores = np.where(~key_valid[:, None, None, :], np.float32(-np.inf), scores)
+    m = scores.max(axis=-1, keepdims=True)
+    m = np.where(np.isfinite(m), m, np.float32(0.0))
+    p = np.exp(scores - m, dtype=np.float32)
+    l = p.sum(axis=-1, keepdims=True)
+    return np.matmul(p, v) / np.where(l > 0, l, np.float32(1.0))
+
+
+@pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal", "pattern"),
+    [
+        (2, 300, 2, True, "random"),
+        (2, 640, 1, True, "left"),  # queries before the first valid key see none
+        (3, 257, 2, False, "right"),
+        (2, 1000, 2, True, "one_empty_row"),
+        (1, 129, 1, False, "random"),
+    ],
+)
+def test_attention_key_padding_mask(batch: int, seq: int, heads: int, causal: bool, pattern: str) -> None:
+    g = torch.Generator().manual_seed(seq + heads)
+    qkv = torch.randn(batch, seq, 3 * heads * 64, generator=g).to(torch.bfloat16)
+    if pattern == "random":
+        valid = torch.rand(batch, seq, generator=g) > 0.3
+    elif pattern == "left":
+        valid = torch.arange(seq)[None, :] >= torch.tensor([[70], [200]])[:batch]
+    elif pattern == "right":
+        valid = torch.arange(seq)[None, :] < torch.tensor([[257], [100], [1]])[:batch]
+    else:
+        valid = torch.rand(batch, seq, generator=g) > 0.5
+        valid[1] = False
+    q, k, v = qkv.float().view(batch, seq, 3, heads, 64).permute(2, 0, 3, 1, 4).numpy()
+    ref = _masked_attention_reference(q, k, v, causal, valid.numpy())
+    ref = ref.transpose(0, 2, 1, 3).reshape(batch, seq, heads * 64)
+    key_valid = valid.to(DEV).view(torch.uint8)
+    with torch.inference_mode():
+        out, _ = sm100_flash_attention(qkv.to(DEV), heads, causal=causal, key_valid=key_valid)
+    got = _bf16_np(out)
+    assert np.isfinite(got).all()
+    max_abs, rel = parity_errors(got, ref)
+    assert rel < 1e-2 and max_abs < 2e-2, (pattern, max_abs, rel)
+    if pattern == "one_empty_row":
+        assert not got[1].any()
+
+
+def test_attention_all_valid_mask_equals_unmasked() -> None:
+    g = torch.Generator().manual_seed(21)
+    qkv = torch.randn(2, 700, 3 * 4 * 64, generator=g).to(torch.bfloat16).to(DEV)
+    ones = torch.ones(2, 700, dtype=torch.uint8, device=DEV)
+    with torch.inference_mode():
+        a, _ = sm100_flash_attention(qkv, 4)
+        b, _ = sm100_flash_attention(qkv, 4, key_valid=ones)
+    assert torch.equal(a, b)
+
+
+def test_attention_mask_needs_the_quad_variant() -> None:
+    qkv = torch.zeros(1, 128, 3 * 64, dtype=torch.bfloat16, device=DEV)
+    ones = torch.ones(1, 128, dtype=torch.uint8, device=DEV)
+    with torch.inference_mode(), pytest.raises(ValueError, match="QUAD"):
+        sm100_flash_attention(qkv, 1, key_valid=ones, variant=_native.ATTN_PAIRED)
+
+
+@pytest.mark.parametrize("mode", [1, 2, 4, 2 | 4, 1 | 4])
+@pytest.mark.parametrize("cols", [1024, 96])
+def test_residual_layer_norm_row_mask(mode: int, cols: int) -> None:
+    rows = 300
+    g = torch.Generator().manual_seed(mode * 7 + cols)
+    resid = torch.randn(rows, cols, generator=g) * 2
+    update = torch.randn(rows, cols, generator=g).to(torch.bfloat16)
+    valid = torch.rand(rows, generator=g) > 0.4
+    gamma = torch.randn(cols, generator=g)
+    beta = torch.randn(cols, generator=g)
+    ln = torch.nn.LayerNorm(cols).to(DEV)
+    with torch.no_grad():
+        ln.weight.copy_(gamma)
+        ln.bias.copy_(beta)
+    r = resid + update.float()
+    keep = valid[:, None]
+    if mode & 1:
+        r = torch.where(keep, r, resid)
+    if mode & 2:
+        r = torch.where(keep, r, torch.zeros(()))
+    n = torch.from_numpy(layer_norm(r.numpy(), gamma.numpy(), beta.numpy()))
+    if mode & 4:
+        n = torch.where(keep, n, torch.zeros(()))
+    with torch.inference_mode():
+        r_out, n_out, _ = sm100_residual_layer_norm(
+            resid.to(DEV),
+            update.to(DEV),
+            ln,
+            final_boundary=True,
+            row_valid=valid.to(DEV).view(torch.uint8),
+            mask_mode=mode,
+        )
+    torch.testing.assert_close(r_out.cpu(), r, rtol=0, atol=1e-6)
+    torch.testing.assert_close(n_out.cpu(), n, rtol=1e-5, atol=1e-5)
+    if mode & 4:
+        assert not n_out.cpu()[~valid].any()

@@ -25,7 +25,6 @@ from oracle import OfficialConfig, official_input, official_state_dict, transfor
 from oracle.weights import per_row_input, state_to_numpy
 from solution import _native
 from solution.config import ConfigSpec, RuntimeBackend, default_program, default_schedule, portable_streamed_config
-from solution.plan_builder import ConfigRejectedError
 from solution.transformer import UserOptimizedTransformer, copy_model_weights
 
 pytestmark = pytest.mark.gpu
@@ -90,12 +89,39 @@ def test_matches_reference_golden(name: str) -> None:
     _gate(y, golden["output"])
 
 
-def test_padding_mask_is_rejected_not_ignored() -> None:
+def test_padding_mask_matches_reference_golden() -> None:
+    """The reference's own output with 30 % padding (masked keys, zeroed rows)."""
+
     golden = load_golden("masked")
     cfg = _golden_config(golden)
     model = _model(cfg)
-    with pytest.raises(ConfigRejectedError):
-        _run(model, torch.from_numpy(golden["input"]), torch.from_numpy(golden["mask"]))
+    mask = torch.from_numpy(golden["mask"])
+    assert not bool(mask.all())
+    y = _run(model, torch.from_numpy(golden["input"]), mask)
+    _gate(y, golden["output"])
+    assert not y.cpu()[~mask].any(), "padding rows must be exactly zero"
+
+
+def test_padding_mask_against_oracle_and_runtimes() -> None:
+    """Left-, right- and scatter-padded rows at a multi-tile length; eager and
+    CUDA-graph runtimes give the same bits."""
+
+    cfg = OfficialConfig(3, 700, 256, 4, 1024, 2)
+    x = official_input(cfg, 11)
+    mask = torch.ones(3, 700, dtype=torch.bool)
+    mask[0, :150] = False  # left padding: early queries see no valid key
+    mask[1, 500:] = False  # right padding
+    mask[2, ::3] = False  # scattered
+    state = state_to_numpy(official_state_dict(cfg, seed=0))
+    with np.errstate(invalid="ignore"):
+        ref = transformer_forward(
+            x.numpy(), state, num_heads=4, num_layers=2, causal=True, valid_token_mask=mask.numpy()
+        )
+    eager = _run(_model(cfg), x, mask)
+    _gate(eager, ref)
+    graph = _model(cfg, ConfigSpec(program=default_program(), schedule=default_schedule(RuntimeBackend.CUDA_GRAPH)))
+    assert torch.equal(_run(graph, x, mask), eager)
+    assert torch.equal(_run(graph, x, mask), eager)
 
 
 def test_bf16_input_gives_bf16_output() -> None:
