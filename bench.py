@@ -331,7 +331,9 @@ def run_gpu(args: argparse.Namespace) -> None:
         model.kernel_events = None
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         kernel_ms = recorder.durations_ms()
-
+        # Peak device memory of the forward itself (the host pipeline below
+        # adds its own input slots).
+    
         # End to end through the public host-batch API (HostPipeline) from
         # pinned host memory: every step copies its input H2D, runs the
         # forward and copies the whole output D2H; the three run on separate
@@ -371,40 +373,45 @@ def run_gpu(args: argparse.Namespace) -> None:
     s, d, f, layers = cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
     m = b_loc * s
     heads_frac = 1.0 / world if parallel == "heads" else 1.0
-    flops_per_launch = {
-        "attention": 2.0 * b_loc * s * s * d * heads_frac,  # causal, counted as 2BS^2D like the reference
-        "qkv_projection": 2.0 * m * 3 * d * d * heads_frac,
-        "attention_output_projection": 2.0 * m * d * d * heads_frac,
-        "ffn_input_projection": 2.0 * m * f * d * heads_frac,
-        "ffn_output_projection": 2.0 * m * d * f * heads_frac,
+    # Algorithmic work of one step per kernel role (the streamed runtime
+    # splits it over several launches per layer, so work and time are both
+    # taken per step): FLOPs for the tensor-core kernels (causal attention
+    # counted as 2BS^2D like the reference), HBM bytes for the norms.
+    flops_per_step = {
+        "attention": layers * 2.0 * b_loc * s * s * d * heads_frac,
+        "qkv_projection": layers * 2.0 * m * 3 * d * d * heads_frac,
+        "attention_output_projection": layers * 2.0 * m * d * d * heads_frac,
+        "ffn_input_projection": layers * 2.0 * m * f * d * heads_frac,
+        "ffn_output_projection": layers * 2.0 * m * d * f * heads_frac,
     }
-    bytes_per_launch = {"residual_norm": 12.0 * m * d, "initial_norm": 6.0 * m * d}
+    bytes_per_step = {"residual_norm": 2 * layers * 12.0 * m * d, "initial_norm": 6.0 * m * d}
     per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
     launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
     roofline = None
     if per_role:
         dominant = max(per_role, key=per_role.get)
         peaks, peak_source = _peaks()
-        avg_launch_ms = per_role[dominant] / max(1, launches[dominant])
-        if dominant in flops_per_launch:
-            achieved = flops_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e12
+        role_s = per_role[dominant] / 1000.0
+        n_launch = max(1, launches[dominant])
+        if dominant in flops_per_step:
+            achieved = flops_per_step[dominant] / role_s / 1e12
             peak = float(peaks["bf16_tflops_sustained"])
             roofline = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dominant,
-                        "algorithmic_per_launch": flops_per_launch[dominant]}
+                        "algorithmic_per_launch": flops_per_step[dominant] / n_launch}
         else:
-            achieved = bytes_per_launch[dominant] / (avg_launch_ms / 1000.0) / 1e9
+            achieved = bytes_per_step[dominant] / role_s / 1e9
             peak = float(peaks["hbm_gbs"])
             roofline = {"bound": "hbm", "unit": "GB/s", "kernel": dominant,
-                        "algorithmic_per_launch": bytes_per_launch[dominant]}
+                        "algorithmic_per_launch": bytes_per_step[dominant] / n_launch}
         roofline.update(
             achieved=achieved,
             peak=peak,
             peak_source=f"{peak_source} ({'bf16_tflops_sustained' if roofline['bound'] == 'tensor' else 'hbm_gbs'})",
             frac=achieved / peak,
             traffic=_profile_traffic(dominant) if args.workload == "c2" else None,
-            avg_launch_ms=avg_launch_ms,
+            avg_launch_ms=per_role[dominant] / n_launch,
         )
-    attention_ms = per_role.get("attention", 0.0) / max(1, launches.get("attention", 1))
+    attention_s = per_role.get("attention", 0.0) / 1000.0
     kernel_table = {
         role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]} for role in sorted(per_role)
     }
@@ -438,7 +445,7 @@ def run_gpu(args: argparse.Namespace) -> None:
                 "l2": "inputs larger than L2" if big_input else "flushed (256 MB write) before every timed step",
                 "runtime": model.active_config.schedule.runtime.value,
             },
-            "attention_tflops": flops_per_launch["attention"] / (attention_ms / 1000.0) / 1e12 if attention_ms else None,
+            "attention_tflops": flops_per_step["attention"] / attention_s / 1e12 if attention_s else None,
             "model_tflops": model_flops / (ms_per_step / 1000.0) / 1e12,
             "peak_memory_gb_per_gpu": peak_gb_max,
             "kernels": kernel_table,
