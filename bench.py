@@ -506,14 +506,15 @@ def run_kernel(args: argparse.Namespace) -> None:
         }[args.kernel]
         launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
         work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
-    elif args.kernel in gemm:
-        k, n, gelu = gemm[args.kernel]
+    elif args.kernel.removesuffix("_pair") in gemm:
+        k, n, gelu = gemm[args.kernel.removesuffix("_pair")]
+        variant = _native.GEMM_PAIR if args.kernel.endswith("_pair") else _native.GEMM_1SM
         a = randn(m, k)
         w = randn(n, k, scale=k**-0.5)
         bias = randn(n, dtype=torch.float32)
         out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
         epi = _native.EPI_BIAS_GELU if gelu else _native.EPI_BIAS
-        launch = lambda: _native.linear(a, w, bias, out, epi)  # noqa: E731
+        launch = lambda: _native.linear(a, w, bias, out, epi, variant)  # noqa: E731
         work, unit, bound = 2.0 * m * n * k, "TFLOP/s", "tensor"
     elif args.kernel == "residual_norm":
         resid = randn(m, d, dtype=torch.float32)
@@ -576,6 +577,10 @@ def main() -> None:
             "out_proj",
             "ffn_in",
             "ffn_out",
+            "qkv_pair",
+            "out_proj_pair",
+            "ffn_in_pair",
+            "ffn_out_pair",
             "residual_norm",
         ),
         default=None,

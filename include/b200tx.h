@@ -39,6 +39,10 @@ extern "C" {
 #define B200TX_EPI_BIAS 0
 #define B200TX_EPI_BIAS_GELU 1
 
+/* GEMM kernel variants (b200tx_linear_ex). */
+#define B200TX_GEMM_1SM 0  /* one CTA per SM, 128x256 tiles, 4-stage 48 KB ring */
+#define B200TX_GEMM_PAIR 1 /* CTA pairs (cta_group::2), 256x256 tiles, 6-stage 32 KB ring */
+
 /* Attention kernel variants (b200tx_attention_ex). */
 #define B200TX_ATTN_PAIRED 0 /* two 128-row query tiles per CTA, P kept in TMEM */
 #define B200TX_ATTN_SINGLE 1 /* one 128-row query tile per CTA, P through shared memory */
@@ -121,6 +125,18 @@ int b200tx_residual_layer_norm_masked(const void* residual_in, int in_dtype, con
  */
 int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
                   int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream);
+
+/*
+ * b200tx_linear with an explicit kernel variant (B200TX_GEMM_PAIR, the variant
+ * of b200tx_linear, or B200TX_GEMM_1SM).  Both compute the same function; the
+ * execution plan's GEMM launch records pick one per projection.  Replaces the
+ * same reference operators as b200tx_linear; the variant is the sm100
+ * counterpart of the reference's GEMM launch parameters
+ * (TritonGemmParams, solution/config.py:279-325).
+ */
+int b200tx_linear_ex(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                     int64_t M, int64_t N, int64_t K, int epilogue, int variant,
+                     cudaStream_t stream);
 
 /*
  * Causal (or full) multi-head attention over the packed projection output.

@@ -46,7 +46,7 @@ struct DeviceState {
   int sm_count = 0;
   int cc_major = 0;
   int cc_minor = 0;
-  bool gemm_attr[4] = {false, false, false, false};
+  bool gemm_attr[8] = {false, false, false, false, false, false, false, false};
   bool attn_attr[4] = {false, false, false, false};  // variants 0-2, masked quad
 };
 
@@ -287,8 +287,14 @@ int b200tx_residual_layer_norm_masked(const void* residual_in, int in_dtype, con
                                   stream);
 }
 
-int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
-                  int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int linear_impl(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                int64_t M, int64_t N, int64_t K, int epilogue, int variant, cudaStream_t stream) {
+  if (variant != B200TX_GEMM_1SM && variant != B200TX_GEMM_PAIR)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: variant %d", variant);
   if (a == nullptr || w == nullptr || out == nullptr)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: null tensor pointer");
   if (M <= 0 || N <= 0 || K <= 0 || M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
@@ -308,18 +314,22 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
   int rc = current_device(&dev);
   if (rc != B200TX_OK) return rc;
 
+  const bool paired = variant == B200TX_GEMM_PAIR;
+  const int tile_m = paired ? b200tx::kGemm2BM : b200tx::kGemmBM;
+  const int tile_n = paired ? b200tx::kGemm2BN : b200tx::kGemmBN;
   CUtensorMap map_a, map_w;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {b200tx::kGemmBK, b200tx::kGemmBM};
+    const uint32_t box[2] = {b200tx::kGemmBK, 128u};  // 128 A rows per CTA in both variants
     rc = encode_bf16_map(&map_a, a, 2, dims, strides, box);
     if (rc != B200TX_OK) return rc;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {b200tx::kGemmBK, b200tx::kGemmBN};
+    // W rows per CTA: the whole 256-row block, or one CTA's half of it.
+    const uint32_t box[2] = {b200tx::kGemmBK, paired ? 128u : static_cast<uint32_t>(b200tx::kGemmBN)};
     rc = encode_bf16_map(&map_w, w, 2, dims, strides, box);
     if (rc != B200TX_OK) return rc;
   }
@@ -329,34 +339,57 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
   args.M = static_cast<int>(M);
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
-  args.num_m_tiles = static_cast<int>((M + b200tx::kGemmBM - 1) / b200tx::kGemmBM);
-  args.num_n_tiles = static_cast<int>((N + b200tx::kGemmBN - 1) / b200tx::kGemmBN);
+  args.num_m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
+  args.num_n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   const int64_t tiles = static_cast<int64_t>(args.num_m_tiles) * args.num_n_tiles;
   if (tiles > 0x7fffffffLL) return fail(B200TX_ERR_UNSUPPORTED, "linear: too many tiles");
-  const unsigned grid = static_cast<unsigned>(tiles < dev->sm_count ? tiles : dev->sm_count);
+  // Persistent grid: one CTA per SM, or one CTA pair per two SMs.
+  const int64_t slots = paired ? dev->sm_count / 2 : dev->sm_count;
+  const unsigned grid =
+      static_cast<unsigned>((tiles < slots ? tiles : slots) * (paired ? 2 : 1));
 
   using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::GemmArgs);
   KernelFn kernel;
-  const int variant = epilogue * 2 + (out_dtype == B200TX_F32 ? 1 : 0);
-  switch (variant) {
+  const int instance = (paired ? 4 : 0) + epilogue * 2 + (out_dtype == B200TX_F32 ? 1 : 0);
+  switch (instance) {
     case 0: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
     case 1: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, float>; break;
     case 2: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
-    default: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, float>; break;
+    case 3: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, float>; break;
+    case 4: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
+    case 5: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, float>; break;
+    case 6: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
+    default: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, float>; break;
   }
+  const size_t smem = paired ? b200tx::kGemm2SmemBytes : b200tx::kGemmSmemBytes;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!dev->gemm_attr[variant]) {
+    if (!dev->gemm_attr[instance]) {
       cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(b200tx::kGemmSmemBytes));
+                                             static_cast<int>(smem));
       if (err != cudaSuccess) return cuda_fail(err, "linear: cudaFuncSetAttribute");
-      dev->gemm_attr[variant] = true;
+      dev->gemm_attr[instance] = true;
     }
   }
-  kernel<<<grid, b200tx::kGemmThreads, b200tx::kGemmSmemBytes, stream>>>(map_a, map_w, args);
+  kernel<<<grid, b200tx::kGemmThreads, smem, stream>>>(map_a, map_w, args);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(err, "linear launch");
   return B200TX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200tx_linear(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                  int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
+  return linear_impl(a, w, bias, out, out_dtype, M, N, K, epilogue, B200TX_GEMM_PAIR, stream);
+}
+
+int b200tx_linear_ex(const void* a, const void* w, const float* bias, void* out, int out_dtype,
+                     int64_t M, int64_t N, int64_t K, int epilogue, int variant,
+                     cudaStream_t stream) {
+  return linear_impl(a, w, bias, out, out_dtype, M, N, K, epilogue, variant, stream);
 }
 
 }  // extern "C"

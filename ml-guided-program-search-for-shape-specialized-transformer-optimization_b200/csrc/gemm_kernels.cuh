@@ -285,4 +285,251 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant: clusters of two CTAs (one per SM) share 256x256 output
+// tiles through the tcgen05 .cta_group::2 MMA.  CTA r of the pair loads rows
+// 128r..128r+127 of the tile's A block and rows 128r..128r+127 of its 256-row
+// W block, 32 KB per stage, so a 6-stage ring fits where the single-CTA kernel
+// holds 4 stages of 48 KB, and every SM streams a third less operand data per
+// FLOP out of L2.  The leader (rank 0) issues 256x256x16 UMMAs that read both
+// CTAs' shared memory and write both CTAs' TMEM (each CTA keeps its 128 rows
+// x 256 fp32 columns, double-buffered in its 512 columns).
+//   warp 0      TMA producer in each CTA; all loads of a stage complete on
+//               the leader's full barrier: the leader arms it with the bytes
+//               of both CTAs (its one arrival) and loads with a plain TMA,
+//               the peer's .cta_group::2 TMA loads report their bytes to it
+//               (no remote arrival, which would serialise the peer's loop)
+//   warp 1      leader only: one elected thread issues the UMMAs; commits are
+//               multicast to both CTAs (stage free, accumulator ready)
+//   warps 2..9  epilogue in each CTA as in the single-CTA kernel; each warp
+//               releases an accumulator on the leader's barrier (16 arrivals)
+// Both CTAs walk the same pair-tile sequence.  A cluster barrier orders the
+// barrier initialisation before any remote use and keeps both CTAs (their
+// shared memory and TMEM) alive until the pair has finished.
+// ---------------------------------------------------------------------------
+constexpr int kGemm2BM = 256;  // rows per pair tile (128 per CTA)
+constexpr int kGemm2BN = 256;  // columns per pair tile (W rows: 128 per CTA)
+constexpr int kGemm2Stages = 6;
+constexpr uint32_t kGemm2TileABytes = 128 * kGemmBK * 2;  // 16 KB
+constexpr uint32_t kGemm2TileBBytes = 128 * kGemmBK * 2;  // 16 KB
+constexpr uint32_t kGemm2StageBytes = kGemm2TileABytes + kGemm2TileBBytes;
+constexpr size_t kGemm2SmemBytes = 1024 + kGemm2Stages * kGemm2StageBytes;  // 193 KB
+
+template <int EPI, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tn_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                             const __grid_constant__ CUtensorMap tmap_w, GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full_bar[kGemm2Stages];
+  __shared__ uint64_t empty_bar[kGemm2Stages];
+  __shared__ uint64_t acc_full_bar[2];
+  __shared__ uint64_t acc_empty_bar[2];
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+  __shared__ float bias_tile[8][kGemm2BN / 2];
+
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* smem_a = smem;
+  uint8_t* smem_w = smem + kGemm2Stages * kGemm2TileABytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+  const int num_tiles = args.num_m_tiles * args.num_n_tiles;  // pair tiles (256 x 256)
+  const int num_kb = (args.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensor_map(&tmap_a);
+    prefetch_tensor_map(&tmap_w);
+    for (int s = 0; s < kGemm2Stages; ++s) {
+      mbar_init(&full_bar[s], 1);  // the leader's arrive.expect_tx
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full_bar[a], 1);
+      mbar_init(&acc_empty_bar[a], 16);  // 8 epilogue warps in each CTA
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_slot, kGemmTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      const uint32_t full_leader_base = peer_smem_addr(&full_bar[0], 0);
+      for (int tile = pair; tile < num_tiles && !abort_flag; tile += num_pairs) {
+        const int m_tile = tile / args.num_n_tiles;
+        const int n_tile = tile - m_tile * args.num_n_tiles;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, kErrGemmProducerWait, &abort_flag)) break;
+          const int a_row = m_tile * kGemm2BM + static_cast<int>(rank) * 128;
+          const int w_row = n_tile * kGemm2BN + static_cast<int>(rank) * 128;
+          if (leader) {
+            mbar_arrive_expect_tx(&full_bar[stage], 2 * kGemm2StageBytes);
+            tma_load_2d(smem_a + stage * kGemm2TileABytes, &tmap_a, &full_bar[stage], kb * kGemmBK, a_row);
+            tma_load_2d(smem_w + stage * kGemm2TileBBytes, &tmap_w, &full_bar[stage], kb * kGemmBK, w_row);
+          } else {
+            const uint32_t full_leader = full_leader_base + stage * static_cast<uint32_t>(sizeof(uint64_t));
+            tma_load_2d_pair(smem_a + stage * kGemm2TileABytes, &tmap_a, full_leader, kb * kGemmBK, a_row);
+            tma_load_2d_pair(smem_w + stage * kGemm2TileBBytes, &tmap_w, full_leader, kb * kGemmBK, w_row);
+          }
+          ++issued;
+          if (++stage == kGemm2Stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader waits for the pair's last loads (complete already on the
+      // normal path) so that no TMA write is in flight when the pair leaves.
+      if (leader) {
+        const int outstanding = issued < kGemm2Stages ? issued : kGemm2Stages;
+        for (int i = 0; i < outstanding; ++i) {
+          if (--stage < 0) {
+            stage = kGemm2Stages - 1;
+            phase ^= 1u;
+          }
+          volatile int no_abort = 0;
+          mbar_wait(&full_bar[stage], phase, kErrGemmProducerWait, &no_abort);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kGemm2BM, kGemm2BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool issued_any = false;
+      for (int tile = pair; tile < num_tiles && !abort_flag; tile += num_pairs, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        if (!mbar_wait(&acc_empty_bar[acc], acc_phase ^ 1u, kErrGemmMmaWait, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kGemm2BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, kErrGemmMmaWait, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * kGemm2TileABytes);
+          const uint32_t w_addr = smem_u32(smem_w + stage * kGemm2TileBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_bf16_ss_pair(d_tmem, sw128_desc(a_addr + k * 32, 16, 1024),
+                              sw128_desc(w_addr + k * 32, 16, 1024), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == kGemm2Stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full_bar[acc], 0x3);
+      }
+      if (issued_any) {
+        umma_commit_pair(&drain_bar, 0x1);
+        volatile int no_abort = 0;
+        mbar_wait(&drain_bar, 0, kErrGemmMmaWait, &no_abort);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
+    const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
+    const uint32_t acc_empty_leader0 = peer_smem_addr(&acc_empty_bar[0], 0);
+    const uint32_t acc_empty_leader1 = peer_smem_addr(&acc_empty_bar[1], 0);
+    int t = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
+      const int acc = t & 1;
+      const uint32_t acc_phase = (t >> 1) & 1;
+      const int m_tile = tile / args.num_n_tiles;
+      const int n_tile = tile - m_tile * args.num_n_tiles;
+      float* warp_bias = bias_tile[warp - 2];
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int col = n_tile * kGemm2BN + col_half * (kGemm2BN / 2) + i * 32 + lane;
+        warp_bias[i * 32 + lane] = (args.bias != nullptr && col < args.N) ? __ldg(args.bias + col) : 0.f;
+      }
+      __syncwarp();
+      bool ok = mbar_wait(&acc_full_bar[acc], acc_phase, kErrGemmEpilogueWait, &abort_flag);
+      if (__any_sync(0xffffffffu, !ok)) break;
+      __syncwarp();
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(m_tile) * kGemm2BM + row_in_tile;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             acc * kGemm2BN + col_half * (kGemm2BN / 2);
+      constexpr int kChunks = kGemm2BN / 2 / 32;
+      uint32_t buf[2][32];
+      tmem_ld_32cols(taddr, buf[0]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        if (c + 1 < kChunks) tmem_ld_32cols(taddr + (c + 1) * 32, buf[(c + 1) & 1]);
+        const uint32_t (&r)[32] = buf[c & 1];
+        const int col0 = n_tile * kGemm2BN + col_half * (kGemm2BN / 2) + c * 32;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + warp_bias[c * 32 + i];
+        if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+        if (row < args.M) {
+          OutT* out_row = static_cast<OutT*>(args.out) + row * args.N + col0;
+          if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (col0 + i < args.N)
+                st_global_v4(out_row + i, pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              if (col0 + i < args.N)
+                st_global_v4(out_row + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]),
+                             __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3]));
+            }
+          }
+        }
+        if (c + 1 < kChunks) tmem_wait_ld();
+      }
+      // This warp has read its columns of the accumulator: one arrival on the
+      // leader's barrier (remote for the peer CTA).
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kGemmTmemCols);
+  }
+}
+
 }  // namespace b200tx

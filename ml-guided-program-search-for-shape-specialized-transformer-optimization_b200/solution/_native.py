@@ -21,6 +21,8 @@ F32 = 0
 BF16 = 1
 EPI_BIAS = 0
 EPI_BIAS_GELU = 1
+GEMM_1SM = 0
+GEMM_PAIR = 1
 ATTN_PAIRED = 0
 ATTN_SINGLE = 1
 ATTN_QUAD = 2
@@ -94,6 +96,20 @@ def _declare(lib: ctypes.CDLL) -> None:
         _c_int64,  # N
         _c_int64,  # K
         ctypes.c_int,  # epilogue
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_linear_ex.restype = ctypes.c_int
+    lib.b200tx_linear_ex.argtypes = [
+        _c_void_p,  # a
+        _c_void_p,  # w
+        _c_void_p,  # bias
+        _c_void_p,  # out
+        ctypes.c_int,  # out_dtype
+        _c_int64,  # M
+        _c_int64,  # N
+        _c_int64,  # K
+        ctypes.c_int,  # epilogue
+        ctypes.c_int,  # variant
         _c_void_p,  # stream
     ]
     lib.b200tx_attention.restype = ctypes.c_int
@@ -271,15 +287,17 @@ def linear(
     bias: torch.Tensor | None,
     out: torch.Tensor,
     epilogue: int,
+    variant: int = GEMM_PAIR,
 ) -> None:
-    """Launch b200tx_linear: out = epilogue(a . w^T + bias)."""
+    """Launch b200tx_linear_ex: out = epilogue(a . w^T + bias) with the given
+    kernel variant (GEMM_1SM or GEMM_PAIR)."""
 
     k = a.shape[-1]
     m = a.numel() // k
     n = w.shape[0]
     lib = load()
     _check(
-        lib.b200tx_linear(
+        lib.b200tx_linear_ex(
             a.data_ptr(),
             w.data_ptr(),
             None if bias is None else bias.data_ptr(),
@@ -289,9 +307,10 @@ def linear(
             n,
             k,
             int(epilogue),
+            int(variant),
             _stream(a.device),
         ),
-        "b200tx_linear",
+        "b200tx_linear_ex",
     )
 
 
@@ -336,6 +355,8 @@ __all__ = [
     "EPI_BIAS",
     "EPI_BIAS_GELU",
     "F32",
+    "GEMM_1SM",
+    "GEMM_PAIR",
     "MASK_DROP_UPDATE",
     "MASK_ZERO_NORMED",
     "MASK_ZERO_RESIDUAL",

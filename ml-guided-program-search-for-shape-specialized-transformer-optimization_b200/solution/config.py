@@ -148,7 +148,11 @@ def _exact_fields(value: dict[str, Any], expected: frozenset[str], *, field: str
 # Kernel variants compiled into libb200tx.  Launch parameters outside these
 # sets are rejected by the dataclasses, so a search never proposes a variant
 # that does not exist.
-SM100_GEMM_VARIANTS = frozenset({(128, 256, 64, 4)})
+# (tile_m, tile_n, tile_k, stages) -> libb200tx GEMM variant:
+#   (128, 256, 64, 4): one CTA per SM (B200TX_GEMM_1SM)
+#   (256, 256, 64, 6): CTA pairs sharing each tile through cta_group::2 (B200TX_GEMM_PAIR)
+SM100_GEMM_VARIANT_CODES = {(128, 256, 64, 4): 0, (256, 256, 64, 6): 1}
+SM100_GEMM_VARIANTS = frozenset(SM100_GEMM_VARIANT_CODES)
 # (block_m, block_n, kv_stages) -> libb200tx attention variant:
 #   (256, 128, 3): two 128-row query tiles per CTA, P kept in TMEM (B200TX_ATTN_PAIRED)
 #   (128, 128, 3): one query tile per CTA, P staged through shared memory (B200TX_ATTN_SINGLE)
@@ -161,10 +165,10 @@ SM100_NORM_ROWS_PER_CTA = frozenset({8})
 class Sm100GemmParams:
     """Tile shape of the tcgen05 GEMM (csrc/gemm_kernels.cuh)."""
 
-    tile_m: int = 128
+    tile_m: int = 256
     tile_n: int = 256
     tile_k: int = 64
-    stages: int = 4
+    stages: int = 6
 
     _FIELDS: ClassVar[frozenset[str]] = frozenset({"tile_m", "tile_n", "tile_k", "stages"})
 
@@ -174,6 +178,12 @@ class Sm100GemmParams:
         key = (self.tile_m, self.tile_n, self.tile_k, self.stages)
         if key not in SM100_GEMM_VARIANTS:
             raise ValueError(f"no sm100 GEMM variant is built for tile {key}")
+
+    @property
+    def kernel_variant(self) -> int:
+        """The libb200tx GEMM variant code (B200TX_GEMM_1SM / _PAIR)."""
+
+        return SM100_GEMM_VARIANT_CODES[(self.tile_m, self.tile_n, self.tile_k, self.stages)]
 
     def to_dict(self) -> dict[str, int]:
         return {

@@ -67,8 +67,11 @@ def sm100_linear(
     gelu: bool = False,
     out_dtype: torch.dtype = torch.bfloat16,
     out: torch.Tensor | None = None,
+    variant: int = _native.GEMM_PAIR,
 ) -> tuple[torch.Tensor, str]:
-    """``[..., K] x [N, K]^T -> [..., N]`` on the tensor cores."""
+    """``[..., K] x [N, K]^T -> [..., N]`` on the tensor cores; ``variant``
+    picks the built kernel (``GEMM_1SM`` 128x256 tiles per SM, ``GEMM_PAIR``
+    256x256 tiles per CTA pair)."""
 
     if not can_use_sm100_linear(value, weight, bias):
         raise RuntimeError("sm100 linear is ineligible for the requested operands")
@@ -87,6 +90,7 @@ def sm100_linear(
         bias,
         result,
         _native.EPI_BIAS_GELU if gelu else _native.EPI_BIAS,
+        variant,
     )
     return result, SM100_LINEAR_GELU_BACKEND if gelu else SM100_LINEAR_BACKEND
 

@@ -549,6 +549,14 @@ class UserOptimizedTransformer(nn.Module):
             plan.attention_launch.kernel_variant if plan.attention_launch is not None else 0
         )
 
+        def gemm_variant(launch: Any) -> int:
+            return launch.kernel_variant if launch is not None else 1  # the CTA-pair GEMM
+
+        qkv_variant = gemm_variant(plan.qkv_launch)
+        out_proj_variant = gemm_variant(plan.attention_output_projection_launch)
+        ffn_in_variant = gemm_variant(plan.ffn_input_launch)
+        ffn_out_variant = gemm_variant(plan.ffn_launch)
+
         flat_in = value.reshape(rows, d_model)
         output = torch.empty((batch, seq, d_model), dtype=value.dtype, device=device)
         # Padding mask (official/torch_transformer_benchmark.py:105-121,
@@ -615,7 +623,7 @@ class UserOptimizedTransformer(nn.Module):
             attention = layer.attention
             w_qkv, b_qkv = attention.qkv_proj.shadow_parameters()
             token = rec.start("qkv_projection")
-            _, marker = sm100_linear(normalized, w_qkv, b_qkv, out=qkv_flat)
+            _, marker = sm100_linear(normalized, w_qkv, b_qkv, out=qkv_flat, variant=qkv_variant)
             rec.stop(token)
             _strict_backend_marker(
                 marker,
@@ -634,7 +642,9 @@ class UserOptimizedTransformer(nn.Module):
             )
             w_o, b_o = attention.out_proj.shadow_parameters()
             token = rec.start("attention_output_projection")
-            _, marker = sm100_linear(context_flat, w_o, b_o, out_dtype=out_update, out=attn_update)
+            _, marker = sm100_linear(
+                context_flat, w_o, b_o, out_dtype=out_update, out=attn_update, variant=out_proj_variant
+            )
             rec.stop(token)
             _strict_backend_marker(
                 marker,
@@ -661,7 +671,7 @@ class UserOptimizedTransformer(nn.Module):
             residual_source = residual
             w_1, b_1 = layer.ffn_in.shadow_parameters()
             token = rec.start("ffn_input_projection")
-            _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden)
+            _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden, variant=ffn_in_variant)
             rec.stop(token)
             _strict_backend_marker(
                 marker,
@@ -670,7 +680,7 @@ class UserOptimizedTransformer(nn.Module):
             )
             w_2, b_2 = layer.ffn_out.shadow_parameters()
             token = rec.start("ffn_output_projection")
-            _, marker = sm100_linear(hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out)
+            _, marker = sm100_linear(hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out, variant=ffn_out_variant)
             rec.stop(token)
             _strict_backend_marker(
                 marker,

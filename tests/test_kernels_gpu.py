@@ -112,9 +112,12 @@ def test_initial_layer_norm(dtype: torch.dtype) -> None:
         (1000, 3072, 1024, False, torch.bfloat16, True),
         (4097, 1024, 4096, False, torch.float32, True),
         (300, 2304, 768, True, torch.bfloat16, True),
+        (257, 392, 136, False, torch.bfloat16, True),  # pair tiles: ragged M and N halves
+        (16384, 1024, 1024, False, torch.bfloat16, True),  # C2 out-projection shape
     ],
 )
-def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias: bool) -> None:
+@pytest.mark.parametrize("variant", [_native.GEMM_1SM, _native.GEMM_PAIR])
+def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias: bool, variant: int) -> None:
     g = torch.Generator().manual_seed(m + 7 * n + 13 * k)
     a = torch.randn(m, k, generator=g).to(torch.bfloat16)
     w = (torch.randn(n, k, generator=g) / k**0.5).to(torch.bfloat16)
@@ -126,7 +129,8 @@ def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias
         ref = gelu_erf(ref.astype(np.float32))
     with torch.inference_mode():
         out, marker = sm100_linear(
-            a.to(DEV), w.to(DEV), None if b is None else b.to(DEV), gelu=gelu, out_dtype=out_dtype
+            a.to(DEV), w.to(DEV), None if b is None else b.to(DEV), gelu=gelu, out_dtype=out_dtype,
+            variant=variant,
         )
     torch.cuda.synchronize()
     assert marker == ("sm100_linear_gelu" if gelu else "sm100_linear")
@@ -135,6 +139,22 @@ def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias
         assert rel < 1e-5, rel
     else:
         assert rel < 4e-3, rel
+
+
+def test_linear_variants_agree_bitwise() -> None:
+    """Both GEMM variants accumulate each output in the same K order: equal bits."""
+
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(2000, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(3072, 1024, generator=g) / 32).to(torch.bfloat16).to(DEV)
+    b = torch.randn(3072, generator=g).to(DEV)
+    with torch.inference_mode():
+        one, _ = sm100_linear(a, w, b, gelu=True, variant=_native.GEMM_1SM)
+        two, _ = sm100_linear(a, w, b, gelu=True, variant=_native.GEMM_PAIR)
+        again, _ = sm100_linear(a, w, b, gelu=True, variant=_native.GEMM_PAIR)
+    assert torch.equal(two, again)
+    max_abs, rel = parity_errors(_bf16_np(one), _bf16_np(two))
+    assert rel < 1e-3, rel
 
 
 def test_linear_three_dimensional_input() -> None:
