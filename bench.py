@@ -248,6 +248,18 @@ def build_model(device: torch.device, spec: dict | None = None):
     return model.to(device).eval()
 
 
+def _c4_tp(args: argparse.Namespace, batch: int, world: int) -> int:
+    """Tensor-parallel group size of the head-sharded C4 run: --tp, else the
+    smallest head sharding (2) that, with data-parallel replicas over the
+    batch rows, covers all ranks (B=4: tp2 on 2, dp2 x tp2 on 4, dp4 x tp2 on 8
+    GPUs; measured fastest on 8 GPUs, where tp8 all-reduces 4x the bytes)."""
+
+    if args.tp:
+        return args.tp
+    tp = max(2, world // batch)
+    return tp if world % tp == 0 else world
+
+
 def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, world: int):
     """This rank's input rows and the parallel mode of the workload."""
 
@@ -257,8 +269,12 @@ def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, 
 
     cfg = OfficialConfig(**spec)
     if args.workload == "c4" and world > 1:
-        # Head-sharded tensor parallel: every rank holds the whole batch.
-        return official_input(cfg, seed), "heads", "strong", cfg.batch_size * cfg.seq_len
+        # Head-sharded tensor parallel over groups of --tp ranks; the
+        # world // tp replicas split the batch rows between them.
+        tp = _c4_tp(args, cfg.batch_size, world)
+        start, stop = batch_shard_bounds(cfg.batch_size, rank // tp, world // tp)
+        x = official_input(cfg, seed)[start:stop].contiguous()
+        return x, "heads", "strong", cfg.batch_size * cfg.seq_len
     if args.workload == "c5":
         # Batch-sharded capacity run: the 32 rows (seed 4 + row) split over ranks.
         start, stop = batch_shard_bounds(cfg.batch_size, rank, world)
@@ -296,7 +312,16 @@ def run_gpu(args: argparse.Namespace) -> None:
     cfg = OfficialConfig(**spec)
     model = build_model(device, spec)
     x_cpu, parallel, scaling, total_tokens = _workload_input(args, spec, seed, rank, world)
-    runner = TensorParallelTransformer(model) if parallel == "heads" else model
+    tp = 1
+    if parallel == "heads":
+        from solution.runtimes.sharded import tensor_parallel_groups
+
+        tp = _c4_tp(args, cfg.batch_size, world)
+        group, _, _ = tensor_parallel_groups(tp)
+        partials = torch.bfloat16 if args.tp_partials == "bf16" else torch.float32
+        runner = TensorParallelTransformer(model, group=group, partial_dtype=partials)
+    else:
+        runner = model
     x_host = x_cpu.pin_memory()
     del x_cpu
     x_dev = x_host.to(device)
@@ -372,7 +397,7 @@ def run_gpu(args: argparse.Namespace) -> None:
     b_loc = x_dev.shape[0]
     s, d, f, layers = cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
     m = b_loc * s
-    heads_frac = 1.0 / world if parallel == "heads" else 1.0
+    heads_frac = 1.0 / tp
     # Algorithmic work of one step per kernel role (the streamed runtime
     # splits it over several launches per layer, so work and time are both
     # taken per step): FLOPs for the tensor-core kernels (causal attention
@@ -437,7 +462,9 @@ def run_gpu(args: argparse.Namespace) -> None:
                 "global_batch": cfg.batch_size * (world if scaling == "weak" else 1),
                 "seq_len": cfg.seq_len,
                 "parallelism": (
-                    f"tp{world} (head-sharded, NCCL all-reduce after out-proj and FFN-down)"
+                    (f"dp{world // tp} x " if tp < world else "")
+                    + f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials"
+                    " after out-proj and FFN-down)"
                     if parallel == "heads"
                     else f"dp{world} (batch-sharded, no collective)"
                 ),
@@ -566,6 +593,10 @@ def main() -> None:
     parser.add_argument("--skip-cpu-baseline", action="store_true")
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default="c2",
                         help="BASELINE config to run (c2 is the bench line the driver records)")
+    parser.add_argument("--tp", type=int, default=0,
+                        help="c4 under torchrun: tensor-parallel group size (default: max(2, N / B))")
+    parser.add_argument("--tp-partials", choices=("fp32", "bf16"), default="bf16",
+                        help="dtype of the partial sums all-reduced by the head-sharded runtime")
     parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")
     parser.add_argument(
         "--kernel",

@@ -10,7 +10,9 @@ solution/shape14/executor.py:12-49; the reference itself is single-GPU):
   collective is needed on the data path.
 
 * Head-sharded tensor parallelism (`TensorParallelTransformer`), for batches
-  smaller than the GPU count (B=4 on 8 GPUs).  Rank r owns
+  smaller than the GPU count (B=4 on 8 GPUs), over the
+  whole world or over the tensor-parallel groups of `tensor_parallel_groups`
+  (data-parallel replicas of tp ranks, each taking its own batch rows).  Rank r owns
   heads [r H/W, (r+1) H/W) and FFN columns [r F/W, (r+1) F/W):
       qkv   = n . Wqkv_r^T + bqkv_r           local heads only (column parallel)
       ctx_r = attention(qkv)                  local heads
@@ -50,6 +52,29 @@ def batch_shard_bounds(batch: int, rank: int, world: int) -> tuple[int, int]:
     start = rank * base + min(rank, extra)
     stop = start + base + (1 if rank < extra else 0)
     return start, stop
+
+
+def tensor_parallel_groups(tp: int) -> tuple[object, int, int]:
+    """Split the world into data-parallel replicas of `tp` consecutive ranks.
+
+    Every rank must call this with the same `tp` (collective group creation).
+    Returns (this rank's tensor-parallel process group, its replica index,
+    the number of replicas).  With tp == world there is one replica over all
+    ranks; with tp == 1 every rank is its own replica.
+    """
+
+    import torch.distributed as dist
+
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    if isinstance(tp, bool) or not isinstance(tp, int) or tp <= 0 or world % tp:
+        raise ValueError(f"tensor-parallel size {tp} must divide the world size {world}")
+    mine = None
+    for first in range(0, world, tp):
+        group = dist.new_group(list(range(first, first + tp)))
+        if first <= rank < first + tp:
+            mine = group
+    return mine, rank // tp, world // tp
 
 
 @dataclass
@@ -236,4 +261,10 @@ class TensorParallelTransformer:
     __call__ = forward
 
 
-__all__ = ["LayerShard", "TensorParallelTransformer", "batch_shard_bounds", "shard_layer"]
+__all__ = [
+    "LayerShard",
+    "TensorParallelTransformer",
+    "batch_shard_bounds",
+    "shard_layer",
+    "tensor_parallel_groups",
+]

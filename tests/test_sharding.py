@@ -143,7 +143,7 @@ def test_tensor_parallel_composition_over_gloo() -> None:
     np.testing.assert_array_equal(outs[0], outs[1])
 
 
-def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+def _nccl_worker(rank: int, world: int, port: int, result_dir: str, partials: str = "fp32") -> None:
     import datetime
 
     from solution.runtimes.sharded import TensorParallelTransformer
@@ -159,7 +159,9 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
         model = UserOptimizedTransformer(SimpleNamespace(**cfg.__dict__))
         copy_model_weights(official_state_dict(cfg, seed=0), model)
         model = model.to(f"cuda:{rank}").eval()
-        tp = TensorParallelTransformer(model)
+        tp = TensorParallelTransformer(
+            model, partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32
+        )
         x = official_input(cfg, 5).to(f"cuda:{rank}")
         y_tp = tp(x)
         with torch.inference_mode():
@@ -173,15 +175,49 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str) -> None:
 
 
 @pytest.mark.gpu
-def test_tensor_parallel_matches_single_gpu() -> None:
+@pytest.mark.parametrize("partials", ["fp32", "bf16"])
+def test_tensor_parallel_matches_single_gpu(partials: str) -> None:
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_nccl_worker, args=(world, _free_port(), tmp), nprocs=world, start_method="spawn")
+        mp.start_processes(
+            _nccl_worker, args=(world, _free_port(), tmp, partials), nprocs=world, start_method="spawn"
+        )
         tp = [np.load(os.path.join(tmp, f"tp{r}.npy")) for r in range(world)]
         single = np.load(os.path.join(tmp, "single0.npy"))
     np.testing.assert_array_equal(tp[0], tp[1])
     diff = tp[0].astype(np.float64) - single
     assert np.abs(diff).max() < 2e-2
     assert np.linalg.norm(diff) / np.linalg.norm(single) < 5e-3
+
+
+def _groups_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    from solution.runtimes.sharded import tensor_parallel_groups
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        group, replica, replicas = tensor_parallel_groups(2)
+        value = torch.tensor([float(rank)])
+        dist.all_reduce(value, group=group)
+        bad = False
+        try:
+            tensor_parallel_groups(3)
+        except ValueError:
+            bad = True
+        np.save(os.path.join(result_dir, f"g{rank}.npy"), np.array([value.item(), replica, replicas, bad]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_groups_split_the_world_into_replicas() -> None:
+    world = 4
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_groups_worker, args=(world, _free_port(), tmp), nprocs=world, start_method="spawn")
+        got = [np.load(os.path.join(tmp, f"g{r}.npy")) for r in range(world)]
+    # ranks {0,1} and {2,3}: group sums 1 and 5; replicas 0,0,1,1 of 2
+    assert [g[0] for g in got] == [1.0, 1.0, 5.0, 5.0]
+    assert [g[1] for g in got] == [0, 0, 1, 1]
+    assert all(g[2] == 2 and g[3] == 1 for g in got)
