@@ -339,9 +339,8 @@ def run_gpu(args: argparse.Namespace) -> None:
             runner(x_dev)
         torch.cuda.synchronize()
 
-        recorder = KernelEventRecorder()
-        if runner is model:
-            model.kernel_events = recorder
+        # Timed steps: nothing but the forward between the step's two events,
+        # so consecutive kernels keep their programmatic launch overlap.
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier()
@@ -353,12 +352,25 @@ def run_gpu(args: argparse.Namespace) -> None:
                 runner(x_dev)
                 ends[i].record()
             barrier()
-        model.kernel_events = None
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-        kernel_ms = recorder.durations_ms()
         # Peak device memory of the forward itself (the host pipeline below
         # adds its own input slots).
-    
+        peak_gb = torch.cuda.max_memory_allocated(device) / 2**30
+
+        # Per-kernel times for the kernel table and the roofline: the same
+        # steps again with CUDA events around every launch (these events sit
+        # between kernels, so this pass is not the step time).
+        recorder = KernelEventRecorder()
+        if runner is model:
+            model.kernel_events = recorder
+        for _ in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            runner(x_dev)
+        torch.cuda.synchronize()
+        model.kernel_events = None
+        kernel_ms = recorder.durations_ms()
+
         # End to end through the public host-batch API (HostPipeline) from
         # pinned host memory: every step copies its input H2D, runs the
         # forward and copies the whole output D2H; the three run on separate
@@ -383,7 +395,6 @@ def run_gpu(args: argparse.Namespace) -> None:
         barrier()
         e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
         out_host = outs_host[0]
-    peak_gb = torch.cuda.max_memory_allocated(device) / 2**30
 
     total_ms = sum(step_ms)
     stats = torch.tensor([total_ms, e2e_ms, peak_gb], dtype=torch.float64, device=device)

@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -427,6 +429,8 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -771,6 +775,8 @@ __global__ void __launch_bounds__(kAttn4Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {

@@ -14,6 +14,7 @@
 #include <mutex>
 #include <string>
 #include <type_traits>
+#include <utility>
 
 #include "attention_kernels.cuh"
 #include "gemm_kernels.cuh"
@@ -124,14 +125,33 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Every kernel goes out with programmatic stream serialization (see
+// griddep_wait in sm100_common.cuh): the next launch of the stream may start
+// its set-up while this one drains.  Compile-time cluster dimensions of a
+// kernel are kept.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ------------------------------------------------------------------ norms
 template <int NV, typename InT, typename UpdT, typename OutT>
 cudaError_t launch_norm_vec(const b200tx::NormArgs& a, cudaStream_t stream) {
   const unsigned grid =
       static_cast<unsigned>((a.rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock);
-  b200tx::residual_layernorm_vec_kernel<NV, InT, UpdT, OutT>
-      <<<grid, b200tx::kNormWarpsPerBlock * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch(b200tx::residual_layernorm_vec_kernel<NV, InT, UpdT, OutT>, dim3(grid),
+                dim3(b200tx::kNormWarpsPerBlock * 32), 0, stream, a);
 }
 
 template <typename InT, typename UpdT, typename OutT>
@@ -152,9 +172,8 @@ cudaError_t launch_norm(const b200tx::NormArgs& a, bool vec_ok, cudaStream_t str
   }
   const unsigned grid =
       static_cast<unsigned>((a.rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock);
-  b200tx::residual_layernorm_generic_kernel<InT, UpdT, OutT>
-      <<<grid, b200tx::kNormWarpsPerBlock * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch(b200tx::residual_layernorm_generic_kernel<InT, UpdT, OutT>, dim3(grid),
+                dim3(b200tx::kNormWarpsPerBlock * 32), 0, stream, a);
 }
 
 template <typename InT, typename UpdT>
@@ -371,8 +390,7 @@ int linear_impl(const void* a, const void* w, const float* bias, void* out, int 
       dev->gemm_attr[instance] = true;
     }
   }
-  kernel<<<grid, b200tx::kGemmThreads, smem, stream>>>(map_a, map_w, args);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = launch(kernel, dim3(grid), dim3(b200tx::kGemmThreads), smem, stream, map_a, map_w, args);
   if (err != cudaSuccess) return cuda_fail(err, "linear launch");
   return B200TX_OK;
 }
@@ -470,9 +488,8 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
         dev->attn_attr[attr_slot] = true;
       }
     }
-    quad_kernel<<<static_cast<unsigned>(blocks), b200tx::kAttn4Threads, b200tx::kAttn4SmemBytes,
-                  stream>>>(map_qkv, map_kv, args);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch(quad_kernel, dim3(static_cast<unsigned>(blocks)), dim3(b200tx::kAttn4Threads),
+                             b200tx::kAttn4SmemBytes, stream, map_qkv, map_kv, args);
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
   }
@@ -490,8 +507,8 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
       dev->attn_attr[variant] = true;
     }
   }
-  kernel<<<static_cast<unsigned>(blocks), threads, smem, stream>>>(map_qkv, args);
-  cudaError_t err = cudaGetLastError();
+  cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), smem, stream,
+                           map_qkv, args);
   if (err != cudaSuccess) return cuda_fail(err, "attention launch");
   return B200TX_OK;
 }

@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -365,6 +367,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (elect_one()) {

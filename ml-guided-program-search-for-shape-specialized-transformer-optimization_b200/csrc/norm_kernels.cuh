@@ -130,6 +130,8 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
     residual_layernorm_vec_kernel(NormArgs args) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarpsPerBlock + (threadIdx.x >> 5);
+  griddep_wait();
+  griddep_launch_dependents();
   if (row >= args.rows) return;
   const int cols = 128 * NV;
   const int64_t base = row * cols;
@@ -198,6 +200,8 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
     residual_layernorm_generic_kernel(NormArgs args) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarpsPerBlock + (threadIdx.x >> 5);
+  griddep_wait();
+  griddep_launch_dependents();
   if (row >= args.rows) return;
   const int cols = args.cols;
   const int64_t base = row * cols;

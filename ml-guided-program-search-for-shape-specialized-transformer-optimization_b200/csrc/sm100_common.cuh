@@ -53,6 +53,21 @@ __device__ __forceinline__ bool device_error_raised() {
   return *reinterpret_cast<volatile unsigned int*>(&g_device_error) != 0u;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// Kernels of this library are launched with programmatic stream serialization:
+// the next kernel of the stream may be scheduled as soon as every CTA of the
+// running one has called griddep_launch_dependents(), so its launch and
+// set-up (barrier init, TMEM allocation, tensor-map prefetch) overlap this
+// kernel's tail.  griddep_wait() blocks until all preceding kernels of the
+// stream have completed and their memory is visible; every kernel calls it
+// after its set-up and before its first global-memory access.  Launched
+// without the attribute, both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
