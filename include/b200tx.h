@@ -178,6 +178,19 @@ int b200tx_attention_masked(const void* qkv, const uint8_t* key_valid, void* out
                             int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
                             int variant, cudaStream_t stream);
 
+/*
+ * Causal (or full) attention for head_dim 8, 16, 32, 64, 128 or 256 on the CUDA
+ * cores, with an optional key padding mask (key_valid [batch, seq] uint8 or
+ * NULL); same layouts and semantics as b200tx_attention_masked.  It covers the
+ * head dims the tensor-core kernels (head_dim 64) do not, e.g. the reference's
+ * official benchmark shapes (official/test_shapes.json: head dims 8, 32, 128,
+ * 256).  Replaces the same reference operators as b200tx_attention
+ * (solution/operators/attention/sdpa.py:76-170 for those shapes).
+ */
+int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                             int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                             cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

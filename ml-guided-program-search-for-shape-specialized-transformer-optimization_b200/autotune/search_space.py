@@ -8,7 +8,8 @@ the same surface -- ``SearchContext``, ``ParameterDomain``, ``StructureSpec``,
 its choices are the sm100 programs and the kernel variants compiled into
 libb200tx, so every candidate it yields is runnable on a B200:
 
-* structure (one branch each): precision plan x runtime schedule
+* structure (one branch each): attention backend (tensor-core flash kernels
+  or the CUDA-core kernel for other head dims) x precision plan x runtime
   (resident scope: eager, CUDA graph, batch-tiled CUDA graph; streamed scope:
   the streamed runtime, reference autotune/shape14_search_space.py:26-156);
 * parameters of a branch: the attention variant (``Sm100AttentionParams``
@@ -33,6 +34,7 @@ from typing import Any, Protocol, Union
 
 from solution.config import (
     SM100_ATTENTION_VARIANTS,
+    AttentionBackend,
     SM100_GEMM_VARIANTS,
     ConfigSpec,
     PrecisionPlan,
@@ -153,13 +155,19 @@ class StructureSpec:
 
     precision_plan: PrecisionPlan
     runtime: RuntimeBackend
+    attention: AttentionBackend = AttentionBackend.SM100_FLASH
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "precision_plan", PrecisionPlan(self.precision_plan))
         object.__setattr__(self, "runtime", RuntimeBackend(self.runtime))
+        object.__setattr__(self, "attention", AttentionBackend(self.attention))
 
     def to_dict(self) -> dict[str, str]:
-        return {"precision_plan": self.precision_plan.value, "runtime": self.runtime.value}
+        return {
+            "attention": self.attention.value,
+            "precision_plan": self.precision_plan.value,
+            "runtime": self.runtime.value,
+        }
 
     @property
     def branch_id(self) -> str:
@@ -167,13 +175,17 @@ class StructureSpec:
 
     @property
     def portable(self) -> bool:
-        """The eager bf16-core branch: the default program's own structure."""
+        """The eager bf16-core tensor-core branch: the default program's own structure."""
 
-        return self.precision_plan is PrecisionPlan.BF16_CORE and self.runtime is RuntimeBackend.EAGER
+        return (
+            self.precision_plan is PrecisionPlan.BF16_CORE
+            and self.runtime is RuntimeBackend.EAGER
+            and self.attention is AttentionBackend.SM100_FLASH
+        )
 
     @classmethod
     def from_config(cls, config: ConfigSpec) -> StructureSpec:
-        return cls(config.program.precision_plan, config.schedule.runtime)
+        return cls(config.program.precision_plan, config.schedule.runtime, config.program.attention)
 
 
 def _divisors(n: int, *, below: int | None = None) -> tuple[int, ...]:
@@ -182,7 +194,9 @@ def _divisors(n: int, *, below: int | None = None) -> tuple[int, ...]:
 
 
 def _domains_for_structure(structure: StructureSpec, context: SearchContext) -> tuple[ParameterDomain, ...]:
-    domains = [ParameterDomain("attention_tile", _ATTENTION_CHOICES, _DEFAULT_ATTENTION)]
+    domains = []
+    if structure.attention is AttentionBackend.SM100_FLASH:
+        domains.append(ParameterDomain("attention_tile", _ATTENTION_CHOICES, _DEFAULT_ATTENTION))
     domains += [ParameterDomain(name, _GEMM_CHOICES, _DEFAULT_GEMM) for name, _ in _GEMM_ROLES]
     batch = context.batch_size
     if structure.runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH:
@@ -200,11 +214,12 @@ def _domains_for_structure(structure: StructureSpec, context: SearchContext) -> 
 def _structure_specs(context: SearchContext) -> tuple[StructureSpec, ...]:
     runtimes = (RuntimeBackend.STREAMED,) if context.scope == "streamed" else _RESIDENT_RUNTIMES
     specs = []
-    for plan in PrecisionPlan:
-        for runtime in runtimes:
-            if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH and context.batch_size < 2:
-                continue
-            specs.append(StructureSpec(plan, runtime))
+    for attention in AttentionBackend:
+        for plan in PrecisionPlan:
+            for runtime in runtimes:
+                if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH and context.batch_size < 2:
+                    continue
+                specs.append(StructureSpec(plan, runtime, attention))
     return tuple(specs)
 
 
@@ -290,24 +305,30 @@ class BranchSpace:
             batch_tile_size=parameters.get("batch_tile_size") if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH else None,
             microbatch_size=parameters.get("microbatch_size") if runtime is RuntimeBackend.STREAMED else None,
             reuse_unchanged_input=bool(parameters.get("reuse_unchanged_input", False)),
+            attention=self.structure.attention,
         )
-        m, n, stages = _tile_key(parameters["attention_tile"])
-        updates: dict[str, Any] = {"attention_launch": Sm100AttentionParams(block_m=m, block_n=n, kv_stages=stages)}
+        updates: dict[str, Any] = {}
+        if "attention_tile" in parameters:
+            m, n, stages = _tile_key(parameters["attention_tile"])
+            updates["attention_launch"] = Sm100AttentionParams(block_m=m, block_n=n, kv_stages=stages)
         for name, launch_field in _GEMM_ROLES:
             tm, tn, tk, st = _tile_key(parameters[name])
             updates[launch_field] = Sm100GemmParams(tile_m=tm, tile_n=tn, tile_k=tk, stages=st)
         return ConfigSpec(
-            program=default_program(self.structure.precision_plan), schedule=replace(schedule, **updates)
+            program=default_program(self.structure.precision_plan, self.structure.attention),
+            schedule=replace(schedule, **updates),
         )
 
     def parameters_for(self, config: ConfigSpec) -> dict[str, Scalar] | None:
         if StructureSpec.from_config(config) != self.structure:
             return None
         schedule = config.schedule
-        if schedule.attention_launch is None:
-            return None
-        a = schedule.attention_launch
-        values: dict[str, Scalar] = {"attention_tile": _tile_name((a.block_m, a.block_n, a.kv_stages))}
+        values: dict[str, Scalar] = {}
+        if "attention_tile" in self.parameter_names:
+            a = schedule.attention_launch
+            if a is None:
+                return None
+            values["attention_tile"] = _tile_name((a.block_m, a.block_n, a.kv_stages))
         for name, launch_field in _GEMM_ROLES:
             g = getattr(schedule, launch_field)
             if g is None:

@@ -137,6 +137,19 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_int,  # variant
         _c_void_p,  # stream
     ]
+    lib.b200tx_attention_generic.restype = ctypes.c_int
+    lib.b200tx_attention_generic.argtypes = [
+        _c_void_p,  # qkv
+        _c_void_p,  # key_valid (nullable)
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # heads
+        _c_int64,  # head_dim
+        ctypes.c_float,  # scale
+        ctypes.c_int,  # causal
+        _c_void_p,  # stream
+    ]
     lib.b200tx_attention_masked.restype = ctypes.c_int
     lib.b200tx_attention_masked.argtypes = [
         _c_void_p,  # qkv
@@ -346,6 +359,37 @@ def attention(
     )
 
 
+def attention_generic(
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    batch: int,
+    seq: int,
+    heads: int,
+    head_dim: int,
+    scale: float,
+    causal: bool,
+    key_valid: torch.Tensor | None = None,
+) -> None:
+    """Launch b200tx_attention_generic (CUDA-core attention, head_dim 8..256)."""
+
+    lib = load()
+    _check(
+        lib.b200tx_attention_generic(
+            qkv.data_ptr(),
+            None if key_valid is None else key_valid.data_ptr(),
+            out.data_ptr(),
+            int(batch),
+            int(seq),
+            int(heads),
+            int(head_dim),
+            float(scale),
+            int(bool(causal)),
+            _stream(qkv.device),
+        ),
+        "b200tx_attention_generic",
+    )
+
+
 __all__ = [
     "ABI_VERSION",
     "ATTN_PAIRED",
@@ -361,6 +405,7 @@ __all__ = [
     "MASK_ZERO_NORMED",
     "MASK_ZERO_RESIDUAL",
     "attention",
+    "attention_generic",
     "device_check",
     "device_error",
     "dtype_code",

@@ -29,6 +29,10 @@ class AttentionBackend(StrEnum):
     # tcgen05 flash attention, head_dim 64, reads the packed [B,S,3D] QKV,
     # writes the [B,S,D] context (csrc/attention_kernels.cuh).
     SM100_FLASH = "sm100_flash"
+    # Tiled flash attention on the CUDA cores for head_dim 8..256 (the head
+    # dims the tensor-core kernels do not build; csrc/attention_simt_kernels.cuh),
+    # same packed [B,S,3D] input and [B,S,D] output.
+    SM100_SIMT = "sm100_simt"
 
 
 class ProjectionBackend(StrEnum):
@@ -305,14 +309,15 @@ class ProgramConfig:
         # The packed-BSD materialisation is only readable by the sm100 flash
         # kernel, which always writes BSD: keep the pairing explicit so a
         # future variant cannot silently mismatch.
+        sm100_attention = (AttentionBackend.SM100_FLASH, AttentionBackend.SM100_SIMT)
         if (
             self.qkv_materialization is QKVMaterialization.PACKED_BSD
-            and self.attention is not AttentionBackend.SM100_FLASH
+            and self.attention not in sm100_attention
         ):
-            raise ValueError("packed_bsd QKV requires the sm100_flash attention")
+            raise ValueError("packed_bsd QKV requires an sm100 attention")
         if (
             self.attention_output_bridge is AttentionOutputBridge.ATTENTION_DIRECT_BSD
-            and self.attention is not AttentionBackend.SM100_FLASH
+            and self.attention not in sm100_attention
         ):
             raise ValueError("attention_direct_bsd requires an attention that writes BSD")
 
@@ -525,11 +530,14 @@ class ConfigSpec:
         )
 
 
-def default_program(precision_plan: PrecisionPlan = PrecisionPlan.BF16_CORE) -> ProgramConfig:
+def default_program(
+    precision_plan: PrecisionPlan = PrecisionPlan.BF16_CORE,
+    attention: AttentionBackend = AttentionBackend.SM100_FLASH,
+) -> ProgramConfig:
     """The sm100 program: every primitive is a libb200tx kernel."""
 
     return ProgramConfig(
-        attention=AttentionBackend.SM100_FLASH,
+        attention=attention,
         qkv_projection=ProjectionBackend.SM100_BF16,
         attention_output_projection=ProjectionBackend.SM100_BF16,
         ffn_input_projection=ProjectionBackend.SM100_BF16,
@@ -549,11 +557,12 @@ def default_schedule(
     batch_tile_size: int | None = None,
     microbatch_size: int | None = None,
     reuse_unchanged_input: bool = False,
+    attention: AttentionBackend = AttentionBackend.SM100_FLASH,
 ) -> ScheduleConfig:
     gemm = Sm100GemmParams()
     return ScheduleConfig(
         runtime=runtime,
-        attention_launch=Sm100AttentionParams(),
+        attention_launch=Sm100AttentionParams() if attention is AttentionBackend.SM100_FLASH else None,
         qkv_launch=gemm,
         attention_output_projection_launch=gemm,
         residual_norm_launch=Sm100NormParams(),
@@ -566,15 +575,24 @@ def default_schedule(
     )
 
 
-def portable_config() -> ConfigSpec:
+def default_attention(head_dim: int | None) -> AttentionBackend:
+    """The tensor-core kernels for head_dim 64 (or unknown), else the CUDA-core one."""
+
+    return AttentionBackend.SM100_FLASH if head_dim in (None, 64) else AttentionBackend.SM100_SIMT
+
+
+def portable_config(*, head_dim: int | None = None) -> ConfigSpec:
     """The default program under the eager schedule.
 
     In the reference this is the torch fallback (solution/config.py:788-806);
     here there is no fallback, so "portable" means the sm100 program with no
-    shape-specific schedule.
+    shape-specific schedule (its attention chosen by head_dim).
     """
 
-    return ConfigSpec(program=default_program(), schedule=default_schedule())
+    attention = default_attention(head_dim)
+    return ConfigSpec(
+        program=default_program(attention=attention), schedule=default_schedule(attention=attention)
+    )
 
 
 def portable_streamed_config(*, microbatch_size: int = 1) -> ConfigSpec:
@@ -607,6 +625,7 @@ __all__ = [
     "Sm100AttentionParams",
     "Sm100GemmParams",
     "Sm100NormParams",
+    "default_attention",
     "default_program",
     "default_schedule",
     "fp32_update_roles",

@@ -12,6 +12,9 @@ There is no fallback path.
 
 from .attention import (
     SM100_FLASH_ATTENTION_BACKEND,
+    SM100_SIMT_ATTENTION_BACKEND,
+    can_use_sm100_simt_attention,
+    sm100_simt_attention,
     can_use_sm100_flash_attention,
     sm100_flash_attention,
     sm100_flash_attention_available,
@@ -40,6 +43,9 @@ __all__ = [
     "MASK_ZERO_NORMED",
     "MASK_ZERO_RESIDUAL",
     "SM100_FLASH_ATTENTION_BACKEND",
+    "SM100_SIMT_ATTENTION_BACKEND",
+    "can_use_sm100_simt_attention",
+    "sm100_simt_attention",
     "SM100_INITIAL_LAYER_NORM_BACKEND",
     "SM100_LINEAR_BACKEND",
     "SM100_LINEAR_GELU_BACKEND",

@@ -32,6 +32,8 @@ from .plan import ExecutionContext, ExecutionPlan, ExpectedExecutionTrace
 Reject = Callable[[str, str, str], None]
 
 SUPPORTED_HEAD_DIMS = frozenset({64})
+# Head dims built into the CUDA-core attention (b200tx_attention_generic).
+SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
 # The attention variant that reads a key padding mask (B200TX_ATTN_QUAD).
 SM100_QUAD_ATTENTION_VARIANT = 2
 SUPPORTED_IO_DTYPES = frozenset({torch.float32, torch.bfloat16})
@@ -272,6 +274,7 @@ class PlanBuilder:
         launch = config.schedule.attention_launch
         if (
             context.has_valid_token_mask
+            and config.program.attention is AttentionBackend.SM100_FLASH
             and launch is not None
             and launch.kernel_variant != SM100_QUAD_ATTENTION_VARIANT
         ):
@@ -287,6 +290,13 @@ class PlanBuilder:
                     "unsupported_shape",
                     "program.attention",
                     f"sm100 flash attention is built for head_dim 64, not {head_dim}",
+                )
+        elif config.program.attention is AttentionBackend.SM100_SIMT:
+            if head_dim is not None and head_dim not in SIMT_HEAD_DIMS:
+                reject(
+                    "unsupported_shape",
+                    "program.attention",
+                    f"sm100 CUDA-core attention is built for head_dim {sorted(SIMT_HEAD_DIMS)}, not {head_dim}",
                 )
         if context.d_model % 8:
             reject(

@@ -29,17 +29,19 @@ from typing import Any
 import torch
 from torch import nn
 
-from .config import ConfigSpec, RuntimeBackend, portable_config
+from .config import AttentionBackend, ConfigSpec, RuntimeBackend, portable_config
 from .kernels import (
     MASK_DROP_UPDATE,
     MASK_ZERO_NORMED,
     MASK_ZERO_RESIDUAL,
     SM100_FLASH_ATTENTION_BACKEND,
+    SM100_SIMT_ATTENTION_BACKEND,
     SM100_INITIAL_LAYER_NORM_BACKEND,
     SM100_LINEAR_BACKEND,
     SM100_LINEAR_GELU_BACKEND,
     SM100_RESIDUAL_LAYER_NORM_BACKEND,
     sm100_flash_attention,
+    sm100_simt_attention,
     sm100_initial_layer_norm,
     sm100_linear,
     sm100_residual_layer_norm,
@@ -277,7 +279,7 @@ class UserOptimizedTransformer(nn.Module):
         self._classified_mask_is_all_valid = False
         self._plan_builder = PlanBuilder()
         self._explicit_config: ConfigSpec | None = None
-        self._active_config = portable_config()
+        self._active_config = portable_config(head_dim=int(config.d_model) // int(config.num_heads))
         self._deployment_signature: tuple[object, ...] | None = None
         self.kernel_events: KernelEventRecorder | None = None
         self.register_load_state_dict_post_hook(_after_weight_load)
@@ -379,7 +381,7 @@ class UserOptimizedTransformer(nn.Module):
         selected = resolved or (
             default_streamed_config(int(shape[0]))
             if is_streamed_shape(shape[1], shape[2])
-            else portable_config()
+            else portable_config(head_dim=int(self.config.d_model) // int(self.config.num_heads))
         )
         if selected != self._active_config:
             self._invalidate_runtime_state()
@@ -548,6 +550,7 @@ class UserOptimizedTransformer(nn.Module):
         attention_variant = (
             plan.attention_launch.kernel_variant if plan.attention_launch is not None else 0
         )
+        simt_attention = plan.attention_backend is AttentionBackend.SM100_SIMT
 
         def gemm_variant(launch: Any) -> int:
             return launch.kernel_variant if launch is not None else 1  # the CTA-pair GEMM
@@ -631,13 +634,16 @@ class UserOptimizedTransformer(nn.Module):
                 planned_backend=plan.qkv_projection_backend.value,
             )
             token = rec.start("attention")
-            _, marker = sm100_flash_attention(
-                qkv, heads, causal=causal, out=context, variant=attention_variant, key_valid=key_valid
-            )
+            if simt_attention:
+                _, marker = sm100_simt_attention(qkv, heads, causal=causal, out=context, key_valid=key_valid)
+            else:
+                _, marker = sm100_flash_attention(
+                    qkv, heads, causal=causal, out=context, variant=attention_variant, key_valid=key_valid
+                )
             rec.stop(token)
             _strict_backend_marker(
                 marker,
-                expected_marker=SM100_FLASH_ATTENTION_BACKEND,
+                expected_marker=SM100_SIMT_ATTENTION_BACKEND if simt_attention else SM100_FLASH_ATTENTION_BACKEND,
                 planned_backend=plan.attention_backend.value,
             )
             w_o, b_o = attention.out_proj.shadow_parameters()

@@ -124,6 +124,33 @@ def test_padding_mask_against_oracle_and_runtimes() -> None:
     assert torch.equal(_run(graph, x, mask), eager)
 
 
+# The reference's official benchmark shapes (official/test_shapes.json) whose
+# head dims are not 64 run on the CUDA-core attention; checked against the
+# oracle on a few batch rows (rows are independent).
+OFFICIAL_SHAPES = {
+    "official_01": OfficialConfig(64, 128, 128, 4, 128, 4),  # head_dim 32
+    "official_07": OfficialConfig(64, 128, 32, 4, 32, 4),  # head_dim 8
+    "official_08": OfficialConfig(64, 128, 1024, 4, 1024, 4),  # head_dim 256
+    "official_09": OfficialConfig(64, 128, 128, 1, 128, 4),  # head_dim 128
+    "official_11": OfficialConfig(64, 128, 128, 16, 128, 4),  # head_dim 8
+    "official_12": OfficialConfig(64, 32, 128, 4, 128, 4),  # S=32
+    "official_13": OfficialConfig(64, 1024, 128, 4, 128, 4),  # S=1024
+}
+
+
+@pytest.mark.parametrize("case", sorted(OFFICIAL_SHAPES))
+def test_reference_official_shapes(case: str) -> None:
+    cfg = OFFICIAL_SHAPES[case]
+    x = official_input(cfg, 7)
+    model = _model(cfg)
+    y = _run(model, x)
+    rows = [0, cfg.batch_size - 1]
+    _gate(y[rows], _rows_reference(cfg, x, rows))
+    head_dim = cfg.d_model // cfg.num_heads
+    expected = "sm100_flash" if head_dim == 64 else "sm100_simt"
+    assert model.active_config.program.attention.value == expected
+
+
 def test_bf16_input_gives_bf16_output() -> None:
     golden = load_golden("c1_official")
     cfg = _golden_config(golden)

@@ -57,7 +57,8 @@ def test_resident_space_has_every_structure_and_the_portable_branch() -> None:
     space = _space()
     runtimes = {b.structure.runtime for b in space.branches}
     assert runtimes == {RuntimeBackend.EAGER, RuntimeBackend.CUDA_GRAPH, RuntimeBackend.BATCH_TILED_CUDA_GRAPH}
-    assert len(space.branches) == 6  # two precision plans x three runtimes
+    # two attention backends (head_dim 64 has both) x two precision plans x three runtimes
+    assert len(space.branches) == 12
     portable = space.branch_for(portable_config())
     assert portable is not None and portable.structure.portable
     assert portable.branch_id in space.mandatory_branch_ids
@@ -105,9 +106,17 @@ def test_streamed_scope_offers_microbatches() -> None:
 
 def test_masked_context_keeps_only_the_quad_attention() -> None:
     space = _space(has_valid_token_mask=True)
-    tiles = {branch.parameters_for(c)["attention_tile"] for branch in space.branches for c in branch.configs()
+    tiles = {branch.parameters_for(c).get("attention_tile") for branch in space.branches for c in branch.configs()
              if space.accepted(c)}
-    assert tiles == {"512x64x6"}
+    assert tiles == {"512x64x6", None}  # the quad kernel, or the CUDA-core kernel (no tile)
+
+
+def test_other_head_dims_search_only_the_cuda_core_attention() -> None:
+    from solution.config import AttentionBackend
+
+    space = _space(d_model=128, num_heads=4)  # head_dim 32, as the reference's official shapes
+    assert {b.structure.attention for b in space.branches} == {AttentionBackend.SM100_SIMT}
+    assert portable_config(head_dim=32) in list(space.configs())
 
 
 def test_trial_suggestion_and_structure_from_config() -> None:
