@@ -319,7 +319,11 @@ def run_gpu(args: argparse.Namespace) -> None:
         tp = _c4_tp(args, cfg.batch_size, world)
         group, _, _ = tensor_parallel_groups(tp)
         partials = torch.bfloat16 if args.tp_partials == "bf16" else torch.float32
-        runner = TensorParallelTransformer(model, group=group, partial_dtype=partials)
+        if args.tp_reduction == "auto":
+            args.tp_reduction = "peer" if tp == 2 else "nccl"
+        runner = TensorParallelTransformer(
+            model, group=group, partial_dtype=partials, reduction=args.tp_reduction
+        )
     else:
         runner = model
     x_host = x_cpu.pin_memory()
@@ -474,8 +478,13 @@ def run_gpu(args: argparse.Namespace) -> None:
                 "seq_len": cfg.seq_len,
                 "parallelism": (
                     (f"dp{world // tp} x " if tp < world else "")
-                    + f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials"
-                    " after out-proj and FFN-down)"
+                    + (
+                        f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials"
+                        " after out-proj and FFN-down)"
+                        if args.tp_reduction == "nccl"
+                        else f"tp{tp} (head-sharded, bf16 partials summed over NVLink peer memory"
+                        " inside the residual LayerNorm after out-proj and FFN-down)"
+                    )
                     if parallel == "heads"
                     else f"dp{world} (batch-sharded, no collective)"
                 ),
@@ -503,6 +512,8 @@ def run_gpu(args: argparse.Namespace) -> None:
                 k: v for k, v in cpu_baseline(steps=1).items() if k in ("value", "unit", "cores", "kind", "sample")
             }
         print(json.dumps(line), flush=True)
+    if hasattr(runner, "close"):
+        runner.close()
     del runner
     if dist is not None:
         dist.barrier()
@@ -606,6 +617,9 @@ def main() -> None:
                         help="BASELINE config to run (c2 is the bench line the driver records)")
     parser.add_argument("--tp", type=int, default=0,
                         help="c4 under torchrun: tensor-parallel group size (default: max(2, N / B))")
+    parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer"), default="auto",
+                        help="c4: NCCL all-reduce, or the peer-memory reduction fused into the "
+                             "LayerNorm (auto: peer for groups of 2, NCCL otherwise)")
     parser.add_argument("--tp-partials", choices=("fp32", "bf16"), default="bf16",
                         help="dtype of the partial sums all-reduced by the head-sharded runtime")
     parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")

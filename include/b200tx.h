@@ -191,6 +191,45 @@ int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* ou
                              int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
                              cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Tensor-parallel reduction over NVLink peer memory.  The reference is
+ * single-GPU; these entry points implement the head-sharded runtime's
+ * reduction after the row-parallel projections (out-proj and FFN-out) without
+ * a separate all-reduce: each rank's GEMM writes its partial into a buffer the
+ * peers opened through CUDA IPC, b200tx_peer_signal publishes an epoch into
+ * each peer's flag array, and b200tx_residual_layer_norm_peer sums every
+ * rank's partial into the residual and normalises in one pass.
+ * ------------------------------------------------------------------------ */
+#define B200TX_IPC_HANDLE_BYTES 64
+
+/* Set-up only (these allocate and map memory): a zero-filled device buffer of
+ * `bytes` and its IPC handle (B200TX_IPC_HANDLE_BYTES) for the peers; opening a
+ * peer's handle in this process; closing / freeing. */
+int b200tx_peer_alloc(size_t bytes, void** device_ptr_out, void* ipc_handle_out);
+int b200tx_peer_open(const void* ipc_handle, void** device_ptr_out);
+int b200tx_peer_close(void* device_ptr);
+int b200tx_peer_free(void* device_ptr);
+
+/* After this rank's partial is complete on `stream`: store `epoch` (release,
+ * system scope) into peer_slots[i], this rank's slot in each peer's flag array
+ * (count <= 8; a NULL slot is skipped). */
+int b200tx_peer_signal(uint32_t* const* peer_slots, int count, uint32_t epoch, cudaStream_t stream);
+
+/*
+ * b200tx_residual_layer_norm_masked with update = the sum of `count` bf16
+ * partials [rows, cols] (partials[self] local, the others peers' buffers):
+ * waits (bounded, system-scope acquire) until flags[r] >= epoch for every peer
+ * r, then r = residual_in + sum_r partials[r], normalised.  residual_in F32;
+ * cols a multiple of 128 up to 2048; row_valid may be NULL.  A wait that runs
+ * out records its code in b200tx_device_error and writes nothing.
+ */
+int b200tx_residual_layer_norm_peer(const float* residual_in, const void* const* partials, int count,
+                                    int self, const uint32_t* flags, uint32_t epoch,
+                                    float* residual_out, void* normed, int out_dtype,
+                                    const float* gamma, const float* beta, const uint8_t* row_valid,
+                                    int mask_mode, int64_t rows, int64_t cols, float eps,
+                                    cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,6 +11,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -531,6 +532,135 @@ int b200tx_attention_masked(const void* qkv, const uint8_t* key_valid, void* out
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_masked: null key_valid");
   return attention_impl(qkv, key_valid, out, batch, seq, heads, head_dim, scale, causal, variant,
                         stream);
+}
+
+int b200tx_peer_alloc(size_t bytes, void** device_ptr_out, void* ipc_handle_out) {
+  if (device_ptr_out == nullptr || ipc_handle_out == nullptr || bytes == 0)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "peer_alloc: null output or zero size");
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, bytes);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_alloc: cudaMalloc");
+  err = cudaMemset(p, 0, bytes);
+  if (err == cudaSuccess) {
+    cudaIpcMemHandle_t h;
+    err = cudaIpcGetMemHandle(&h, p);
+    if (err == cudaSuccess) {
+      static_assert(sizeof(h) == B200TX_IPC_HANDLE_BYTES, "IPC handle size");
+      std::memcpy(ipc_handle_out, &h, sizeof(h));
+      *device_ptr_out = p;
+      return B200TX_OK;
+    }
+  }
+  cudaFree(p);
+  return cuda_fail(err, "peer_alloc: zero fill / cudaIpcGetMemHandle");
+}
+
+int b200tx_peer_open(const void* ipc_handle, void** device_ptr_out) {
+  if (ipc_handle == nullptr || device_ptr_out == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "peer_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t err = cudaIpcOpenMemHandle(device_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_open: cudaIpcOpenMemHandle");
+  return B200TX_OK;
+}
+
+int b200tx_peer_close(void* device_ptr) {
+  cudaError_t err = cudaIpcCloseMemHandle(device_ptr);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_close: cudaIpcCloseMemHandle");
+  return B200TX_OK;
+}
+
+int b200tx_peer_free(void* device_ptr) {
+  cudaError_t err = cudaFree(device_ptr);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_free: cudaFree");
+  return B200TX_OK;
+}
+
+int b200tx_peer_signal(uint32_t* const* peer_slots, int count, uint32_t epoch, cudaStream_t stream) {
+  if (peer_slots == nullptr || count <= 0 || count > b200tx::kMaxPeers)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "peer_signal: count %d (1..%d)", count, b200tx::kMaxPeers);
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  b200tx::PeerSignalArgs a = {};
+  for (int i = 0; i < count; ++i) a.slots[i] = peer_slots[i];
+  a.count = count;
+  a.epoch = epoch;
+  cudaError_t err = launch(b200tx::peer_signal_kernel, dim3(1), dim3(32), 0, stream, a);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_signal launch");
+  return B200TX_OK;
+}
+
+int b200tx_residual_layer_norm_peer(const float* residual_in, const void* const* partials, int count,
+                                    int self, const uint32_t* flags, uint32_t epoch,
+                                    float* residual_out, void* normed, int out_dtype,
+                                    const float* gamma, const float* beta, const uint8_t* row_valid,
+                                    int mask_mode, int64_t rows, int64_t cols, float eps,
+                                    cudaStream_t stream) {
+  if (residual_in == nullptr || partials == nullptr || flags == nullptr || normed == nullptr ||
+      gamma == nullptr || beta == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer: null pointer");
+  if (count < 1 || count > b200tx::kMaxPeers || self < 0 || self >= count)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer: count %d self %d", count, self);
+  if (rows <= 0 || cols <= 0 || cols % 128 != 0 || (rows + 7) / 8 > 0x7fffffffLL)
+    return fail(B200TX_ERR_UNSUPPORTED, "residual_layer_norm_peer: shape [%lld, %lld] (cols %% 128 == 0)",
+                (long long)rows, (long long)cols);
+  if (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer: out_dtype %d", out_dtype);
+  if (mask_mode < 0 || mask_mode > 7)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer: mask_mode %d", mask_mode);
+  bool ok = aligned16(residual_in) && aligned16(normed) && aligned16(gamma) && aligned16(beta) &&
+            (residual_out == nullptr || aligned16(residual_out));
+  b200tx::PeerSumArgs p = {};
+  for (int i = 0; i < count; ++i) {
+    if (partials[i] == nullptr || (reinterpret_cast<uintptr_t>(partials[i]) & 7u) != 0) ok = false;
+    p.partials[i] = static_cast<const __nv_bfloat16*>(partials[i]);
+  }
+  if (!ok) return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer: misaligned or null operand");
+  p.count = count;
+  p.self = self;
+  p.flags = flags;
+  p.epoch = epoch;
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  b200tx::NormArgs a;
+  a.residual_in = residual_in;
+  a.update = nullptr;
+  a.residual_out = residual_out;
+  a.normed = normed;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.row_valid = row_valid;
+  a.mask_mode = row_valid != nullptr ? mask_mode : 0;
+  a.rows = rows;
+  a.cols = static_cast<int>(cols);
+  a.eps = eps;
+  const dim3 grid(static_cast<unsigned>((rows + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock));
+  const dim3 block(b200tx::kNormWarpsPerBlock * 32);
+  const bool bf16 = out_dtype == B200TX_BF16;
+  cudaError_t err;
+#define B200TX_PEER_NV(NV)                                                                         \
+  case NV:                                                                                        \
+    err = bf16 ? launch(b200tx::residual_layernorm_peer_kernel<NV, __nv_bfloat16>, grid, block, 0, \
+                        stream, a, p)                                                             \
+               : launch(b200tx::residual_layernorm_peer_kernel<NV, float>, grid, block, 0, stream, a, p); \
+    break;
+  switch (cols / 128) {
+    B200TX_PEER_NV(1)
+    B200TX_PEER_NV(2)
+    B200TX_PEER_NV(4)
+    B200TX_PEER_NV(6)
+    B200TX_PEER_NV(8)
+    B200TX_PEER_NV(12)
+    B200TX_PEER_NV(16)
+    default:
+      return fail(B200TX_ERR_UNSUPPORTED, "residual_layer_norm_peer: cols %lld not built", (long long)cols);
+  }
+#undef B200TX_PEER_NV
+  if (err != cudaSuccess) return cuda_fail(err, "residual_layer_norm_peer launch");
+  return B200TX_OK;
 }
 
 int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,

@@ -236,4 +236,183 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel reduction fused into the residual LayerNorm.  Each rank of a
+// tensor-parallel group writes its partial sum of a row-parallel projection
+// (out-proj, FFN-out) into a buffer its peers can read over NVLink; this
+// kernel adds the partials of all `count` ranks (its own and the peers') to the
+// residual and normalises, in one pass, so no separate all-reduce moves the
+// partials.  Before reading, one thread per CTA waits until every peer has
+// published the epoch (peer_signal_kernel after its GEMM) with a bounded
+// acquire spin at system scope; a wait that runs out records
+// kErrPeerWait and the CTA stops without writing.
+// ---------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;
+
+struct PeerSumArgs {
+  const __nv_bfloat16* partials[kMaxPeers];  // [rows, cols] bf16, index = group rank
+  int count;                                 // ranks in the group
+  int self;                                  // this rank (its partial is local)
+  const uint32_t* flags;                     // [count] local slots written by the peers
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait for every peer's epoch; one thread per CTA, then the CTA syncs.
+__device__ __forceinline__ bool wait_peer_epoch(const PeerSumArgs& p) {
+  __shared__ int ok_shared;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned long long start = global_timer_ns();
+    for (int r = 0; r < p.count && ok; ++r) {
+      if (r == p.self) continue;
+      uint32_t spins = 0;
+      while (static_cast<int32_t>(ld_acquire_sys(p.flags + r) - p.epoch) < 0) {
+        if ((++spins & 63u) == 0u &&
+            (device_error_raised() || global_timer_ns() - start > kWaitTimeoutNs)) {
+          record_device_error(kErrPeerWait);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_shared = ok;
+  }
+  __syncthreads();
+  return ok_shared != 0;
+}
+
+template <int NV, typename OutT>
+__global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
+    residual_layernorm_peer_kernel(NormArgs args, PeerSumArgs peers) {
+  griddep_wait();
+  griddep_launch_dependents();
+  if (!wait_peer_epoch(peers)) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kNormWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= args.rows) return;
+  const int cols = 128 * NV;
+  const int64_t base = row * cols;
+  const float* rin = static_cast<const float*>(args.residual_in);
+  const RowMask mask = row_mask(args, row);
+  float4 v[NV];
+  if (mask.zero_residual) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else if (peers.count == 2 && mask.add_update) {
+    // Two ranks (the common tensor-parallel group): issue the NVLink loads of
+    // the peer's partial first, so their latency overlaps the local loads.
+    const __nv_bfloat16* remote = peers.partials[peers.self ^ 1];
+    const __nv_bfloat16* local = peers.partials[peers.self];
+    uint2 rraw[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) rraw[i] = __ldcg(reinterpret_cast<const uint2*>(remote + base + (i * 32 + lane) * 4));
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t idx = base + (i * 32 + lane) * 4;
+      v[i] = load4<float>(rin, idx);
+      const uint2 lraw = __ldg(reinterpret_cast<const uint2*>(local + idx));
+      const float2 la = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lraw.x));
+      const float2 lb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lraw.y));
+      const float2 ra = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rraw[i].x));
+      const float2 rb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rraw[i].y));
+      // Rank order of the sum is kept (partial 0 first) so both ranks agree bit for bit.
+      const float2 a0 = peers.self == 0 ? la : ra, a1 = peers.self == 0 ? ra : la;
+      const float2 b0 = peers.self == 0 ? lb : rb, b1 = peers.self == 0 ? rb : lb;
+      v[i].x += a0.x;
+      v[i].y += a0.y;
+      v[i].z += b0.x;
+      v[i].w += b0.y;
+      v[i].x += a1.x;
+      v[i].y += a1.y;
+      v[i].z += b1.x;
+      v[i].w += b1.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = load4<float>(rin, base + (i * 32 + lane) * 4);
+    if (mask.add_update) {
+      for (int r = 0; r < peers.count; ++r) {
+        const __nv_bfloat16* part = peers.partials[r];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int64_t idx = base + (i * 32 + lane) * 4;
+          // Peer partials bypass L1 (written by another GPU during this
+          // program); the local one may use the read-only path.
+          uint2 raw;
+          if (r == peers.self) {
+            raw = __ldg(reinterpret_cast<const uint2*>(part + idx));
+          } else {
+            raw = __ldcg(reinterpret_cast<const uint2*>(part + idx));
+          }
+          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+          v[i].x += a.x;
+          v[i].y += a.y;
+          v[i].z += b.x;
+          v[i].w += b.y;
+        }
+      }
+    }
+  }
+  if (args.residual_out != nullptr) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) store4<float>(args.residual_out, base + (i * 32 + lane) * 4, v[i]);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  const float mean = warp_sum(s) * (1.0f / cols);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / cols) + args.eps);
+  OutT* out = static_cast<OutT*>(args.normed);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(args.gamma + c));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(args.beta + c));
+    float4 o;
+    o.x = (v[i].x - mean) * rstd * g.x + b.x;
+    o.y = (v[i].y - mean) * rstd * g.y + b.y;
+    o.z = (v[i].z - mean) * rstd * g.z + b.z;
+    o.w = (v[i].w - mean) * rstd * g.w + b.w;
+    if (mask.zero_normed) o = make_float4(0.f, 0.f, 0.f, 0.f);
+    store4<OutT>(out, base + c, o);
+  }
+}
+
+// Publishes `epoch` to the peers after this rank's partial is complete: the
+// kernel runs after the GEMM on the stream, fences at system scope and stores
+// the epoch with release semantics into this rank's slot of every peer's flag
+// array (peer memory over NVLink).
+struct PeerSignalArgs {
+  uint32_t* slots[kMaxPeers];  // this rank's slot in each peer's flag array
+  int count;
+  uint32_t epoch;
+};
+
+__global__ void peer_signal_kernel(PeerSignalArgs args) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = threadIdx.x;
+  if (i < args.count && args.slots[i] != nullptr) {
+    __threadfence_system();
+    st_release_sys(args.slots[i], args.epoch);
+  }
+}
+
 }  // namespace b200tx

@@ -29,6 +29,7 @@ enum DeviceErrorCode : unsigned int {
   kErrAttnProducerWait = 0x201,
   kErrAttnMmaWait = 0x202,
   kErrAttnSoftmaxWait = 0x203,
+  kErrPeerWait = 0x301,  // a tensor-parallel peer did not publish its partial in time
 };
 
 // A single wait gives up after this many nanoseconds.  Every event waited on

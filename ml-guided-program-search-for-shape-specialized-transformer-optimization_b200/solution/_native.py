@@ -137,6 +137,36 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_int,  # variant
         _c_void_p,  # stream
     ]
+    lib.b200tx_peer_alloc.restype = ctypes.c_int
+    lib.b200tx_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
+    lib.b200tx_peer_open.restype = ctypes.c_int
+    lib.b200tx_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.b200tx_peer_close.restype = ctypes.c_int
+    lib.b200tx_peer_close.argtypes = [_c_void_p]
+    lib.b200tx_peer_free.restype = ctypes.c_int
+    lib.b200tx_peer_free.argtypes = [_c_void_p]
+    lib.b200tx_peer_signal.restype = ctypes.c_int
+    lib.b200tx_peer_signal.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_uint32, _c_void_p]
+    lib.b200tx_residual_layer_norm_peer.restype = ctypes.c_int
+    lib.b200tx_residual_layer_norm_peer.argtypes = [
+        _c_void_p,  # residual_in (fp32)
+        ctypes.POINTER(ctypes.c_void_p),  # partials
+        ctypes.c_int,  # count
+        ctypes.c_int,  # self
+        _c_void_p,  # flags
+        ctypes.c_uint32,  # epoch
+        _c_void_p,  # residual_out
+        _c_void_p,  # normed
+        ctypes.c_int,  # out_dtype
+        _c_void_p,  # gamma
+        _c_void_p,  # beta
+        _c_void_p,  # row_valid
+        ctypes.c_int,  # mask_mode
+        _c_int64,  # rows
+        _c_int64,  # cols
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
     lib.b200tx_attention_generic.restype = ctypes.c_int
     lib.b200tx_attention_generic.argtypes = [
         _c_void_p,  # qkv
@@ -390,7 +420,91 @@ def attention_generic(
     )
 
 
+IPC_HANDLE_BYTES = 64
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A zero-filled device buffer of this library's own and its IPC handle."""
+
+    lib = load()
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib.b200tx_peer_alloc(int(nbytes), ctypes.byref(ptr), handle), "b200tx_peer_alloc")
+    return int(ptr.value), bytes(handle.raw)
+
+
+def peer_open(handle: bytes) -> int:
+    lib = load()
+    ptr = ctypes.c_void_p()
+    _check(lib.b200tx_peer_open(handle, ctypes.byref(ptr)), "b200tx_peer_open")
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    _check(load().b200tx_peer_close(ptr), "b200tx_peer_close")
+
+
+def peer_free(ptr: int) -> None:
+    _check(load().b200tx_peer_free(ptr), "b200tx_peer_free")
+
+
+def peer_signal(slots: list[int], epoch: int, device: torch.device) -> None:
+    arr = (ctypes.c_void_p * len(slots))(*slots)
+    _check(load().b200tx_peer_signal(arr, len(slots), epoch & 0xFFFFFFFF, _stream(device)), "b200tx_peer_signal")
+
+
+def residual_layer_norm_peer(
+    residual_in: torch.Tensor,
+    partials: list[int],
+    self_index: int,
+    flags: int,
+    epoch: int,
+    residual_out: torch.Tensor | None,
+    normed: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    row_valid: torch.Tensor | None = None,
+    mask_mode: int = 0,
+) -> None:
+    """Launch b200tx_residual_layer_norm_peer: residual + sum of the group's
+    bf16 partials (device pointers, partials[self_index] local), normalised."""
+
+    cols = residual_in.shape[-1]
+    rows = residual_in.numel() // cols
+    arr = (ctypes.c_void_p * len(partials))(*partials)
+    _check(
+        load().b200tx_residual_layer_norm_peer(
+            residual_in.data_ptr(),
+            arr,
+            len(partials),
+            int(self_index),
+            flags,
+            epoch & 0xFFFFFFFF,
+            None if residual_out is None else residual_out.data_ptr(),
+            normed.data_ptr(),
+            dtype_code(normed.dtype),
+            gamma.data_ptr(),
+            beta.data_ptr(),
+            None if row_valid is None else row_valid.data_ptr(),
+            int(mask_mode),
+            rows,
+            cols,
+            float(eps),
+            _stream(residual_in.device),
+        ),
+        "b200tx_residual_layer_norm_peer",
+    )
+
+
 __all__ = [
+    "IPC_HANDLE_BYTES",
+    "peer_alloc",
+    "peer_close",
+    "peer_free",
+    "peer_open",
+    "peer_signal",
+    "residual_layer_norm_peer",
     "ABI_VERSION",
     "ATTN_PAIRED",
     "ATTN_QUAD",

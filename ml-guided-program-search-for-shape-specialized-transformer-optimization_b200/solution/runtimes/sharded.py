@@ -20,9 +20,16 @@ solution/shape14/executor.py:12-49; the reference itself is single-GPU):
       r, n  = r + u, LN(r)                    replicated on every rank
       h_r   = GELU(n . W1_r^T + b1_r)         (column parallel)
       u     = allreduce_sum(h_r . W2_r^T) + b2         (row parallel)
-  The partial sums travel through NCCL (NVLink/NVSwitch) into local buffers;
-  the biases of the row-parallel projections are added once, after the
-  reduction, by rank 0's partial.  Every rank ends with the full output.
+  The biases of the row-parallel projections are added once, by rank 0's
+  partial.  Every rank ends with the full output.  Two reductions are built:
+  * ``reduction="nccl"``: the partial is all-reduced by NCCL (NVLink/NVSwitch)
+    and the residual LayerNorm reads the sum;
+  * ``reduction="peer"`` (`PeerReduction`): the GEMM writes its partial into a
+    buffer the other ranks of the group mapped through CUDA IPC, a one-warp
+    kernel publishes an epoch into each peer's flag array, and the residual
+    LayerNorm kernel itself waits for the peers' epochs and sums all partials
+    over NVLink loads while it normalises -- the reduction is fused into the
+    kernel that consumes it, and no all-reduce moves the data twice.
 """
 
 from __future__ import annotations
@@ -39,6 +46,110 @@ from ..kernels import (
 )
 
 HEAD_DIM = 64
+
+
+class _DeviceBuffer:
+    """A raw device allocation of this library, addressed by the launch
+    wrappers like a contiguous tensor (they read data_ptr() and dtype)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], dtype: torch.dtype) -> None:
+        self.ptr = ptr
+        self.shape = shape
+        self.dtype = dtype
+
+    def data_ptr(self) -> int:
+        return self.ptr
+
+
+class PeerReduction:
+    """Partial-sum exchange of one tensor-parallel group over NVLink peer memory.
+
+    Every rank owns two bf16 partial buffers (used alternately by the two
+    reductions of a block) and a flag array with one uint32 slot per group
+    rank, all allocated by libb200tx and shared with the group through CUDA
+    IPC handles (exchanged once with ``all_gather_object``).  ``signal()``
+    publishes the next epoch into this rank's slot of every peer's flags
+    after the partial is written; the peer LayerNorm waits for all epochs.
+
+    Reuse needs no extra acknowledgement: a rank rewrites buffer k only two
+    reductions later, after its own LayerNorm waited for the peers' epoch of
+    the reduction in between, which each peer publishes only after its
+    LayerNorm finished reading buffer k.
+    """
+
+    def __init__(self, group: object, rows: int, cols: int, device: torch.device) -> None:
+        import torch.distributed as dist
+
+        from .. import _native
+
+        self._native = _native
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the peer reduction is built for groups of up to 8 ranks")
+        self.rows, self.cols, self.device = rows, cols, device
+        with torch.cuda.device(device):
+            own = [_native.peer_alloc(rows * cols * 2) for _ in range(2)]
+            flags = _native.peer_alloc(4 * 8)
+        self._own = [ptr for ptr, _ in own] + [flags[0]]
+        handles = [[h for _, h in own] + [flags[1]]]
+        gathered: list[object] = [None] * self.world
+        dist.all_gather_object(gathered, handles[0], group=group)
+        self._opened: list[int] = []
+        self.partials: list[list[int]] = [[0] * self.world for _ in range(2)]
+        peer_flags: list[int] = [0] * self.world
+        with torch.cuda.device(device):
+            for r, hs in enumerate(gathered):
+                if r == self.rank:
+                    ptrs = self._own
+                else:
+                    ptrs = [_native.peer_open(h) for h in hs]
+                    self._opened += ptrs
+                self.partials[0][r], self.partials[1][r], peer_flags[r] = ptrs
+        self.flags = flags[0]
+        # This rank's slot in each peer's flag array (its own slot unused).
+        self.slots = [peer_flags[r] + 4 * self.rank for r in range(self.world) if r != self.rank]
+        self.epoch = 0
+        self._buffer = 0
+
+    def partial(self, rows: int) -> _DeviceBuffer:
+        """This rank's buffer for the next reduction."""
+
+        if rows > self.rows:
+            raise ValueError(f"{rows} rows exceed the {self.rows} the peer buffers were sized for")
+        return _DeviceBuffer(self._own[self._buffer], (rows, self.cols), torch.bfloat16)
+
+    def signal(self) -> None:
+        self.epoch += 1
+        self._native.peer_signal(self.slots, self.epoch, self.device)
+
+    def reduce_layer_norm(self, residual_in: torch.Tensor, **kwargs: object) -> None:
+        """residual_in + the group's partials of this reduction, normalised."""
+
+        self._native.residual_layer_norm_peer(
+            residual_in, self.partials[self._buffer], self.rank, self.flags, self.epoch, **kwargs
+        )
+        self._buffer ^= 1
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then (once every rank has) free our own.
+
+        Collective over the group: every rank must call it.
+        """
+
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                self._native.peer_close(ptr)
+        self._opened = []
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for ptr in self._own:
+                self._native.peer_free(ptr)
+        self._own = []
 
 
 def batch_shard_bounds(batch: int, rank: int, world: int) -> tuple[int, int]:
@@ -154,6 +265,7 @@ class TensorParallelTransformer:
         *,
         group: object | None = None,
         partial_dtype: torch.dtype = torch.float32,
+        reduction: str = "nccl",
     ) -> None:
         import torch.distributed as dist
 
@@ -161,6 +273,10 @@ class TensorParallelTransformer:
             raise RuntimeError("TensorParallelTransformer needs an initialised process group")
         if partial_dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("partial_dtype must be float32 or bfloat16")
+        if reduction not in ("nccl", "peer"):
+            raise ValueError("reduction must be 'nccl' or 'peer'")
+        self.reduction = reduction
+        self._peer: PeerReduction | None = None
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -211,8 +327,25 @@ class TensorParallelTransformer:
 
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
 
+    def _peer_reduction(self, rows: int, d_model: int) -> PeerReduction:
+        if self._peer is None or self._peer.rows < rows:
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = PeerReduction(self.group, rows, d_model, self.device)
+        return self._peer
+
+    def close(self) -> None:
+        """Release the peer buffers (the group must still be alive)."""
+
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
     @torch.inference_mode()
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        from .. import _native
+        from ..kernels.projection import can_use_sm100_linear
+
         if x.device != self.device or not x.is_contiguous() or x.dim() != 3:
             raise ValueError("x must be a contiguous [B, S, D] tensor on this rank's GPU")
         batch, seq, d_model = x.shape
@@ -224,37 +357,66 @@ class TensorParallelTransformer:
         if not self.layers:
             sm100_initial_layer_norm(flat, self.final_norm, out_dtype=x.dtype, normalized_out=out.view(rows, d_model))
             return out
+        peer = None
+        if self.reduction == "peer":
+            if x.dtype != torch.float32:
+                raise ValueError("the peer reduction reads the fp32 input as the first residual")
+            peer = self._peer_reduction(rows, d_model)
         residual = torch.empty((rows, d_model), dtype=torch.float32, device=x.device)
         normed = torch.empty((rows, d_model), dtype=torch.bfloat16, device=x.device)
         qkv = torch.empty((batch, seq, 3 * d_local), dtype=torch.bfloat16, device=x.device)
         context = torch.empty((batch, seq, d_local), dtype=torch.bfloat16, device=x.device)
         hidden = torch.empty((rows, f_local), dtype=torch.bfloat16, device=x.device)
-        partial = torch.empty((rows, d_model), dtype=self.partial_dtype, device=x.device)
+        partial = (
+            None if peer is not None else torch.empty((rows, d_model), dtype=self.partial_dtype, device=x.device)
+        )
+
+        def reduce_norm(
+            a: torch.Tensor,
+            w: torch.Tensor,
+            b: torch.Tensor,
+            residual_in: torch.Tensor,
+            norm: torch.nn.LayerNorm,
+            *,
+            last: bool,
+            normalized_out: torch.Tensor,
+        ) -> None:
+            """Row-parallel projection, group reduction, residual add + LN."""
+
+            out_dtype = x.dtype if last else torch.bfloat16
+            if peer is None:
+                sm100_linear(a, w, b, out_dtype=self.partial_dtype, out=partial)
+                self._all_reduce(partial)
+                sm100_residual_layer_norm(
+                    residual_in, partial, norm, final_boundary=last, out_dtype=out_dtype,
+                    residual_out=residual, normalized_out=normalized_out,
+                )
+                return
+            if not can_use_sm100_linear(a, w, b):
+                raise RuntimeError("sm100 linear is ineligible for the requested operands")
+            _native.linear(a, w, b, peer.partial(rows), _native.EPI_BIAS, _native.GEMM_PAIR)
+            peer.signal()
+            peer.reduce_layer_norm(
+                residual_in, residual_out=residual, normed=normalized_out,
+                gamma=norm.weight, beta=norm.bias, eps=norm.eps,
+            )
 
         sm100_initial_layer_norm(flat, self.norms[0][0], normalized_out=normed)
         source = flat
         for index, shard in enumerate(self.layers):
             sm100_linear(normed, shard.w_qkv, shard.b_qkv, out=qkv.view(rows, 3 * d_local))
             sm100_flash_attention(qkv, self.heads_local, causal=self.causal, out=context)
-            sm100_linear(
-                context.view(rows, d_local), shard.w_o, shard.b_o, out_dtype=self.partial_dtype, out=partial
-            )
-            self._all_reduce(partial)
-            sm100_residual_layer_norm(
-                source, partial, self.norms[index][1], final_boundary=False,
-                residual_out=residual, normalized_out=normed,
+            reduce_norm(
+                context.view(rows, d_local), shard.w_o, shard.b_o, source, self.norms[index][1],
+                last=False, normalized_out=normed,
             )
             source = residual
             sm100_linear(normed, shard.w_1, shard.b_1, gelu=True, out=hidden)
-            sm100_linear(hidden, shard.w_2, shard.b_2, out_dtype=self.partial_dtype, out=partial)
-            self._all_reduce(partial)
             last = index == len(self.layers) - 1
             next_norm = self.final_norm if last else self.norms[index + 1][0]
-            sm100_residual_layer_norm(
-                residual, partial, next_norm, final_boundary=last,
-                out_dtype=x.dtype if last else torch.bfloat16,
-                residual_out=residual,
-                normalized_out=out.view(rows, d_model) if last else normed,
+            reduce_norm(
+                hidden, shard.w_2, shard.b_2, residual, next_norm,
+                last=last, normalized_out=out.view(rows, d_model) if last else normed,
             )
         return out
 
@@ -263,6 +425,7 @@ class TensorParallelTransformer:
 
 __all__ = [
     "LayerShard",
+    "PeerReduction",
     "TensorParallelTransformer",
     "batch_shard_bounds",
     "shard_layer",

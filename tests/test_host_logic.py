@@ -200,6 +200,24 @@ def test_argument_errors_are_reported_before_any_launch() -> None:
     assert rc == -2 and b"multiples of 8" in lib.b200tx_last_error()
     rc = lib.b200tx_residual_layer_norm(buf, 5, None, 0, None, buf, 1, buf, buf, 4, 8, ctypes.c_float(1e-5), None)
     assert rc == -1 and b"in_dtype" in lib.b200tx_last_error()
+    rc = lib.b200tx_linear_ex(buf, buf, None, buf, 1, 16, 16, 64, 0, 9, None)
+    assert rc == -1 and b"variant" in lib.b200tx_last_error()
+    rc = lib.b200tx_attention_generic(buf, None, buf, 1, 16, 1, 48, ctypes.c_float(0.125), 1, None)
+    assert rc == -2 and b"head_dim" in lib.b200tx_last_error()
+    rc = lib.b200tx_attention_masked(buf, None, buf, 1, 16, 1, 64, ctypes.c_float(0.125), 1, 2, None)
+    assert rc == -1 and b"key_valid" in lib.b200tx_last_error()
+    slots = (ctypes.c_void_p * 1)(None)
+    rc = lib.b200tx_peer_signal(slots, 0, 1, None)
+    assert rc == -1 and b"count" in lib.b200tx_last_error()
+    parts = (ctypes.c_void_p * 2)(ctypes.addressof(buf), ctypes.addressof(buf))
+    rc = lib.b200tx_residual_layer_norm_peer(
+        buf, parts, 2, 2, buf, 1, None, buf, 1, buf, buf, None, 0, 4, 128, ctypes.c_float(1e-5), None
+    )
+    assert rc == -1 and b"self" in lib.b200tx_last_error()
+    rc = lib.b200tx_residual_layer_norm_peer(
+        buf, parts, 2, 0, buf, 1, None, buf, 1, buf, buf, None, 0, 4, 100, ctypes.c_float(1e-5), None
+    )
+    assert rc == -2 and b"cols" in lib.b200tx_last_error()
 
 
 def test_kernel_wrappers_refuse_cpu_tensors() -> None:

@@ -143,7 +143,9 @@ def test_tensor_parallel_composition_over_gloo() -> None:
     np.testing.assert_array_equal(outs[0], outs[1])
 
 
-def _nccl_worker(rank: int, world: int, port: int, result_dir: str, partials: str = "fp32") -> None:
+def _nccl_worker(
+    rank: int, world: int, port: int, result_dir: str, partials: str = "fp32", reduction: str = "nccl"
+) -> None:
     import datetime
 
     from solution.runtimes.sharded import TensorParallelTransformer
@@ -160,10 +162,17 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str, partials: st
         copy_model_weights(official_state_dict(cfg, seed=0), model)
         model = model.to(f"cuda:{rank}").eval()
         tp = TensorParallelTransformer(
-            model, partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32
+            model, partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32, reduction=reduction
         )
         x = official_input(cfg, 5).to(f"cuda:{rank}")
         y_tp = tp(x)
+        # Repeated forwards reuse the partial buffers and flags: same bits.
+        for _ in range(4):
+            assert torch.equal(tp(x), y_tp)
+        from solution import _native
+
+        assert _native.device_error(clear=True) == 0
+        tp.close()
         with torch.inference_mode():
             y_single = model(x)
         torch.cuda.synchronize()
@@ -175,14 +184,14 @@ def _nccl_worker(rank: int, world: int, port: int, result_dir: str, partials: st
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("partials", ["fp32", "bf16"])
-def test_tensor_parallel_matches_single_gpu(partials: str) -> None:
+@pytest.mark.parametrize(("partials", "reduction"), [("fp32", "nccl"), ("bf16", "nccl"), ("bf16", "peer")])
+def test_tensor_parallel_matches_single_gpu(partials: str, reduction: str) -> None:
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
         mp.start_processes(
-            _nccl_worker, args=(world, _free_port(), tmp, partials), nprocs=world, start_method="spawn"
+            _nccl_worker, args=(world, _free_port(), tmp, partials, reduction), nprocs=world, start_method="spawn"
         )
         tp = [np.load(os.path.join(tmp, f"tp{r}.npy")) for r in range(world)]
         single = np.load(os.path.join(tmp, "single0.npy"))
