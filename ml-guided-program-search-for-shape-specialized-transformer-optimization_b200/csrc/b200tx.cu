@@ -98,10 +98,12 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return B200TX_OK;
 }
 
-// Tiled bf16 tensor map with a 128-byte swizzle; out-of-range elements of a
-// box read as zero.  dims/strides innermost first; strides in bytes for dims 1..
+// Tiled bf16 tensor map (128-byte swizzle unless given); out-of-range elements
+// of a box read as zero and are not written by stores.  dims/strides innermost
+// first; strides in bytes for dims 1..
 int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box) {
+                    const uint64_t* strides_bytes, const uint32_t* box,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   int rc = encoder(&encode);
   if (rc != B200TX_OK) return rc;
@@ -117,7 +119,7 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
   }
   CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
                         const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (res != CUDA_SUCCESS) {
     return fail(B200TX_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", int(res));
@@ -363,36 +365,74 @@ int linear_impl(const void* a, const void* w, const float* bias, void* out, int 
   args.num_m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
   args.num_n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   const int64_t tiles = static_cast<int64_t>(args.num_m_tiles) * args.num_n_tiles;
-  if (tiles > 0x7fffffffLL) return fail(B200TX_ERR_UNSUPPORTED, "linear: too many tiles");
+  if (tiles > 0x3fffffffLL) return fail(B200TX_ERR_UNSUPPORTED, "linear: too many tiles");
   // Persistent grid: one CTA per SM, or one CTA pair per two SMs.
   const int64_t slots = paired ? dev->sm_count / 2 : dev->sm_count;
-  const unsigned grid =
-      static_cast<unsigned>((tiles < slots ? tiles : slots) * (paired ? 2 : 1));
-
-  using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::GemmArgs);
-  KernelFn kernel;
-  const int instance = (paired ? 4 : 0) + epilogue * 2 + (out_dtype == B200TX_F32 ? 1 : 0);
-  switch (instance) {
-    case 0: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
-    case 1: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, float>; break;
-    case 2: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
-    case 3: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, float>; break;
-    case 4: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
-    case 5: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, float>; break;
-    case 6: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
-    default: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, float>; break;
+  // Pair kernel: when the last wave holds at most half as many tiles as there
+  // are pairs, those tiles run as two 128-column halves each, on twice as many
+  // pairs for half as long.
+  int64_t units = tiles;
+  int64_t full_units = tiles;
+  if (paired) {
+    const int64_t tail = tiles % slots;
+    if (tail > 0 && 2 * tail <= slots) {
+      full_units = tiles - tail;
+      units = tiles + tail;
+    }
   }
+  args.full_units = static_cast<int>(full_units);
+  args.num_units = static_cast<int>(units);
+  const unsigned grid =
+      static_cast<unsigned>((units < slots ? units : slots) * (paired ? 2 : 1));
+
+  const int instance = (paired ? 4 : 0) + epilogue * 2 + (out_dtype == B200TX_F32 ? 1 : 0);
   const size_t smem = paired ? b200tx::kGemm2SmemBytes : b200tx::kGemmSmemBytes;
-  {
+  auto set_smem = [&](const void* fn) -> int {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!dev->gemm_attr[instance]) {
-      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
       if (err != cudaSuccess) return cuda_fail(err, "linear: cudaFuncSetAttribute");
       dev->gemm_attr[instance] = true;
     }
+    return B200TX_OK;
+  };
+  cudaError_t err = cudaSuccess;
+  if (!paired) {
+    using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::GemmArgs);
+    KernelFn kernel;
+    switch (instance) {
+      case 0: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
+      case 1: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBias, float>; break;
+      case 2: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
+      default: kernel = b200tx::gemm_bf16_tn_kernel<b200tx::kEpiBiasGelu, float>; break;
+    }
+    rc = set_smem(reinterpret_cast<const void*>(kernel));
+    if (rc != B200TX_OK) return rc;
+    err = launch(kernel, dim3(grid), dim3(b200tx::kGemmThreads), smem, stream, map_a, map_w, args);
+  } else {
+    // bf16 outputs are written by TMA stores of 32 x 32 boxes (64-byte rows,
+    // 64-byte swizzle); fp32 outputs by the threads (the map is not read).
+    CUtensorMap map_out = map_a;
+    if (out_dtype == B200TX_BF16) {
+      const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(N) * 2};
+      const uint32_t box[2] = {32u, 32u};
+      rc = encode_bf16_map(&map_out, out, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc != B200TX_OK) return rc;
+    }
+    using PairFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, b200tx::GemmArgs);
+    PairFn kernel;
+    switch (instance) {
+      case 4: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, __nv_bfloat16>; break;
+      case 5: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBias, float>; break;
+      case 6: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>; break;
+      default: kernel = b200tx::gemm_bf16_tn_pair_kernel<b200tx::kEpiBiasGelu, float>; break;
+    }
+    rc = set_smem(reinterpret_cast<const void*>(kernel));
+    if (rc != B200TX_OK) return rc;
+    err = launch(kernel, dim3(grid), dim3(b200tx::kGemmThreads), smem, stream, map_a, map_w, map_out, args);
   }
-  cudaError_t err = launch(kernel, dim3(grid), dim3(b200tx::kGemmThreads), smem, stream, map_a, map_w, args);
   if (err != cudaSuccess) return cuda_fail(err, "linear launch");
   return B200TX_OK;
 }

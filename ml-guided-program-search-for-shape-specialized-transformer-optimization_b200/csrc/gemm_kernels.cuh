@@ -46,6 +46,9 @@ struct GemmArgs {
   void* out;          // [M, N] row-major, bf16 or fp32
   int M, N, K;
   int num_m_tiles, num_n_tiles;
+  // Pair kernel only: work units are the first `full_units` tiles, then the
+  // remaining tiles each split into two 128-column halves (num_units in all).
+  int full_units, num_units;
 };
 
 // Exact-erf GELU, 0.5 x (1 + erf(x / sqrt 2)), with erf from Abramowitz &
@@ -315,12 +318,44 @@ constexpr int kGemm2Stages = 6;
 constexpr uint32_t kGemm2TileABytes = 128 * kGemmBK * 2;  // 16 KB
 constexpr uint32_t kGemm2TileBBytes = 128 * kGemmBK * 2;  // 16 KB
 constexpr uint32_t kGemm2StageBytes = kGemm2TileABytes + kGemm2TileBBytes;
-constexpr size_t kGemm2SmemBytes = 1024 + kGemm2Stages * kGemm2StageBytes;  // 193 KB
+// Epilogue staging for the TMA stores of bf16 outputs: per epilogue warp two
+// 2 KB buffers of 32 rows x 32 columns (64-byte rows, 64-byte swizzle).
+constexpr uint32_t kGemm2StoreBoxBytes = 32 * 32 * 2;
+constexpr uint32_t kGemm2StoreBytes = 8 * 2 * kGemm2StoreBoxBytes;  // 32 KB
+constexpr size_t kGemm2SmemBytes =
+    1024 + kGemm2Stages * kGemm2StageBytes + kGemm2StoreBytes;  // 225 KB
+
+// Work unit u of the pair kernel: a whole 256 x 256 tile, or (in the last,
+// partial wave) one 256 x 128 half of a tile.  Halving the tail tiles lets a
+// wave of R < pairs/2 leftover tiles occupy 2R pairs for half as long.
+struct PairUnit {
+  int m_tile;
+  int col_base;  // first output column
+  int width;     // 256 or 128 columns
+};
+
+__device__ __forceinline__ PairUnit pair_unit(const GemmArgs& args, int u) {
+  int tile = u;
+  int half = -1;
+  if (u >= args.full_units) {
+    const int h = u - args.full_units;
+    tile = args.full_units + (h >> 1);
+    half = h & 1;
+  }
+  const int m_tile = tile / args.num_n_tiles;
+  const int n_tile = tile - m_tile * args.num_n_tiles;
+  PairUnit unit;
+  unit.m_tile = m_tile;
+  unit.col_base = n_tile * kGemm2BN + (half > 0 ? kGemm2BN / 2 : 0);
+  unit.width = half >= 0 ? kGemm2BN / 2 : kGemm2BN;
+  return unit;
+}
 
 template <int EPI, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tn_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                             const __grid_constant__ CUtensorMap tmap_w, GemmArgs args) {
+                             const __grid_constant__ CUtensorMap tmap_w,
+                             const __grid_constant__ CUtensorMap tmap_out, GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[kGemm2Stages];
   __shared__ uint64_t empty_bar[kGemm2Stages];
@@ -329,7 +364,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
-  __shared__ float bias_tile[8][kGemm2BN / 2];
 
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* smem_a = smem;
@@ -341,12 +375,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int num_pairs = static_cast<int>(gridDim.x >> 1);
-  const int num_tiles = args.num_m_tiles * args.num_n_tiles;  // pair tiles (256 x 256)
+  const int num_units = args.num_units;  // pair tiles (256 x 256) and tail halves (256 x 128)
   const int num_kb = (args.K + kGemmBK - 1) / kGemmBK;
 
   if (threadIdx.x == 0) {
     prefetch_tensor_map(&tmap_a);
     prefetch_tensor_map(&tmap_w);
+    if constexpr (std::is_same<OutT, __nv_bfloat16>::value) prefetch_tensor_map(&tmap_out);
     for (int s = 0; s < kGemm2Stages; ++s) {
       mbar_init(&full_bar[s], 1);  // the leader's arrive.expect_tx
       mbar_init(&empty_bar[s], 1);
@@ -376,13 +411,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       const uint32_t full_leader_base = peer_smem_addr(&full_bar[0], 0);
-      for (int tile = pair; tile < num_tiles && !abort_flag; tile += num_pairs) {
-        const int m_tile = tile / args.num_n_tiles;
-        const int n_tile = tile - m_tile * args.num_n_tiles;
+      for (int u = pair; u < num_units && !abort_flag; u += num_pairs) {
+        const PairUnit unit = pair_unit(args, u);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, kErrGemmProducerWait, &abort_flag)) break;
-          const int a_row = m_tile * kGemm2BM + static_cast<int>(rank) * 128;
-          const int w_row = n_tile * kGemm2BN + static_cast<int>(rank) * 128;
+          const int a_row = unit.m_tile * kGemm2BM + static_cast<int>(rank) * 128;
+          // A half-width unit uses the first 64 of the 128 W rows loaded.
+          const int w_row = unit.col_base + static_cast<int>(rank) * (unit.width / 2);
           if (leader) {
             mbar_arrive_expect_tx(&full_bar[stage], 2 * kGemm2StageBytes);
             tma_load_2d(smem_a + stage * kGemm2TileABytes, &tmap_a, &full_bar[stage], kb * kGemmBK, a_row);
@@ -415,12 +450,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (leader && elect_one()) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kGemm2BM, kGemm2BN, false, false);
+      constexpr uint32_t idesc_full = umma_idesc_bf16(kGemm2BM, kGemm2BN, false, false);
+      constexpr uint32_t idesc_half = umma_idesc_bf16(kGemm2BM, kGemm2BN / 2, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
       bool issued_any = false;
-      for (int tile = pair; tile < num_tiles && !abort_flag; tile += num_pairs, ++t) {
+      for (int u = pair; u < num_units && !abort_flag; u += num_pairs, ++t) {
+        const uint32_t idesc = u < args.full_units ? idesc_full : idesc_half;
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (!mbar_wait(&acc_empty_bar[acc], acc_phase ^ 1u, kErrGemmMmaWait, &abort_flag)) break;
@@ -462,68 +499,89 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
     const uint32_t acc_empty_leader0 = peer_smem_addr(&acc_empty_bar[0], 0);
     const uint32_t acc_empty_leader1 = peer_smem_addr(&acc_empty_bar[1], 0);
+    // bf16 outputs leave through shared memory and TMA stores: this warp's two
+    // staging boxes alternate, one store group per 32 x 32 chunk.
+    uint8_t* const stage_out = smem + kGemm2Stages * kGemm2StageBytes + (warp - 2) * 2 * kGemm2StoreBoxBytes;
+    uint32_t store_seq = 0;
     int t = 0;
-    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
+    for (int u = pair; u < num_units; u += num_pairs, ++t) {
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
-      const int m_tile = tile / args.num_n_tiles;
-      const int n_tile = tile - m_tile * args.num_n_tiles;
-      float* warp_bias = bias_tile[warp - 2];
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int col = n_tile * kGemm2BN + col_half * (kGemm2BN / 2) + i * 32 + lane;
-        warp_bias[i * 32 + lane] = (args.bias != nullptr && col < args.N) ? __ldg(args.bias + col) : 0.f;
-      }
-      __syncwarp();
+      const PairUnit unit = pair_unit(args, u);
+      const int m_tile = unit.m_tile;
       bool ok = mbar_wait(&acc_full_bar[acc], acc_phase, kErrGemmEpilogueWait, &abort_flag);
       if (__any_sync(0xffffffffu, !ok)) break;
       __syncwarp();
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(m_tile) * kGemm2BM + row_in_tile;
+      const int row_base = m_tile * kGemm2BM + static_cast<int>(rank) * 128 + quarter * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             acc * kGemm2BN + col_half * (kGemm2BN / 2);
-      constexpr int kChunks = kGemm2BN / 2 / 32;
+                             acc * kGemm2BN + col_half * (unit.width / 2);
+      constexpr int kMaxChunks = kGemm2BN / 2 / 32;
+      const int chunks = unit.width / 2 / 32;
       uint32_t buf[2][32];
       tmem_ld_32cols(taddr, buf[0]);
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        if (c + 1 < kChunks) tmem_ld_32cols(taddr + (c + 1) * 32, buf[(c + 1) & 1]);
+      for (int c = 0; c < kMaxChunks; ++c) {
+        if (c >= chunks) break;
+        if (c + 1 < chunks) tmem_ld_32cols(taddr + (c + 1) * 32, buf[(c + 1) & 1]);
         const uint32_t (&r)[32] = buf[c & 1];
-        const int col0 = n_tile * kGemm2BN + col_half * (kGemm2BN / 2) + c * 32;
+        const int col0 = unit.col_base + col_half * (unit.width / 2) + c * 32;
+        // N % 8 == 0 (checked on the host): each group of eight columns is
+        // either entirely inside the matrix or entirely past its edge.
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + warp_bias[c * 32 + i];
+        for (int i = 0; i < 32; ++i) {
+          const float b = (args.bias != nullptr && col0 + (i & ~7) < args.N) ? __ldg(args.bias + col0 + i) : 0.f;
+          v[i] = __uint_as_float(r[i]) + b;
+        }
         if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
         }
-        if (row < args.M) {
-          OutT* out_row = static_cast<OutT*>(args.out) + row * args.N + col0;
-          if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+        if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+          // The store that last read this staging box (two groups ago) is done.
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* const box = stage_out + (store_seq & 1u) * kGemm2StoreBoxBytes;
+          const uint32_t row_addr = smem_u32(box) + static_cast<uint32_t>(lane) * 64u;
+          const uint32_t swz = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              if (col0 + i < args.N)
-                st_global_v4(out_row + i, pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
-                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
-            }
-          } else {
+          for (int j = 0; j < 4; ++j) {
+            st_shared_v4(row_addr + ((static_cast<uint32_t>(j) ^ swz) << 4), pack_bf16x2(v[8 * j], v[8 * j + 1]),
+                         pack_bf16x2(v[8 * j + 2], v[8 * j + 3]), pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                         pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row_base < args.M && col0 < args.N) tma_store_2d(&tmap_out, box, col0, row_base);
+            bulk_commit_group();
+          }
+          ++store_seq;
+        } else if (row < args.M) {
+          float* out_row = static_cast<float*>(args.out) + row * args.N + col0;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              if (col0 + i < args.N)
-                st_global_v4(out_row + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]),
-                             __float_as_uint(v[i + 2]), __float_as_uint(v[i + 3]));
-            }
+          for (int i = 0; i < 32; i += 4) {
+            if (col0 + i < args.N)
+              st_global_v4(out_row + i, __float_as_uint(v[i]), __float_as_uint(v[i + 1]), __float_as_uint(v[i + 2]),
+                           __float_as_uint(v[i + 3]));
           }
         }
-        if (c + 1 < kChunks) tmem_wait_ld();
+        if (c + 1 < chunks) tmem_wait_ld();
       }
       // This warp has read its columns of the accumulator: one arrival on the
       // leader's barrier (remote for the peer CTA).
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
+    }
+    // No store may still read the staging boxes (or be unperformed) when the
+    // CTA leaves.
+    if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+      if (lane == 0) bulk_wait_group_all();
+      __syncwarp();
     }
   }
 
