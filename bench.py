@@ -364,6 +364,24 @@ def run_gpu(args: argparse.Namespace) -> None:
         # Per-kernel times for the kernel table and the roofline: the same
         # steps again with CUDA events around every launch (these events sit
         # between kernels, so this pass is not the step time).
+        # A graph runtime replays its launches where the events cannot sit, so
+        # this pass runs the same program with the eager runtime.
+        from dataclasses import replace as _replace
+
+        from solution.config import RuntimeBackend
+
+        graph_config = None
+        if runner is model and model.active_config.schedule.runtime in (
+            RuntimeBackend.CUDA_GRAPH,
+            RuntimeBackend.BATCH_TILED_CUDA_GRAPH,
+        ):
+            graph_config = model.active_config
+            model.configure_execution(
+                config=_replace(
+                    graph_config,
+                    schedule=_replace(graph_config.schedule, runtime=RuntimeBackend.EAGER, batch_tile_size=None),
+                )
+            )
         recorder = KernelEventRecorder()
         if runner is model:
             model.kernel_events = recorder
@@ -374,6 +392,8 @@ def run_gpu(args: argparse.Namespace) -> None:
         torch.cuda.synchronize()
         model.kernel_events = None
         kernel_ms = recorder.durations_ms()
+        if graph_config is not None:
+            model.configure_execution(config=graph_config)
 
         # End to end through the public host-batch API (HostPipeline) from
         # pinned host memory: every step copies its input H2D, runs the
@@ -552,6 +572,7 @@ def run_kernel(args: argparse.Namespace) -> None:
             "attention": _native.ATTN_QUAD,
             "attention_paired": _native.ATTN_PAIRED,
             "attention_single": _native.ATTN_SINGLE,
+            "attention_persistent": _native.ATTN_PERSISTENT,
         }[args.kernel]
         launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
         work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
@@ -629,6 +650,7 @@ def main() -> None:
             "attention",
             "attention_paired",
             "attention_single",
+            "attention_persistent",
             "qkv",
             "out_proj",
             "ffn_in",

@@ -18,6 +18,7 @@
 #include <utility>
 
 #include "attention_kernels.cuh"
+#include "attention_persistent.cuh"
 #include "attention_simt_kernels.cuh"
 #include "gemm_kernels.cuh"
 #include "norm_kernels.cuh"
@@ -50,7 +51,7 @@ struct DeviceState {
   int cc_major = 0;
   int cc_minor = 0;
   bool gemm_attr[8] = {false, false, false, false, false, false, false, false};
-  bool attn_attr[4] = {false, false, false, false};  // variants 0-2, masked quad
+  bool attn_attr[6] = {};  // variants 0-3, then the masked quad (4) and masked persistent (5) builds
 };
 
 std::mutex g_mutex;
@@ -467,19 +468,22 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   if (head_dim != b200tx::kAttnDh)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: head_dim %lld (only 64 is built)",
                 (long long)head_dim);
-  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE && variant != B200TX_ATTN_QUAD)
+  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE && variant != B200TX_ATTN_QUAD &&
+      variant != B200TX_ATTN_PERSISTENT)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: variant %d", variant);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
-  if (key_valid != nullptr && variant != B200TX_ATTN_QUAD)
+  if (key_valid != nullptr && variant != B200TX_ATTN_QUAD && variant != B200TX_ATTN_PERSISTENT)
     return fail(B200TX_ERR_UNSUPPORTED,
-                "attention: padding masks are built into the QUAD variant only (variant %d)",
+                "attention: padding masks are built into the QUAD and PERSISTENT variants only "
+                "(variant %d)",
                 variant);
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
   const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
-  const int64_t units = variant == B200TX_ATTN_PAIRED ? (q_tiles + 1) / 2
-                        : variant == B200TX_ATTN_QUAD ? (q_tiles + 3) / 4
-                                                      : q_tiles;
+  const int64_t units = variant == B200TX_ATTN_PAIRED       ? (q_tiles + 1) / 2
+                        : variant == B200TX_ATTN_QUAD       ? (q_tiles + 3) / 4
+                        : variant == B200TX_ATTN_PERSISTENT ? (q_tiles + 1) / 2
+                                                            : q_tiles;
   const int64_t blocks = units * heads * batch;
   if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: problem too large for one launch");
@@ -507,6 +511,35 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   args.num_q_tiles = static_cast<int>(q_tiles);
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
+  if (variant == B200TX_ATTN_PERSISTENT) {
+    CUtensorMap map_kv;
+    const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(3 * d_model) * 2,
+                                 static_cast<uint64_t>(3 * d_model) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t box[3] = {b200tx::kAttnDh, b200tx::kAttnPBN, 1};
+    rc = encode_bf16_map(&map_kv, qkv, 3, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+    using PersistFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
+    const PersistFn kernel = key_valid != nullptr ? b200tx::attention_fwd_dh64_persistent_kernel<true>
+                                                  : b200tx::attention_fwd_dh64_persistent_kernel<false>;
+    const int attr_slot = key_valid != nullptr ? 5 : variant;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (!dev->attn_attr[attr_slot]) {
+        cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(b200tx::kAttnPSmemBytes));
+        if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
+        dev->attn_attr[attr_slot] = true;
+      }
+    }
+    // Persistent: at most one CTA per SM walks the work items.
+    const int64_t grid = blocks < dev->sm_count ? blocks : dev->sm_count;
+    cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(b200tx::kAttnPThreads),
+                             b200tx::kAttnPSmemBytes, stream, map_qkv, map_kv, args);
+    if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+    return B200TX_OK;
+  }
   if (variant == B200TX_ATTN_QUAD) {
     CUtensorMap map_kv;
     const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),
@@ -519,7 +552,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     using QuadFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
     const QuadFn quad_kernel = key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true>
                                                     : b200tx::attention_fwd_dh64_quad_kernel<false>;
-    const int attr_slot = key_valid != nullptr ? 3 : variant;
+    const int attr_slot = key_valid != nullptr ? 4 : variant;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
       if (!dev->attn_attr[attr_slot]) {

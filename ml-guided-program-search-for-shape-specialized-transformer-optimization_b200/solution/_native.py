@@ -26,6 +26,7 @@ GEMM_PAIR = 1
 ATTN_PAIRED = 0
 ATTN_SINGLE = 1
 ATTN_QUAD = 2
+ATTN_PERSISTENT = 3
 MASK_DROP_UPDATE = 1
 MASK_ZERO_RESIDUAL = 2
 MASK_ZERO_NORMED = 4
@@ -507,6 +508,7 @@ __all__ = [
     "residual_layer_norm_peer",
     "ABI_VERSION",
     "ATTN_PAIRED",
+    "ATTN_PERSISTENT",
     "ATTN_QUAD",
     "ATTN_SINGLE",
     "BF16",

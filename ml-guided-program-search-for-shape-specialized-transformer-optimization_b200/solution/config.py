@@ -161,7 +161,9 @@ SM100_GEMM_VARIANTS = frozenset(SM100_GEMM_VARIANT_CODES)
 #   (256, 128, 3): two 128-row query tiles per CTA, P kept in TMEM (B200TX_ATTN_PAIRED)
 #   (128, 128, 3): one query tile per CTA, P staged through shared memory (B200TX_ATTN_SINGLE)
 #   (512, 64, 6):  four query tiles per CTA, 64-row KV tiles, P in TMEM (B200TX_ATTN_QUAD)
-SM100_ATTENTION_VARIANTS = {(256, 128, 3): 0, (128, 128, 3): 1, (512, 64, 6): 2}
+#   (256, 64, 8):  persistent grid, two query tiles per work item, double-buffered
+#                  scores, 8-slot KV rings (B200TX_ATTN_PERSISTENT)
+SM100_ATTENTION_VARIANTS = {(256, 128, 3): 0, (128, 128, 3): 1, (512, 64, 6): 2, (256, 64, 8): 3}
 SM100_NORM_ROWS_PER_CTA = frozenset({8})
 
 
@@ -226,7 +228,7 @@ class Sm100AttentionParams:
 
     @property
     def kernel_variant(self) -> int:
-        """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE)."""
+        """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE / _QUAD / _PERSISTENT)."""
 
         return SM100_ATTENTION_VARIANTS[(self.block_m, self.block_n, self.kv_stages)]
 

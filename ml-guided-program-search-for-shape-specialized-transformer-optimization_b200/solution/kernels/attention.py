@@ -78,7 +78,10 @@ def sm100_flash_attention(
             and tuple(key_valid.shape) == (batch, seq),
             "key_valid must be a contiguous uint8 [B, S] tensor on the qkv device",
         )
-        require(variant == _native.ATTN_QUAD, "padding masks are built into the QUAD variant only")
+        require(
+            variant in (_native.ATTN_QUAD, _native.ATTN_PERSISTENT),
+            "padding masks are built into the QUAD and PERSISTENT variants only",
+        )
     launch(
         _native.attention,
         qkv,

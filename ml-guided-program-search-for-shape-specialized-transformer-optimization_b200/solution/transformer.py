@@ -336,7 +336,11 @@ class UserOptimizedTransformer(nn.Module):
             if value is None
             else tuple(value.shape)
         )
-        signature = (device.type, device.index, dtype, shape)
+        # Training and autograd state are part of the key: a deployed config
+        # rejected while the module was still in training mode (at .to(),
+        # before .eval()) is resolved again for the inference forward.
+        grad = torch.is_grad_enabled() if value is not None else False
+        signature = (device.type, device.index, dtype, shape, self.training, grad)
         if signature == self._deployment_signature:
             return
         from .shape14.defaults import default_streamed_config, is_streamed_shape

@@ -183,7 +183,7 @@ def test_structured_rejections(overrides: dict, hardware: HardwareCapabilities, 
         result.require_plan()
 
 
-def test_padding_masks_need_the_quad_attention_variant() -> None:
+def test_padding_masks_need_a_mask_reading_attention_variant() -> None:
     masked = _context(has_valid_token_mask=True)
     plan = PlanBuilder().build(portable_config(), masked, B200)
     assert plan.describe()["valid_token_mask"] == "direct_key_mask"
@@ -196,6 +196,13 @@ def test_padding_masks_need_the_quad_attention_variant() -> None:
     assert PlanBuilder().evaluate(paired, _context(), B200).accepted
     result = PlanBuilder().evaluate(paired, masked, B200)
     assert "mask_not_supported" in _codes(result)
+    persistent = ConfigSpec(
+        program=default_program(),
+        schedule=replace(
+            default_schedule(), attention_launch=Sm100AttentionParams(block_m=256, block_n=64, kv_stages=8)
+        ),
+    )
+    assert PlanBuilder().evaluate(persistent, masked, B200).accepted
 
 
 def test_runtime_rules() -> None:

@@ -168,7 +168,7 @@ def test_linear_three_dimensional_input() -> None:
     assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
 
 
-VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD]
+VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT]
 
 
 def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, variant: int) -> None:
@@ -225,13 +225,21 @@ def test_attention_is_deterministic(variant: int) -> None:
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize(("batch", "seq", "heads", "causal"), [(8, 1024, 16, True), (4, 640, 40, False)])
+def test_attention_persistent_many_items_per_cta(batch: int, seq: int, heads: int, causal: bool) -> None:
+    """More work items than 2x the SM count: each CTA of the persistent kernel
+    walks several items, its barrier phases and Q buffers carried across them."""
+
+    _attention_case(batch, seq, heads, causal, seed=seq + heads, variant=_native.ATTN_PERSISTENT)
+
+
 @pytest.mark.parametrize("causal", [True, False])
 def test_attention_variants_agree(causal: bool) -> None:
     g = torch.Generator().manual_seed(13)
     qkv = torch.randn(3, 1000, 3 * 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
     with torch.inference_mode():
         a, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=_native.ATTN_PAIRED)
-        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD):
+        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT):
             b, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=other)
             max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
             # Two bf16 results of different summation orders: a few bf16 ulps apart.
@@ -282,9 +290,13 @@ def _masked_attention_reference(
         (3, 257, 2, False, "right"),
         (2, 1000, 2, True, "one_empty_row"),
         (1, 129, 1, False, "random"),
+        (8, 768, 16, True, "random"),  # several work items per persistent CTA
     ],
 )
-def test_attention_key_padding_mask(batch: int, seq: int, heads: int, causal: bool, pattern: str) -> None:
+@pytest.mark.parametrize("variant", [_native.ATTN_QUAD, _native.ATTN_PERSISTENT])
+def test_attention_key_padding_mask(
+    batch: int, seq: int, heads: int, causal: bool, pattern: str, variant: int
+) -> None:
     g = torch.Generator().manual_seed(seq + heads)
     qkv = torch.randn(batch, seq, 3 * heads * 64, generator=g).to(torch.bfloat16)
     if pattern == "random":
@@ -301,7 +313,7 @@ def test_attention_key_padding_mask(batch: int, seq: int, heads: int, causal: bo
     ref = ref.transpose(0, 2, 1, 3).reshape(batch, seq, heads * 64)
     key_valid = valid.to(DEV).view(torch.uint8)
     with torch.inference_mode():
-        out, _ = sm100_flash_attention(qkv.to(DEV), heads, causal=causal, key_valid=key_valid)
+        out, _ = sm100_flash_attention(qkv.to(DEV), heads, causal=causal, key_valid=key_valid, variant=variant)
     got = _bf16_np(out)
     assert np.isfinite(got).all()
     max_abs, rel = parity_errors(got, ref)
@@ -310,13 +322,14 @@ def test_attention_key_padding_mask(batch: int, seq: int, heads: int, causal: bo
         assert not got[1].any()
 
 
-def test_attention_all_valid_mask_equals_unmasked() -> None:
+@pytest.mark.parametrize("variant", [_native.ATTN_QUAD, _native.ATTN_PERSISTENT])
+def test_attention_all_valid_mask_equals_unmasked(variant: int) -> None:
     g = torch.Generator().manual_seed(21)
     qkv = torch.randn(2, 700, 3 * 4 * 64, generator=g).to(torch.bfloat16).to(DEV)
     ones = torch.ones(2, 700, dtype=torch.uint8, device=DEV)
     with torch.inference_mode():
-        a, _ = sm100_flash_attention(qkv, 4)
-        b, _ = sm100_flash_attention(qkv, 4, key_valid=ones)
+        a, _ = sm100_flash_attention(qkv, 4, variant=variant)
+        b, _ = sm100_flash_attention(qkv, 4, key_valid=ones, variant=variant)
     assert torch.equal(a, b)
 
 

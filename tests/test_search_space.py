@@ -4,7 +4,7 @@ CPU tests check the space against the plan builder the reference's autotune
 loop uses (reference autotune/search_space.py:1589-1693): every branch has an
 accepted witness, config_at/index_for are inverse, every enumerated config
 round-trips through ConfigSpec JSON, the portable branch is always present,
-and a masked context keeps only the quad attention variant.  The GPU test
+and a masked context keeps only the attention variants that read masks.  The GPU test
 sweeps a small shape exhaustively and checks that every candidate matches
 the portable program and that the winner publishes into a registry file the
 model then resolves.
@@ -62,8 +62,8 @@ def test_resident_space_has_every_structure_and_the_portable_branch() -> None:
     portable = space.branch_for(portable_config())
     assert portable is not None and portable.structure.portable
     assert portable.branch_id in space.mandatory_branch_ids
-    # 3 attention variants x 2^4 GEMM variants
-    assert portable.cardinality == 3 * 16
+    # 4 attention variants x 2^4 GEMM variants
+    assert portable.cardinality == 4 * 16
     assert space.cardinality == sum(b.cardinality for b in space.branches)
 
 
@@ -104,11 +104,12 @@ def test_streamed_scope_offers_microbatches() -> None:
     assert micro.choices == (1, 2, 4, 8)
 
 
-def test_masked_context_keeps_only_the_quad_attention() -> None:
+def test_masked_context_keeps_only_the_mask_reading_attention() -> None:
     space = _space(has_valid_token_mask=True)
     tiles = {branch.parameters_for(c).get("attention_tile") for branch in space.branches for c in branch.configs()
              if space.accepted(c)}
-    assert tiles == {"512x64x6", None}  # the quad kernel, or the CUDA-core kernel (no tile)
+    # the quad and persistent kernels, or the CUDA-core kernel (no tile)
+    assert tiles == {"512x64x6", "256x64x8", None}
 
 
 def test_other_head_dims_search_only_the_cuda_core_attention() -> None:
