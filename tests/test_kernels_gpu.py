@@ -225,7 +225,9 @@ def test_attention_is_deterministic(variant: int) -> None:
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize(("batch", "seq", "heads", "causal"), [(8, 1024, 16, True), (4, 640, 40, False)])
+@pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal"), [(8, 1024, 16, True), (4, 640, 40, False), (8, 2048, 8, True), (3, 1000, 20, True)]
+)
 def test_attention_persistent_many_items_per_cta(batch: int, seq: int, heads: int, causal: bool) -> None:
     """More work items than 2x the SM count: each CTA of the persistent kernel
     walks several items, its barrier phases and Q buffers carried across them."""
