@@ -76,6 +76,40 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return x >= 0.0f ? x - h : -h;
 }
 
+// gelu_erf on two values with the packed f32x2 FMA/MUL pipes: the same
+// operations in the same order (each lane of a packed op is one IEEE fp32
+// operation), so the results equal gelu_erf bit for bit, with about a third
+// fewer issued instructions.  The reciprocal and exp2 stay per value on MUFU.
+__device__ __forceinline__ void gelu_erf_x2(float& x0, float& x1) {
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f;
+  constexpr float kA2 = -0.284496736f;
+  constexpr float kA3 = 1.421413741f;
+  constexpr float kA4 = -1.453152027f;
+  constexpr float kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const uint64_t ax = f32x2(fabsf(x0), fabsf(x1));
+  const uint64_t z = mul_f32x2(ax, f32x2(kInvSqrt2, kInvSqrt2));
+  const float2 d = unpack_f32x2(fma_f32x2(f32x2(kP, kP), z, f32x2(1.0f, 1.0f)));
+  float t0, t1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(d.y));
+  const uint64_t t = f32x2(t0, t1);
+  uint64_t q = fma_f32x2(f32x2(kA5, kA5), t, f32x2(kA4, kA4));
+  q = fma_f32x2(q, t, f32x2(kA3, kA3));
+  q = fma_f32x2(q, t, f32x2(kA2, kA2));
+  q = fma_f32x2(q, t, f32x2(kA1, kA1));
+  const uint64_t poly = mul_f32x2(t, q);
+  const uint64_t zz = mul_f32x2(z, z);
+  const float2 arg = unpack_f32x2(mul_f32x2(f32x2(-unpack_f32x2(zz).x, -unpack_f32x2(zz).y), f32x2(kLog2e, kLog2e)));
+  const uint64_t e = f32x2(fast_exp2(arg.x), fast_exp2(arg.y));
+  const uint64_t half_ax = mul_f32x2(f32x2(0.5f, 0.5f), ax);
+  const float2 h = unpack_f32x2(mul_f32x2(mul_f32x2(half_ax, poly), e));
+  x0 = x0 >= 0.0f ? x0 - h.x : -h.x;
+  x1 = x1 >= 0.0f ? x1 - h.y : -h.y;
+}
+
 template <int EPI, typename OutT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -251,7 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + warp_bias[c * 32 + i];
         if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          for (int i = 0; i < 32; i += 2) gelu_erf_x2(v[i], v[i + 1]);
         }
         if (row < args.M) {
           // N % 8 == 0 (checked on the host): each group of eight columns is
@@ -538,7 +572,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         }
         if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          for (int i = 0; i < 32; i += 2) gelu_erf_x2(v[i], v[i + 1]);
         }
         if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
           // The store that last read this staging box (two groups ago) is done.
