@@ -359,6 +359,7 @@ int linear_impl(const void* a, const void* w, const float* bias, void* out, int 
   }
   b200tx::GemmArgs args;
   args.bias = bias;
+  args.bias_vec4 = (bias != nullptr && aligned16(bias)) ? 1 : 0;
   args.out = out;
   args.M = static_cast<int>(M);
   args.N = static_cast<int>(N);

@@ -49,6 +49,7 @@ struct GemmArgs {
   // Pair kernel only: work units are the first `full_units` tiles, then the
   // remaining tiles each split into two 128-column halves (num_units in all).
   int full_units, num_units;
+  int bias_vec4;  // bias is 16-byte aligned: whole 32-column chunks read it as float4
 };
 
 // Exact-erf GELU, 0.5 x (1 + erf(x / sqrt 2)), with erf from Abramowitz &
@@ -565,10 +566,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         // N % 8 == 0 (checked on the host): each group of eight columns is
         // either entirely inside the matrix or entirely past its edge.
         float v[32];
+        if (args.bias_vec4 && col0 + 32 <= args.N) {
+          // Eight broadcast 16-byte loads (every lane reads the same columns).
+          const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float b = (args.bias != nullptr && col0 + (i & ~7) < args.N) ? __ldg(args.bias + col0 + i) : 0.f;
-          v[i] = __uint_as_float(r[i]) + b;
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 bb = __ldg(b4 + q4);
+            v[4 * q4 + 0] = __uint_as_float(r[4 * q4 + 0]) + bb.x;
+            v[4 * q4 + 1] = __uint_as_float(r[4 * q4 + 1]) + bb.y;
+            v[4 * q4 + 2] = __uint_as_float(r[4 * q4 + 2]) + bb.z;
+            v[4 * q4 + 3] = __uint_as_float(r[4 * q4 + 3]) + bb.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float b = (args.bias != nullptr && col0 + (i & ~7) < args.N) ? __ldg(args.bias + col0 + i) : 0.f;
+            v[i] = __uint_as_float(r[i]) + b;
+          }
         }
         if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll

@@ -157,6 +157,22 @@ def test_linear_variants_agree_bitwise() -> None:
     assert rel < 1e-3, rel
 
 
+def test_linear_bias_not_16_byte_aligned() -> None:
+    """A bias view one float into its storage takes the per-column load path."""
+
+    g = torch.Generator().manual_seed(4)
+    a = torch.randn(300, 512, generator=g).to(torch.bfloat16)
+    w = (torch.randn(1024, 512, generator=g) / 16).to(torch.bfloat16)
+    storage = torch.randn(1025, generator=g)
+    b = storage[1:]
+    ref = a.float().numpy() @ w.float().numpy().T + b.numpy()
+    with torch.inference_mode():
+        bias_dev = storage.to(DEV)[1:]
+        assert bias_dev.data_ptr() % 16 != 0
+        out, _ = sm100_linear(a.to(DEV), w.to(DEV), bias_dev, out_dtype=torch.float32)
+    assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
+
+
 def test_linear_three_dimensional_input() -> None:
     g = torch.Generator().manual_seed(1)
     a = torch.randn(3, 50, 256, generator=g).to(torch.bfloat16)
