@@ -81,10 +81,18 @@ def _peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+# Committed ncu summary of each kernel role at C2 (profiles/<name>_c2.txt).
+PROFILE_OF_ROLE = {
+    "attention": "attention",
+    "ffn_input_projection": "gemm_ffn_in_gelu",
+    "residual_norm": "residual_layernorm",
+}
+
+
 def _profile_traffic(kernel: str) -> float | None:
     """DRAM bytes per launch from the committed ncu summary, if any."""
 
-    path = REPO / "profiles" / f"{kernel}_c2.txt"
+    path = REPO / "profiles" / f"{PROFILE_OF_ROLE.get(kernel, kernel)}_c2.txt"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
