@@ -581,6 +581,7 @@ def run_kernel(args: argparse.Namespace) -> None:
             "attention_paired": _native.ATTN_PAIRED,
             "attention_single": _native.ATTN_SINGLE,
             "attention_persistent": _native.ATTN_PERSISTENT,
+            "attention_duo": _native.ATTN_DUO,
         }[args.kernel]
         launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
         work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
@@ -659,6 +660,7 @@ def main() -> None:
             "attention_paired",
             "attention_single",
             "attention_persistent",
+            "attention_duo",
             "qkv",
             "out_proj",
             "ffn_in",

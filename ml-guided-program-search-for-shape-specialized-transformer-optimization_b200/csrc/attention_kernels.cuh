@@ -690,23 +690,39 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 // of the other three, so the MUFU pipe, not latency, bounds the kernel.
 // TMEM (512 columns): S_w/P_w at 64w .. 64w+63 (P packed into the first 32),
 // O_w at 256 + 64w .. +63.
+//
+// Duo variant: the same kernel with two query tiles per CTA (320 threads,
+// 256 TMEM columns, 4-slot KV rings, 97 KB shared memory), so that two CTAs
+// share an SM. The four tiles in flight then belong to two independent CTAs:
+// one CTA's prologue, epilogue and causal tail (tiles that end before the
+// CTA's longest one) overlap the other's main loop, at the cost of loading
+// each K/V tile for two query tiles instead of four.
 // ---------------------------------------------------------------------------
-constexpr int kAttn4Tiles = 4;
 constexpr int kAttn4BN = 64;
-constexpr int kAttn4Ring = 6;
-constexpr int kAttn4Threads = 64 + kAttn4Tiles * 128;
-constexpr uint32_t kAttn4TmemCols = 512;
 constexpr uint32_t kAttn4KvBytes = kAttn4BN * kAttnDh * 2;  // 8 KB
-constexpr size_t kAttn4SmemBytes =
-    1024 + kAttn4Tiles * kAttnTileBytes + 2 * kAttn4Ring * kAttn4KvBytes;  // 161 KB
 constexpr float kAttn4MaxSlack = 8.0f;
 
+template <int kTiles>
+struct QuadShape {
+  static_assert(kTiles == 2 || kTiles == 4, "two or four query tiles per CTA");
+  static constexpr int kRing = kTiles == 4 ? 6 : 4;
+  static constexpr int kThreads = 64 + kTiles * 128;
+  static constexpr int kCtasPerSm = 4 / kTiles;
+  static constexpr uint32_t kTmemCols = kTiles * 128;
+  static constexpr size_t kSmemBytes =
+      1024 + kTiles * kAttnTileBytes + 2 * kRing * kAttn4KvBytes;  // 161 KB / 97 KB
+};
+
 // kMasked: the build that reads args.key_valid (padding masks); the unmasked
-// build carries none of that code.
-template <bool kMasked>
-__global__ void __launch_bounds__(kAttn4Threads, 1)
+// build carries none of that code. kTiles: query tiles per CTA (4 = QUAD,
+// 2 = DUO).
+template <bool kMasked, int kTiles>
+__global__ void __launch_bounds__(QuadShape<kTiles>::kThreads, QuadShape<kTiles>::kCtasPerSm)
     attention_fwd_dh64_quad_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                    const __grid_constant__ CUtensorMap tmap_kv, AttnArgs args) {
+  constexpr int kAttn4Tiles = kTiles;
+  constexpr int kAttn4Ring = QuadShape<kTiles>::kRing;
+  constexpr uint32_t kAttn4TmemCols = QuadShape<kTiles>::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full_bar;
   __shared__ uint64_t k_full_bar[kAttn4Ring];

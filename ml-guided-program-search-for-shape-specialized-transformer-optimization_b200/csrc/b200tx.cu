@@ -45,13 +45,16 @@ int cuda_fail(cudaError_t err, const char* what) {
   return fail(B200TX_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
 }
 
+// Attention variant codes run 0 .. kAttnVariants-1 (B200TX_ATTN_*).
+constexpr int kAttnVariants = 5;
+
 struct DeviceState {
   bool probed = false;
   int sm_count = 0;
   int cc_major = 0;
   int cc_minor = 0;
   bool gemm_attr[8] = {false, false, false, false, false, false, false, false};
-  bool attn_attr[6] = {};  // variants 0-3, then the masked quad (4) and masked persistent (5) builds
+  bool attn_attr[2 * kAttnVariants] = {};  // unmasked builds by variant, then the masked builds
 };
 
 std::mutex g_mutex;
@@ -469,14 +472,14 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   if (head_dim != b200tx::kAttnDh)
     return fail(B200TX_ERR_UNSUPPORTED, "attention: head_dim %lld (only 64 is built)",
                 (long long)head_dim);
-  if (variant != B200TX_ATTN_PAIRED && variant != B200TX_ATTN_SINGLE && variant != B200TX_ATTN_QUAD &&
-      variant != B200TX_ATTN_PERSISTENT)
+  if (variant < 0 || variant >= kAttnVariants)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: variant %d", variant);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
-  if (key_valid != nullptr && variant != B200TX_ATTN_QUAD && variant != B200TX_ATTN_PERSISTENT)
+  if (key_valid != nullptr && variant != B200TX_ATTN_QUAD && variant != B200TX_ATTN_PERSISTENT &&
+      variant != B200TX_ATTN_DUO)
     return fail(B200TX_ERR_UNSUPPORTED,
-                "attention: padding masks are built into the QUAD and PERSISTENT variants only "
+                "attention: padding masks are built into the QUAD, DUO and PERSISTENT variants only "
                 "(variant %d)",
                 variant);
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
@@ -484,6 +487,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   const int64_t units = variant == B200TX_ATTN_PAIRED       ? (q_tiles + 1) / 2
                         : variant == B200TX_ATTN_QUAD       ? (q_tiles + 3) / 4
                         : variant == B200TX_ATTN_PERSISTENT ? (q_tiles + 1) / 2
+                        : variant == B200TX_ATTN_DUO        ? (q_tiles + 1) / 2
                                                             : q_tiles;
   const int64_t blocks = units * heads * batch;
   if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
@@ -524,7 +528,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     using PersistFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
     const PersistFn kernel = key_valid != nullptr ? b200tx::attention_fwd_dh64_persistent_kernel<true>
                                                   : b200tx::attention_fwd_dh64_persistent_kernel<false>;
-    const int attr_slot = key_valid != nullptr ? 5 : variant;
+    const int attr_slot = key_valid != nullptr ? kAttnVariants + variant : variant;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
       if (!dev->attn_attr[attr_slot]) {
@@ -541,7 +545,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
   }
-  if (variant == B200TX_ATTN_QUAD) {
+  if (variant == B200TX_ATTN_QUAD || variant == B200TX_ATTN_DUO) {
     CUtensorMap map_kv;
     const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),
                               static_cast<uint64_t>(batch)};
@@ -551,21 +555,27 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     rc = encode_bf16_map(&map_kv, qkv, 3, dims, strides, box);
     if (rc != B200TX_OK) return rc;
     using QuadFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
-    const QuadFn quad_kernel = key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true>
-                                                    : b200tx::attention_fwd_dh64_quad_kernel<false>;
-    const int attr_slot = key_valid != nullptr ? 4 : variant;
+    const bool duo = variant == B200TX_ATTN_DUO;
+    const QuadFn quad_kernel =
+        duo ? (key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true, 2>
+                                    : b200tx::attention_fwd_dh64_quad_kernel<false, 2>)
+            : (key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true, 4>
+                                    : b200tx::attention_fwd_dh64_quad_kernel<false, 4>);
+    const size_t smem = duo ? b200tx::QuadShape<2>::kSmemBytes : b200tx::QuadShape<4>::kSmemBytes;
+    const int threads = duo ? b200tx::QuadShape<2>::kThreads : b200tx::QuadShape<4>::kThreads;
+    const int attr_slot = key_valid != nullptr ? kAttnVariants + variant : variant;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
       if (!dev->attn_attr[attr_slot]) {
         cudaError_t err = cudaFuncSetAttribute(quad_kernel,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(b200tx::kAttn4SmemBytes));
+                                               static_cast<int>(smem));
         if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
         dev->attn_attr[attr_slot] = true;
       }
     }
-    cudaError_t err = launch(quad_kernel, dim3(static_cast<unsigned>(blocks)), dim3(b200tx::kAttn4Threads),
-                             b200tx::kAttn4SmemBytes, stream, map_qkv, map_kv, args);
+    cudaError_t err = launch(quad_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), smem,
+                             stream, map_qkv, map_kv, args);
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
   }

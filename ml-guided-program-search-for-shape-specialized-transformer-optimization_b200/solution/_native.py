@@ -27,6 +27,7 @@ ATTN_PAIRED = 0
 ATTN_SINGLE = 1
 ATTN_QUAD = 2
 ATTN_PERSISTENT = 3
+ATTN_DUO = 4
 MASK_DROP_UPDATE = 1
 MASK_ZERO_RESIDUAL = 2
 MASK_ZERO_NORMED = 4
@@ -507,6 +508,7 @@ __all__ = [
     "peer_signal",
     "residual_layer_norm_peer",
     "ABI_VERSION",
+    "ATTN_DUO",
     "ATTN_PAIRED",
     "ATTN_PERSISTENT",
     "ATTN_QUAD",

@@ -163,7 +163,15 @@ SM100_GEMM_VARIANTS = frozenset(SM100_GEMM_VARIANT_CODES)
 #   (512, 64, 6):  four query tiles per CTA, 64-row KV tiles, P in TMEM (B200TX_ATTN_QUAD)
 #   (256, 64, 8):  persistent grid, two query tiles per work item, double-buffered
 #                  scores, 8-slot KV rings (B200TX_ATTN_PERSISTENT)
-SM100_ATTENTION_VARIANTS = {(256, 128, 3): 0, (128, 128, 3): 1, (512, 64, 6): 2, (256, 64, 8): 3}
+#   (256, 64, 4):  two query tiles per CTA, 64-row KV tiles, 4-slot KV rings, two CTAs
+#                  per SM (B200TX_ATTN_DUO)
+SM100_ATTENTION_VARIANTS = {
+    (256, 128, 3): 0,
+    (128, 128, 3): 1,
+    (512, 64, 6): 2,
+    (256, 64, 8): 3,
+    (256, 64, 4): 4,
+}
 SM100_NORM_ROWS_PER_CTA = frozenset({8})
 
 
@@ -228,7 +236,7 @@ class Sm100AttentionParams:
 
     @property
     def kernel_variant(self) -> int:
-        """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE / _QUAD / _PERSISTENT)."""
+        """The libb200tx attention variant code (B200TX_ATTN_PAIRED / _SINGLE / _QUAD / _PERSISTENT / _DUO)."""
 
         return SM100_ATTENTION_VARIANTS[(self.block_m, self.block_n, self.kv_stages)]
 

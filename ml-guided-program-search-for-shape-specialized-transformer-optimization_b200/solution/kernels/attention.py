@@ -51,8 +51,9 @@ def sm100_flash_attention(
     key_valid: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, str]:
     """``softmax(q k^T / 8 [+ causal] [+ key padding]) v`` per head; returns
-    the ``[B, S, D]`` context.  With ``key_valid`` only the QUAD variant is
-    built; a query that sees no valid key gets a zero row."""
+    the ``[B, S, D]`` context.  With ``key_valid`` the QUAD, DUO and
+    PERSISTENT variants are built; a query that sees no valid key gets a zero
+    row."""
 
     if not can_use_sm100_flash_attention(qkv, num_heads):
         raise RuntimeError("sm100 flash attention is ineligible for the requested inputs")
@@ -79,8 +80,8 @@ def sm100_flash_attention(
             "key_valid must be a contiguous uint8 [B, S] tensor on the qkv device",
         )
         require(
-            variant in (_native.ATTN_QUAD, _native.ATTN_PERSISTENT),
-            "padding masks are built into the QUAD and PERSISTENT variants only",
+            variant in (_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO),
+            "padding masks are built into the QUAD, PERSISTENT and DUO variants only",
         )
     launch(
         _native.attention,

@@ -34,10 +34,10 @@ Reject = Callable[[str, str, str], None]
 SUPPORTED_HEAD_DIMS = frozenset({64})
 # Head dims built into the CUDA-core attention (b200tx_attention_generic).
 SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
-# The attention variants that read a key padding mask (B200TX_ATTN_QUAD and
-# B200TX_ATTN_PERSISTENT).
+# The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
+# B200TX_ATTN_PERSISTENT and B200TX_ATTN_DUO).
 SM100_QUAD_ATTENTION_VARIANT = 2
-SM100_MASKED_ATTENTION_VARIANTS = frozenset({2, 3})
+SM100_MASKED_ATTENTION_VARIANTS = frozenset({2, 3, 4})
 SUPPORTED_IO_DTYPES = frozenset({torch.float32, torch.bfloat16})
 _INT32_MAX = 2**31 - 1
 
@@ -283,8 +283,8 @@ class PlanBuilder:
             reject(
                 "mask_not_supported",
                 "schedule.attention_launch",
-                "padding masks are built into the quad (block_m 512, block_n 64, kv_stages 6) "
-                "and persistent (256, 64, 8) attention variants only",
+                "padding masks are built into the quad (block_m 512, block_n 64, kv_stages 6), "
+                "persistent (256, 64, 8) and duo (256, 64, 4) attention variants only",
             )
         if config.program.attention is AttentionBackend.SM100_FLASH:
             if head_dim is not None and head_dim not in SUPPORTED_HEAD_DIMS:

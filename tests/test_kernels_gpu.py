@@ -184,7 +184,8 @@ def test_linear_three_dimensional_input() -> None:
     assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
 
 
-VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT]
+VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO]
+MASKED_VARIANTS = [_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO]
 
 
 def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, variant: int) -> None:
@@ -251,13 +252,23 @@ def test_attention_persistent_many_items_per_cta(batch: int, seq: int, heads: in
     _attention_case(batch, seq, heads, causal, seed=seq + heads, variant=_native.ATTN_PERSISTENT)
 
 
+@pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal"), [(8, 2048, 16, True), (4, 640, 40, False), (16, 512, 12, True)]
+)
+def test_attention_duo_two_ctas_per_sm(batch: int, seq: int, heads: int, causal: bool) -> None:
+    """More CTAs than 2x the SM count: two DUO CTAs share each SM's TMEM and
+    shared memory, and CTAs of short and long causal pairs interleave."""
+
+    _attention_case(batch, seq, heads, causal, seed=seq + 3 * heads, variant=_native.ATTN_DUO)
+
+
 @pytest.mark.parametrize("causal", [True, False])
 def test_attention_variants_agree(causal: bool) -> None:
     g = torch.Generator().manual_seed(13)
     qkv = torch.randn(3, 1000, 3 * 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
     with torch.inference_mode():
         a, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=_native.ATTN_PAIRED)
-        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT):
+        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO):
             b, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=other)
             max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
             # Two bf16 results of different summation orders: a few bf16 ulps apart.
@@ -311,7 +322,7 @@ def _masked_attention_reference(
         (8, 768, 16, True, "random"),  # several work items per persistent CTA
     ],
 )
-@pytest.mark.parametrize("variant", [_native.ATTN_QUAD, _native.ATTN_PERSISTENT])
+@pytest.mark.parametrize("variant", MASKED_VARIANTS)
 def test_attention_key_padding_mask(
     batch: int, seq: int, heads: int, causal: bool, pattern: str, variant: int
 ) -> None:
@@ -340,7 +351,7 @@ def test_attention_key_padding_mask(
         assert not got[1].any()
 
 
-@pytest.mark.parametrize("variant", [_native.ATTN_QUAD, _native.ATTN_PERSISTENT])
+@pytest.mark.parametrize("variant", MASKED_VARIANTS)
 def test_attention_all_valid_mask_equals_unmasked(variant: int) -> None:
     g = torch.Generator().manual_seed(21)
     qkv = torch.randn(2, 700, 3 * 4 * 64, generator=g).to(torch.bfloat16).to(DEV)

@@ -62,8 +62,8 @@ def test_resident_space_has_every_structure_and_the_portable_branch() -> None:
     portable = space.branch_for(portable_config())
     assert portable is not None and portable.structure.portable
     assert portable.branch_id in space.mandatory_branch_ids
-    # 4 attention variants x 2^4 GEMM variants
-    assert portable.cardinality == 4 * 16
+    # 5 attention variants x 2^4 GEMM variants
+    assert portable.cardinality == 5 * 16
     assert space.cardinality == sum(b.cardinality for b in space.branches)
 
 
@@ -108,8 +108,8 @@ def test_masked_context_keeps_only_the_mask_reading_attention() -> None:
     space = _space(has_valid_token_mask=True)
     tiles = {branch.parameters_for(c).get("attention_tile") for branch in space.branches for c in branch.configs()
              if space.accepted(c)}
-    # the quad and persistent kernels, or the CUDA-core kernel (no tile)
-    assert tiles == {"512x64x6", "256x64x8", None}
+    # the quad, persistent and duo kernels, or the CUDA-core kernel (no tile)
+    assert tiles == {"512x64x6", "256x64x8", "256x64x4", None}
 
 
 def test_other_head_dims_search_only_the_cuda_core_attention() -> None:
