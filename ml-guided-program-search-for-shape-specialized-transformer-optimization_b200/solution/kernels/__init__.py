@@ -37,6 +37,7 @@ from .projection import (
     sm100_linear,
     sm100_linear_available,
 )
+from . import ops  # noqa: E402 - registers the torch.ops.b200tx.* operators
 
 __all__ = [
     "MASK_DROP_UPDATE",
@@ -60,4 +61,5 @@ __all__ = [
     "sm100_linear",
     "sm100_linear_available",
     "sm100_residual_layer_norm",
+    "ops",
 ]
