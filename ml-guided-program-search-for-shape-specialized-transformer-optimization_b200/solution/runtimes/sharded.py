@@ -44,6 +44,7 @@ from ..kernels import (
     sm100_linear,
     sm100_residual_layer_norm,
 )
+from .liveness import StepLiveness
 
 HEAD_DIM = 64
 
@@ -266,6 +267,7 @@ class TensorParallelTransformer:
         group: object | None = None,
         partial_dtype: torch.dtype = torch.float32,
         reduction: str = "nccl",
+        liveness: StepLiveness | None = None,
     ) -> None:
         import torch.distributed as dist
 
@@ -276,6 +278,7 @@ class TensorParallelTransformer:
         if reduction not in ("nccl", "peer"):
             raise ValueError("reduction must be 'nccl' or 'peer'")
         self.reduction = reduction
+        self.liveness = liveness
         self._peer: PeerReduction | None = None
         self.group = group
         self.rank = dist.get_rank(group)
@@ -348,6 +351,10 @@ class TensorParallelTransformer:
 
         if x.device != self.device or not x.is_contiguous() or x.dim() != 3:
             raise ValueError("x must be a contiguous [B, S, D] tensor on this rank's GPU")
+        if self.liveness is not None:
+            # Every rank of the group is alive at this step boundary, or
+            # RankFailure is raised before anything of this step is launched.
+            self.liveness.enter()
         batch, seq, d_model = x.shape
         rows = batch * seq
         d_local = d_model // self.world

@@ -161,8 +161,15 @@ def _nccl_worker(
         model = UserOptimizedTransformer(SimpleNamespace(**cfg.__dict__))
         copy_model_weights(official_state_dict(cfg, seed=0), model)
         model = model.to(f"cuda:{rank}").eval()
+        from solution.runtimes.liveness import StepLiveness
+
+        # Every forward passes the host-side liveness check of the group first.
+        live = StepLiveness(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=60.0)
         tp = TensorParallelTransformer(
-            model, partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32, reduction=reduction
+            model,
+            partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32,
+            reduction=reduction,
+            liveness=live,
         )
         x = official_input(cfg, 5).to(f"cuda:{rank}")
         y_tp = tp(x)
