@@ -452,7 +452,14 @@ def run_gpu(args: argparse.Namespace) -> None:
         "ffn_input_projection": layers * 2.0 * m * f * d * heads_frac,
         "ffn_output_projection": layers * 2.0 * m * d * f * heads_frac,
     }
-    bytes_per_step = {"residual_norm": 2 * layers * 12.0 * m * d, "initial_norm": 6.0 * m * d}
+    # Residual LN: read r (fp32) + u (bf16), write r (fp32) + n (bf16) = 12 B per
+    # element; the last one writes no residual and the output in the input's
+    # dtype: 4 + 2 + out bytes.  Initial LN: read x, write bf16 n.
+    io_bytes = float(x_dev.element_size())
+    bytes_per_step = {
+        "residual_norm": ((2 * layers - 1) * 12.0 + 6.0 + io_bytes) * m * d,
+        "initial_norm": (io_bytes + 2.0) * m * d,
+    }
     per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
     launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
     roofline = None

@@ -91,7 +91,8 @@ def sm100_residual_layer_norm(
     normalized_out: torch.Tensor | None = None,
     row_valid: torch.Tensor | None = None,
     mask_mode: int = 0,
-) -> tuple[torch.Tensor, torch.Tensor, str]:
+    keep_residual: bool = True,
+) -> tuple[torch.Tensor | None, torch.Tensor, str]:
     """``r = value + update`` (fp32) and ``LN(r)``.
 
     The normalised output is bf16 for an inner boundary and fp32 at the final
@@ -99,6 +100,9 @@ def sm100_residual_layer_norm(
     dtype there).  ``residual_out`` may be ``value`` itself for an in-place
     update of an fp32 residual stream.  ``row_valid`` / ``mask_mode`` apply
     the padding-mask behaviours (MASK_* bits) to rows whose flag is 0.
+    With ``keep_residual=False`` the sum is not written at all (the block's
+    last boundary, whose residual nobody reads: 4 bytes per element less
+    traffic) and the returned residual is ``None``.
     """
 
     if not can_use_sm100_residual_layer_norm(value, update, layer_norm):
@@ -106,18 +110,22 @@ def sm100_residual_layer_norm(
     if out_dtype is None:
         out_dtype = torch.float32 if final_boundary else torch.bfloat16
     require(out_dtype in _IO, "out_dtype must be float32 or bfloat16")
-    residual = (
-        torch.empty(value.shape, dtype=torch.float32, device=value.device)
-        if residual_out is None
-        else residual_out
-    )
+    if not keep_residual:
+        require(residual_out is None, "residual_out is given but keep_residual is False")
+        residual = None
+    elif residual_out is None:
+        residual = torch.empty(value.shape, dtype=torch.float32, device=value.device)
+    else:
+        residual = residual_out
     normalized = (
         torch.empty(value.shape, dtype=out_dtype, device=value.device)
         if normalized_out is None
         else normalized_out
     )
-    require(residual.shape == value.shape and residual.dtype == torch.float32, "bad residual_out")
-    require(residual.is_contiguous() and normalized.is_contiguous(), "outputs must be contiguous")
+    if residual is not None:
+        require(residual.shape == value.shape and residual.dtype == torch.float32, "bad residual_out")
+        require(residual.is_contiguous(), "residual_out must be contiguous")
+    require(normalized.is_contiguous(), "normalized_out must be contiguous")
     require(
         normalized.shape == value.shape and normalized.dtype == out_dtype,
         f"normalized_out must be {out_dtype} of shape {tuple(value.shape)}",

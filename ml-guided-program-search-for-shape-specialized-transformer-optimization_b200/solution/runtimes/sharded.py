@@ -396,7 +396,8 @@ class TensorParallelTransformer:
                 self._all_reduce(partial)
                 sm100_residual_layer_norm(
                     residual_in, partial, norm, final_boundary=last, out_dtype=out_dtype,
-                    residual_out=residual, normalized_out=normalized_out,
+                    residual_out=None if last else residual, keep_residual=not last,
+                    normalized_out=normalized_out,
                 )
                 return
             if not can_use_sm100_linear(a, w, b):

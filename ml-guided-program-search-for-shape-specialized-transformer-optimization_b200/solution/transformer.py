@@ -706,7 +706,8 @@ class UserOptimizedTransformer(nn.Module):
                 next_norm.kernel_norm(),
                 final_boundary=last,
                 out_dtype=value.dtype if last else torch.bfloat16,
-                residual_out=residual,
+                residual_out=None if last else residual,
+                keep_residual=not last,
                 normalized_out=output.view(rows, d_model) if last else normalized,
                 row_valid=row_valid,
                 mask_mode=MASK_ZERO_RESIDUAL | (MASK_ZERO_NORMED if last else 0),
