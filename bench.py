@@ -24,6 +24,10 @@ rank's time.
 ``--kernel NAME`` times one libb200tx kernel alone on its C2-shaped operands
                (attention, qkv, out_proj, ffn_in, ffn_out, residual_norm) and
                prints its own JSON line; ncu profiles in profiles/ use this mode.
+``--workload official`` times the reference's own benchmark table (its 14
+               official shapes) under the eager and CUDA-graph schedules and
+               prints one JSON line with the reference's published medians
+               beside each shape.
 """
 
 from __future__ import annotations
@@ -247,12 +251,12 @@ def run_reference(args: argparse.Namespace) -> None:
 
 # ---------------------------------------------------------------- GPU arm
 def build_model(device: torch.device, spec: dict | None = None):
-    from oracle import OfficialConfig, official_state_dict
     from solution.transformer import UserOptimizedTransformer, copy_model_weights
+    from workloads import WorkloadConfig, seeded_state_dict
 
     spec = spec or WORKLOAD
     model = UserOptimizedTransformer(SimpleNamespace(**spec))
-    copy_model_weights(official_state_dict(OfficialConfig(**spec), seed=WEIGHT_SEED), model)
+    copy_model_weights(seeded_state_dict(WorkloadConfig(**spec), seed=WEIGHT_SEED), model)
     return model.to(device).eval()
 
 
@@ -271,26 +275,25 @@ def _c4_tp(args: argparse.Namespace, batch: int, world: int) -> int:
 def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, world: int):
     """This rank's input rows and the parallel mode of the workload."""
 
-    from oracle import OfficialConfig, official_input
-    from oracle.weights import per_row_input
     from solution.runtimes.sharded import batch_shard_bounds
+    from workloads import WorkloadConfig, seeded_input, seeded_row
 
-    cfg = OfficialConfig(**spec)
+    cfg = WorkloadConfig(**spec)
     if args.workload == "c4" and world > 1:
         # Head-sharded tensor parallel over groups of --tp ranks; the
         # world // tp replicas split the batch rows between them.
         tp = _c4_tp(args, cfg.batch_size, world)
         start, stop = batch_shard_bounds(cfg.batch_size, rank // tp, world // tp)
-        x = official_input(cfg, seed)[start:stop].contiguous()
+        x = seeded_input(cfg, seed)[start:stop].contiguous()
         return x, "heads", "strong", cfg.batch_size * cfg.seq_len
     if args.workload == "c5":
         # Batch-sharded capacity run: the 32 rows (seed 4 + row) split over ranks.
         start, stop = batch_shard_bounds(cfg.batch_size, rank, world)
-        rows = [per_row_input(cfg, seed, r) for r in range(start, stop)]
+        rows = [seeded_row(cfg, seed, r) for r in range(start, stop)]
         x = torch.cat(rows, dim=0)
         return x, "batch", "strong", cfg.batch_size * cfg.seq_len
     # c2 / c3: every rank runs its own full batch (rank r: seed + r).
-    return official_input(cfg, seed + rank), "batch", "weak", world * cfg.batch_size * cfg.seq_len
+    return seeded_input(cfg, seed + rank), "batch", "weak", world * cfg.batch_size * cfg.seq_len
 
 
 def run_gpu(args: argparse.Namespace) -> None:
@@ -310,14 +313,14 @@ def run_gpu(args: argparse.Namespace) -> None:
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         dist = dist_mod
 
-    from oracle import OfficialConfig
     from solution import _native
     from solution.runtimes.sharded import TensorParallelTransformer
     from solution.transformer import KernelEventRecorder
+    from workloads import WorkloadConfig
 
     _native.device_check()
     spec, seed, workload_name = WORKLOADS[args.workload]
-    cfg = OfficialConfig(**spec)
+    cfg = WorkloadConfig(**spec)
     model = build_model(device, spec)
     x_cpu, parallel, scaling, total_tokens = _workload_input(args, spec, seed, rank, world)
     tp = 1
@@ -643,6 +646,118 @@ def run_kernel(args: argparse.Namespace) -> None:
     }), flush=True)
 
 
+def run_official(args: argparse.Namespace) -> None:
+    """The reference's headline table on one B200: its official shapes.
+
+    The reference publishes, per official shape, the median forward latency
+    of its deployed program and of the official PyTorch baseline on one
+    RTX 4080 (fp32 I/O; workloads.REFERENCE_PUBLISHED_MS).  This mode runs the
+    same shapes (fp32 input from seed 0, weights from seed 0) through
+    ``UserOptimizedTransformer`` with its default eager config and with the
+    CUDA-graph schedule, each forward bracketed by CUDA events after an L2
+    flush, and reports the median of each schedule beside the published
+    numbers.  official_14 (B32 S100000, the streamed capacity shape) runs its
+    default streamed config with at most 2 timed forwards.
+    """
+
+    from solution import _native
+    from solution.config import (
+        ConfigSpec,
+        RuntimeBackend,
+        default_attention,
+        default_program,
+        default_schedule,
+    )
+    from workloads import OFFICIAL_SHAPES, REFERENCE_PUBLISHED_MS, seeded_input, seeded_row
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    _native.device_check()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    cases = args.cases.split(",") if args.cases else sorted(OFFICIAL_SHAPES)
+
+    def median_ms(model, x, warmup: int, steps: int) -> float:  # noqa: ANN001
+        with torch.inference_mode():
+            for _ in range(warmup):
+                model(x)
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(steps):
+                flush.zero_()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                model(x)
+                end.record()
+                torch.cuda.synchronize()
+                times.append(start.elapsed_time(end))
+        return statistics.median(times)
+
+    shapes: dict[str, dict] = {}
+    with ClockSampler(0) as clocks:
+        for case in cases:
+            cfg = OFFICIAL_SHAPES[case]
+            streamed = case == "official_14"
+            if streamed:
+                x_cpu = torch.cat([seeded_row(cfg, 0, r) for r in range(cfg.batch_size)])
+            else:
+                x_cpu = seeded_input(cfg, 0)
+            x = x_cpu.to(device)
+            del x_cpu
+            model = build_model(device, cfg.as_dict())
+            warmup, steps = (1, min(2, args.steps)) if streamed else (max(3, args.warmup), args.steps)
+            row: dict = {"B": cfg.batch_size, "S": cfg.seq_len, "D": cfg.d_model, "H": cfg.num_heads,
+                         "F": cfg.ffn_dim, "L": cfg.num_layers}
+            row["eager_ms"] = median_ms(model, x, warmup, steps)
+            row["eager_runtime"] = model.active_config.schedule.runtime.value
+            if not streamed:
+                attention = default_attention(cfg.d_model // cfg.num_heads)
+                model.configure_execution(config=ConfigSpec(
+                    program=default_program(attention=attention),
+                    schedule=default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention),
+                ))
+                row["graph_ms"] = median_ms(model, x, warmup, steps)
+            row["attention"] = model.active_config.program.attention.value
+            best = min(v for k, v in row.items() if k.endswith("_ms"))
+            ref_deployed, ref_baseline = REFERENCE_PUBLISHED_MS[case]
+            row.update(
+                best_ms=best,
+                tokens_per_s=cfg.tokens / (best / 1000.0),
+                ref_rtx4080_deployed_ms=ref_deployed,
+                ref_rtx4080_pytorch_ms=ref_baseline,
+                speedup_vs_ref_deployed=ref_deployed / best,
+            )
+            if ref_baseline is not None:
+                row["speedup_vs_ref_pytorch"] = ref_baseline / best
+            shapes[case] = row
+            del model, x
+            torch.cuda.empty_cache()
+    if _native.device_error() != 0:
+        raise SystemExit("a kernel wait timed out")
+
+    def geomean(values: list[float]) -> float | None:
+        return math.exp(sum(math.log(v) for v in values) / len(values)) if values else None
+
+    core = [c for c in shapes if c != "official_14"]
+    print(json.dumps({
+        "metric": "official shapes: fwd median latency per shape",
+        "unit": "ms",
+        "higher_is_better": False,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "dtype": "bf16",
+        "data": "synthetic (seeded x ~ N(0,1), seeded default-init weights)",
+        "config": {"workload": "reference official shapes (official/test_shapes.json)", "io": "float32",
+                   "l2": "flushed before every timed forward"},
+        "reference_platform": "RTX 4080, published (result/20260831T083857.848038Z/final_performance.md)",
+        "geomean_speedup_vs_ref_deployed_01_13": geomean([shapes[c]["speedup_vs_ref_deployed"] for c in core]),
+        "geomean_speedup_vs_ref_pytorch_01_13": geomean([shapes[c]["speedup_vs_ref_pytorch"] for c in core]),
+        "shapes": shapes,
+        "clocks": clocks.summary(),
+    }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -650,8 +765,11 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="c2",
-                        help="BASELINE config to run (c2 is the bench line the driver records)")
+    parser.add_argument("--workload", choices=[*sorted(WORKLOADS), "official"], default="c2",
+                        help="BASELINE config to run (c2 is the bench line the driver records), "
+                             "or 'official' for the reference's official-shapes table")
+    parser.add_argument("--cases", default=None,
+                        help="--workload official: comma-separated case ids (default: all 14)")
     parser.add_argument("--tp", type=int, default=0,
                         help="c4 under torchrun: tensor-parallel group size (default: max(2, N / B))")
     parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer"), default="auto",
@@ -688,6 +806,9 @@ def main() -> None:
         return
     if args.kernel is not None:
         run_kernel(args)
+        return
+    if args.workload == "official":
+        run_official(args)
         return
     run_gpu(args)
 
