@@ -195,6 +195,20 @@ int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* ou
                              int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
                              cudaStream_t stream);
 
+/*
+ * The same attention as b200tx_attention_generic for head_dim 8, 16 or 32 on
+ * warp-level tensor-core MMAs (mma.sync m16n8k16, bf16 inputs, fp32
+ * accumulation): 64 query rows per CTA, 64-key tiles, P kept in registers.
+ * Same layouts, masks and semantics.  Replaces, for the reference's official
+ * shapes with these head dims (official/test_shapes.json: 8 and 32), its
+ * small-head kernels solution/kernels/attention/triton_dh8.py:72-260 and
+ * solution/kernels/attention/triton_s1024_dh32.py:72-366, and the SDPA
+ * operators solution/operators/attention/sdpa.py:76-170.
+ */
+int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                         int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                         cudaStream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tensor-parallel reduction over NVLink peer memory.  The reference is
  * single-GPU; these entry points implement the head-sharded runtime's

@@ -18,6 +18,7 @@
 #include <utility>
 
 #include "attention_kernels.cuh"
+#include "attention_mma_kernels.cuh"
 #include "attention_persistent.cuh"
 #include "attention_simt_kernels.cuh"
 #include "gemm_kernels.cuh"
@@ -791,6 +792,50 @@ int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* ou
     default: err = launch(b200tx::attention_simt_kernel<256>, grid, block, 0, stream, a); break;
   }
   if (err != cudaSuccess) return cuda_fail(err, "attention_generic launch");
+  return B200TX_OK;
+}
+
+int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
+                         int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
+                         cudaStream_t stream) {
+  if (qkv == nullptr || out == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: null tensor pointer");
+  if (batch <= 0 || seq <= 0 || heads <= 0)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: bad shape B=%lld S=%lld H=%lld",
+                (long long)batch, (long long)seq, (long long)heads);
+  if (head_dim != 8 && head_dim != 16 && head_dim != 32)
+    return fail(B200TX_ERR_UNSUPPORTED, "attention_mma: head_dim %lld (built: 8, 16, 32)",
+                (long long)head_dim);
+  if (!aligned16(qkv) || !aligned16(out))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: operands must be 16-byte aligned");
+  if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: scale must be > 0");
+  const int64_t q_blocks = (seq + b200tx::kMmaAttnRows - 1) / b200tx::kMmaAttnRows;
+  const int64_t blocks = q_blocks * heads * batch;
+  if (blocks > 0x7fffffffLL || batch * heads > 0x7fffffffLL ||
+      batch * seq * heads * head_dim * 3 > (1LL << 62))
+    return fail(B200TX_ERR_UNSUPPORTED, "attention_mma: problem too large for one launch");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  b200tx::MmaAttnArgs a;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.key_valid = key_valid;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.batch = static_cast<int>(batch);
+  a.seq = static_cast<int>(seq);
+  a.heads = static_cast<int>(heads);
+  a.q_blocks = static_cast<int>(q_blocks);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.causal = causal ? 1 : 0;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const dim3 block(b200tx::kMmaAttnThreads);
+  cudaError_t err;
+  switch (head_dim) {
+    case 8: err = launch(b200tx::attention_mma_kernel<8>, grid, block, 0, stream, a); break;
+    case 16: err = launch(b200tx::attention_mma_kernel<16>, grid, block, 0, stream, a); break;
+    default: err = launch(b200tx::attention_mma_kernel<32>, grid, block, 0, stream, a); break;
+  }
+  if (err != cudaSuccess) return cuda_fail(err, "attention_mma launch");
   return B200TX_OK;
 }
 

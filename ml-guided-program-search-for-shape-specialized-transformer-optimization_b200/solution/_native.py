@@ -182,6 +182,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_int,  # causal
         _c_void_p,  # stream
     ]
+    lib.b200tx_attention_mma.restype = ctypes.c_int
+    lib.b200tx_attention_mma.argtypes = list(lib.b200tx_attention_generic.argtypes)
     lib.b200tx_attention_masked.restype = ctypes.c_int
     lib.b200tx_attention_masked.argtypes = [
         _c_void_p,  # qkv
@@ -388,6 +390,37 @@ def attention(
             qkv.data_ptr(), key_valid.data_ptr(), out.data_ptr(), *shape, _stream(qkv.device)
         ),
         "b200tx_attention_masked",
+    )
+
+
+def attention_mma(
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    batch: int,
+    seq: int,
+    heads: int,
+    head_dim: int,
+    scale: float,
+    causal: bool,
+    key_valid: torch.Tensor | None = None,
+) -> None:
+    """Launch b200tx_attention_mma (warp-level tensor-core attention, head_dim 8, 16, 32)."""
+
+    lib = load()
+    _check(
+        lib.b200tx_attention_mma(
+            qkv.data_ptr(),
+            None if key_valid is None else key_valid.data_ptr(),
+            out.data_ptr(),
+            int(batch),
+            int(seq),
+            int(heads),
+            int(head_dim),
+            float(scale),
+            int(bool(causal)),
+            _stream(qkv.device),
+        ),
+        "b200tx_attention_mma",
     )
 
 

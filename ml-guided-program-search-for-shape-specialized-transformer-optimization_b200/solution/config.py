@@ -33,6 +33,9 @@ class AttentionBackend(StrEnum):
     # dims the tensor-core kernels do not build; csrc/attention_simt_kernels.cuh),
     # same packed [B,S,3D] input and [B,S,D] output.
     SM100_SIMT = "sm100_simt"
+    # Flash attention for head_dim 8, 16 and 32 on warp-level tensor-core MMAs
+    # (mma.sync m16n8k16; csrc/attention_mma_kernels.cuh), same input and output.
+    SM100_MMA = "sm100_mma"
 
 
 class ProjectionBackend(StrEnum):
@@ -319,7 +322,7 @@ class ProgramConfig:
         # The packed-BSD materialisation is only readable by the sm100 flash
         # kernel, which always writes BSD: keep the pairing explicit so a
         # future variant cannot silently mismatch.
-        sm100_attention = (AttentionBackend.SM100_FLASH, AttentionBackend.SM100_SIMT)
+        sm100_attention = (AttentionBackend.SM100_FLASH, AttentionBackend.SM100_SIMT, AttentionBackend.SM100_MMA)
         if (
             self.qkv_materialization is QKVMaterialization.PACKED_BSD
             and self.attention not in sm100_attention
@@ -586,9 +589,14 @@ def default_schedule(
 
 
 def default_attention(head_dim: int | None) -> AttentionBackend:
-    """The tensor-core kernels for head_dim 64 (or unknown), else the CUDA-core one."""
+    """The tcgen05 kernels for head_dim 64 (or unknown), the warp-MMA kernel for
+    8, 16 and 32, else the CUDA-core one (128, 256)."""
 
-    return AttentionBackend.SM100_FLASH if head_dim in (None, 64) else AttentionBackend.SM100_SIMT
+    if head_dim in (None, 64):
+        return AttentionBackend.SM100_FLASH
+    if head_dim in (8, 16, 32):
+        return AttentionBackend.SM100_MMA
+    return AttentionBackend.SM100_SIMT
 
 
 def portable_config(*, head_dim: int | None = None) -> ConfigSpec:

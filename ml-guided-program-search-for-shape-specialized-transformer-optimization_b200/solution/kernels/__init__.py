@@ -12,6 +12,9 @@ There is no fallback path.
 
 from .attention import (
     SM100_FLASH_ATTENTION_BACKEND,
+    SM100_MMA_ATTENTION_BACKEND,
+    can_use_sm100_mma_attention,
+    sm100_mma_attention,
     SM100_SIMT_ATTENTION_BACKEND,
     can_use_sm100_simt_attention,
     sm100_simt_attention,
@@ -44,6 +47,9 @@ __all__ = [
     "MASK_ZERO_NORMED",
     "MASK_ZERO_RESIDUAL",
     "SM100_FLASH_ATTENTION_BACKEND",
+    "SM100_MMA_ATTENTION_BACKEND",
+    "can_use_sm100_mma_attention",
+    "sm100_mma_attention",
     "SM100_SIMT_ATTENTION_BACKEND",
     "can_use_sm100_simt_attention",
     "sm100_simt_attention",

@@ -170,8 +170,83 @@ def sm100_simt_attention(
     return result, SM100_SIMT_ATTENTION_BACKEND
 
 
+SM100_MMA_ATTENTION_BACKEND = "sm100_mma_attention"
+MMA_HEAD_DIMS = (8, 16, 32)
+
+
+def can_use_sm100_mma_attention(qkv: torch.Tensor, num_heads: int) -> bool:
+    """Whether the warp-MMA attention can read this packed projection (never raises)."""
+
+    try:
+        if not library_ready() or torch.is_grad_enabled() or not is_sm100_cuda(qkv):
+            return False
+        if qkv.dtype != torch.bfloat16 or qkv.ndim != 3 or not qkv.is_contiguous():
+            return False
+        if num_heads <= 0 or qkv.shape[-1] % (3 * num_heads):
+            return False
+        return qkv.shape[-1] // (3 * num_heads) in MMA_HEAD_DIMS and qkv.data_ptr() % 16 == 0
+    except Exception:  # noqa: BLE001 - predicate contract: never raise
+        return False
+
+
+def sm100_mma_attention(
+    qkv: torch.Tensor,
+    num_heads: int,
+    *,
+    causal: bool = True,
+    out: torch.Tensor | None = None,
+    key_valid: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, str]:
+    """The same attention as ``sm100_flash_attention`` for head_dim 8, 16 and 32
+    on warp-level tensor-core MMAs (csrc/attention_mma_kernels.cuh); the
+    reference's official shapes use head dims 8 and 32."""
+
+    if not can_use_sm100_mma_attention(qkv, num_heads):
+        raise RuntimeError("sm100 warp-MMA attention is ineligible for the requested inputs")
+    batch, seq, width = qkv.shape
+    d_model = width // 3
+    head_dim = d_model // num_heads
+    result = (
+        torch.empty((batch, seq, d_model), dtype=torch.bfloat16, device=qkv.device)
+        if out is None
+        else out
+    )
+    require(
+        tuple(result.shape) == (batch, seq, d_model)
+        and result.dtype == torch.bfloat16
+        and result.is_contiguous()
+        and result.data_ptr() % 16 == 0,
+        "out must be a contiguous, 16-byte aligned bf16 [B, S, D] tensor",
+    )
+    if key_valid is not None:
+        require(
+            key_valid.dtype == torch.uint8
+            and key_valid.device == qkv.device
+            and key_valid.is_contiguous()
+            and tuple(key_valid.shape) == (batch, seq),
+            "key_valid must be a contiguous uint8 [B, S] tensor on the qkv device",
+        )
+    launch(
+        _native.attention_mma,
+        qkv,
+        result,
+        batch,
+        seq,
+        num_heads,
+        head_dim,
+        head_dim**-0.5,
+        causal,
+        key_valid,
+    )
+    return result, SM100_MMA_ATTENTION_BACKEND
+
+
 __all__ = [
     "HEAD_DIM",
+    "MMA_HEAD_DIMS",
+    "SM100_MMA_ATTENTION_BACKEND",
+    "can_use_sm100_mma_attention",
+    "sm100_mma_attention",
     "SIMT_HEAD_DIMS",
     "SM100_SIMT_ATTENTION_BACKEND",
     "can_use_sm100_simt_attention",

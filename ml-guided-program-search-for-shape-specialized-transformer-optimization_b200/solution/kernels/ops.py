@@ -10,12 +10,15 @@ under meta and fake tensors (tests/solution/test_triton_shape13_attention.py:
 * ``b200tx::linear``               -- ``sm100_linear`` (bias, optional erf GELU)
 * ``b200tx::flash_attention``      -- ``sm100_flash_attention`` (head_dim 64)
 * ``b200tx::simt_attention``       -- ``sm100_simt_attention`` (head_dim 8..256)
+* ``b200tx::mma_attention``        -- ``sm100_mma_attention`` (head_dim 8, 16, 32)
 * ``b200tx::residual_layer_norm``  -- ``sm100_residual_layer_norm`` (returns
   the fp32 residual and the normalised tensor)
 * ``b200tx::layer_norm``           -- ``sm100_initial_layer_norm``
 
 Each operator is functional: it allocates its outputs and launches on the
-current stream of the inputs' CUDA device.  The fake implementations check
+current stream of the inputs' CUDA device.  The kernels are inference-only
+(no autograd formula is registered); an operator runs them with gradient
+recording off whatever the caller's grad mode is.  The fake implementations check
 the same shape and dtype contract (``ValueError`` on a violation, as the
 wrappers raise) and return empty outputs, so the operators trace under
 ``FakeTensorMode``, meta tensors and ``torch.export`` without a GPU.  A CPU
@@ -33,11 +36,25 @@ from __future__ import annotations
 import torch
 
 from .. import _native
-from .attention import HEAD_DIM, SIMT_HEAD_DIMS, sm100_flash_attention, sm100_simt_attention
+from .attention import (
+    HEAD_DIM,
+    MMA_HEAD_DIMS,
+    SIMT_HEAD_DIMS,
+    sm100_flash_attention,
+    sm100_mma_attention,
+    sm100_simt_attention,
+)
 from .projection import sm100_linear
 
 NAMESPACE = "b200tx"
-OPERATORS = ("linear", "flash_attention", "simt_attention", "residual_layer_norm", "layer_norm")
+OPERATORS = (
+    "linear",
+    "flash_attention",
+    "simt_attention",
+    "mma_attention",
+    "residual_layer_norm",
+    "layer_norm",
+)
 
 _IO = (torch.float32, torch.bfloat16)
 
@@ -87,10 +104,11 @@ def linear(
     """``epilogue(value . weight^T + bias)`` on the tcgen05 GEMM."""
 
     _linear_shape(value, weight, bias, out_dtype)
-    out, _ = sm100_linear(
-        value.contiguous(), weight.contiguous(), bias, gelu=gelu, out_dtype=out_dtype,
-        variant=variant,
-    )
+    with torch.no_grad():
+        out, _ = sm100_linear(
+            value.contiguous(), weight.contiguous(), bias, gelu=gelu, out_dtype=out_dtype,
+            variant=variant,
+        )
     return out
 
 
@@ -133,10 +151,11 @@ def flash_attention(
     on the tensor cores; returns the ``[B, S, D]`` context."""
 
     _attention_shape(qkv, num_heads, key_valid, (HEAD_DIM,))
-    out, _ = sm100_flash_attention(
-        qkv.contiguous(), num_heads, causal=causal, variant=variant,
-        key_valid=None if key_valid is None else key_valid.contiguous(),
-    )
+    with torch.no_grad():
+        out, _ = sm100_flash_attention(
+            qkv.contiguous(), num_heads, causal=causal, variant=variant,
+            key_valid=None if key_valid is None else key_valid.contiguous(),
+        )
     return out
 
 
@@ -159,10 +178,11 @@ def simt_attention(
     """The same attention for head_dim 8..256 on the CUDA cores."""
 
     _attention_shape(qkv, num_heads, key_valid, SIMT_HEAD_DIMS)
-    out, _ = sm100_simt_attention(
-        qkv.contiguous(), num_heads, causal=causal,
-        key_valid=None if key_valid is None else key_valid.contiguous(),
-    )
+    with torch.no_grad():
+        out, _ = sm100_simt_attention(
+            qkv.contiguous(), num_heads, causal=causal,
+            key_valid=None if key_valid is None else key_valid.contiguous(),
+        )
     return out
 
 
@@ -172,6 +192,32 @@ def _simt_attention_fake(qkv, num_heads, causal=True, key_valid=None):  # noqa: 
 
 
 simt_attention.register_kernel("cpu")(_no_cpu("simt_attention"))
+
+
+@torch.library.custom_op(f"{NAMESPACE}::mma_attention", mutates_args=(), device_types="cuda")
+def mma_attention(
+    qkv: torch.Tensor,
+    num_heads: int,
+    causal: bool = True,
+    key_valid: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """The same attention for head_dim 8, 16 and 32 on warp-level tensor-core MMAs."""
+
+    _attention_shape(qkv, num_heads, key_valid, MMA_HEAD_DIMS)
+    with torch.no_grad():
+        out, _ = sm100_mma_attention(
+            qkv.contiguous(), num_heads, causal=causal,
+            key_valid=None if key_valid is None else key_valid.contiguous(),
+        )
+    return out
+
+
+@mma_attention.register_fake
+def _mma_attention_fake(qkv, num_heads, causal=True, key_valid=None):  # noqa: ANN001, ANN202, ARG001
+    return qkv.new_empty(_attention_shape(qkv, num_heads, key_valid, MMA_HEAD_DIMS))
+
+
+mma_attention.register_kernel("cpu")(_no_cpu("mma_attention"))
 
 
 # ---------------------------------------------------------------- LayerNorm
@@ -281,6 +327,7 @@ __all__ = [
     "flash_attention",
     "layer_norm",
     "linear",
+    "mma_attention",
     "residual_layer_norm",
     "simt_attention",
 ]

@@ -34,6 +34,7 @@ Reject = Callable[[str, str, str], None]
 SUPPORTED_HEAD_DIMS = frozenset({64})
 # Head dims built into the CUDA-core attention (b200tx_attention_generic).
 SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
+MMA_HEAD_DIMS = frozenset({8, 16, 32})
 # The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
 # B200TX_ATTN_PERSISTENT and B200TX_ATTN_DUO).
 SM100_QUAD_ATTENTION_VARIANT = 2
@@ -299,6 +300,13 @@ class PlanBuilder:
                     "unsupported_shape",
                     "program.attention",
                     f"sm100 CUDA-core attention is built for head_dim {sorted(SIMT_HEAD_DIMS)}, not {head_dim}",
+                )
+        elif config.program.attention is AttentionBackend.SM100_MMA:
+            if head_dim is not None and head_dim not in MMA_HEAD_DIMS:
+                reject(
+                    "unsupported_shape",
+                    "program.attention",
+                    f"sm100 warp-MMA attention is built for head_dim {sorted(MMA_HEAD_DIMS)}, not {head_dim}",
                 )
         if context.d_model % 8:
             reject(

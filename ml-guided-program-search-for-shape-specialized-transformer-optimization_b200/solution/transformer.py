@@ -35,12 +35,14 @@ from .kernels import (
     MASK_ZERO_NORMED,
     MASK_ZERO_RESIDUAL,
     SM100_FLASH_ATTENTION_BACKEND,
+    SM100_MMA_ATTENTION_BACKEND,
     SM100_SIMT_ATTENTION_BACKEND,
     SM100_INITIAL_LAYER_NORM_BACKEND,
     SM100_LINEAR_BACKEND,
     SM100_LINEAR_GELU_BACKEND,
     SM100_RESIDUAL_LAYER_NORM_BACKEND,
     sm100_flash_attention,
+    sm100_mma_attention,
     sm100_simt_attention,
     sm100_initial_layer_norm,
     sm100_linear,
@@ -555,6 +557,14 @@ class UserOptimizedTransformer(nn.Module):
             plan.attention_launch.kernel_variant if plan.attention_launch is not None else 0
         )
         simt_attention = plan.attention_backend is AttentionBackend.SM100_SIMT
+        mma_attention = plan.attention_backend is AttentionBackend.SM100_MMA
+        attention_marker = (
+            SM100_SIMT_ATTENTION_BACKEND
+            if simt_attention
+            else SM100_MMA_ATTENTION_BACKEND
+            if mma_attention
+            else SM100_FLASH_ATTENTION_BACKEND
+        )
 
         def gemm_variant(launch: Any) -> int:
             return launch.kernel_variant if launch is not None else 1  # the CTA-pair GEMM
@@ -640,6 +650,8 @@ class UserOptimizedTransformer(nn.Module):
             token = rec.start("attention")
             if simt_attention:
                 _, marker = sm100_simt_attention(qkv, heads, causal=causal, out=context, key_valid=key_valid)
+            elif mma_attention:
+                _, marker = sm100_mma_attention(qkv, heads, causal=causal, out=context, key_valid=key_valid)
             else:
                 _, marker = sm100_flash_attention(
                     qkv, heads, causal=causal, out=context, variant=attention_variant, key_valid=key_valid
@@ -647,7 +659,7 @@ class UserOptimizedTransformer(nn.Module):
             rec.stop(token)
             _strict_backend_marker(
                 marker,
-                expected_marker=SM100_SIMT_ATTENTION_BACKEND if simt_attention else SM100_FLASH_ATTENTION_BACKEND,
+                expected_marker=attention_marker,
                 planned_backend=plan.attention_backend.value,
             )
             w_o, b_o = attention.out_proj.shadow_parameters()

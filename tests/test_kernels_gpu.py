@@ -444,6 +444,63 @@ def test_simt_attention_key_padding_mask(head_dim: int) -> None:
     assert rel < 1e-2 and max_abs < 2e-2, (max_abs, rel)
 
 
+# ---------------------------------------------------------------- warp-MMA attention
+@pytest.mark.parametrize("head_dim", [8, 16, 32])
+@pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal"),
+    [(2, 128, 4, True), (1, 300, 2, False), (3, 33, 1, True), (1, 1, 2, True), (2, 1000, 3, True), (1, 65, 1, False)],
+)
+def test_mma_attention_head_dims(head_dim: int, batch: int, seq: int, heads: int, causal: bool) -> None:
+    from solution.kernels import sm100_mma_attention
+
+    g = torch.Generator().manual_seed(head_dim * 11 + seq)
+    qkv = torch.randn(batch, seq, 3 * heads * head_dim, generator=g).to(torch.bfloat16)
+    q, k, v = qkv.float().view(batch, seq, 3, heads, head_dim).permute(2, 0, 3, 1, 4).numpy()
+    ref = attention_core(q, k, v, causal).transpose(0, 2, 1, 3).reshape(batch, seq, heads * head_dim)
+    with torch.inference_mode():
+        out, marker = sm100_mma_attention(qkv.to(DEV), heads, causal=causal)
+    assert marker == "sm100_mma_attention"
+    max_abs, rel = parity_errors(_bf16_np(out), ref)
+    assert rel < 1e-2 and max_abs < 2e-2, (head_dim, max_abs, rel)
+
+
+@pytest.mark.parametrize("head_dim", [8, 32])
+def test_mma_attention_key_padding_mask_and_large_logits(head_dim: int) -> None:
+    from solution.kernels import sm100_mma_attention
+
+    batch, seq, heads = 2, 200, 2
+    g = torch.Generator().manual_seed(head_dim + 5)
+    qkv = torch.randn(batch, seq, 3 * heads * head_dim, generator=g)
+    qkv[..., : heads * head_dim] *= 6.0  # large logits: the running max moves often
+    qkv = qkv.to(torch.bfloat16)
+    valid = torch.rand(batch, seq, generator=g) > 0.3
+    valid[0, :40] = False  # early queries of row 0 see no valid key
+    valid[1, 70:140] = False  # a whole 64-key tile of row 1 is padding
+    q, k, v = qkv.float().view(batch, seq, 3, heads, head_dim).permute(2, 0, 3, 1, 4).numpy()
+    ref = _masked_attention_reference(q, k, v, True, valid.numpy())
+    ref = ref.transpose(0, 2, 1, 3).reshape(batch, seq, heads * head_dim)
+    with torch.inference_mode():
+        out, _ = sm100_mma_attention(qkv.to(DEV), heads, key_valid=valid.to(DEV).view(torch.uint8))
+    got = _bf16_np(out)
+    assert np.isfinite(got).all() and not got[0, :40].any()
+    max_abs, rel = parity_errors(got, ref)
+    assert rel < 1e-2 and max_abs < 2e-2, (max_abs, rel)
+
+
+def test_mma_and_cuda_core_attention_agree_and_are_deterministic() -> None:
+    from solution.kernels import sm100_mma_attention, sm100_simt_attention
+
+    g = torch.Generator().manual_seed(32)
+    qkv = torch.randn(4, 1024, 3 * 4 * 32, generator=g).to(torch.bfloat16).to(DEV)  # official_13 rows
+    with torch.inference_mode():
+        a, _ = sm100_mma_attention(qkv, 4)
+        a2, _ = sm100_mma_attention(qkv, 4)
+        b, _ = sm100_simt_attention(qkv, 4)
+    assert torch.equal(a, a2)
+    max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
+    assert rel < 5e-3 and max_abs < 4e-2, (max_abs, rel)
+
+
 def test_simt_and_tensor_core_attention_agree_at_head_dim_64() -> None:
     from solution.kernels import sm100_simt_attention
 

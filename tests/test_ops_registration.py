@@ -20,6 +20,7 @@ from solution.kernels import (
     ops,
     sm100_flash_attention,
     sm100_linear,
+    sm100_mma_attention,
     sm100_residual_layer_norm,
     sm100_simt_attention,
 )
@@ -52,6 +53,8 @@ def test_operators_trace_on_meta_tensors() -> None:
     assert tuple(ctx.shape) == (2, 10, 128)
     ctx = B200.simt_attention(_meta(3, 17, 3 * 32), 4)  # head_dim 8
     assert tuple(ctx.shape) == (3, 17, 32)
+    ctx = B200.mma_attention(_meta(3, 17, 3 * 128), 4)  # head_dim 32
+    assert tuple(ctx.shape) == (3, 17, 128)
 
     gamma, beta = _meta(768, dtype=torch.float32), _meta(768, dtype=torch.float32)
     r, n = B200.residual_layer_norm(_meta(5, 7, 768, dtype=torch.float32), _meta(5, 7, 768),
@@ -110,6 +113,7 @@ def test_operators_export_as_graph_nodes() -> None:
         (lambda: B200.flash_attention(_meta(2, 8, 3 * 128), 2, True, _native.ATTN_QUAD,
                                       _meta(2, 9, dtype=torch.uint8)), "key_valid"),
         (lambda: B200.simt_attention(_meta(2, 8, 3 * 96), 1), "head_dim 96"),
+        (lambda: B200.mma_attention(_meta(2, 8, 3 * 128), 2), "head_dim 64"),
         (lambda: B200.layer_norm(_meta(4, 64, dtype=torch.float32), _meta(32, dtype=torch.float32),
                                  _meta(32, dtype=torch.float32)), "weight and bias"),
         (lambda: B200.residual_layer_norm(_meta(4, 64, dtype=torch.float32), _meta(4, 32),
@@ -155,7 +159,9 @@ def test_operators_match_the_wrappers_bit_for_bit() -> None:
             want, _ = sm100_flash_attention(qkv, 4, variant=variant)
             got = B200.flash_attention(qkv, 4, True, variant)
             assert torch.equal(got, want)
-        want, _ = sm100_simt_attention(qkv, 8)  # head_dim 32
+        want, _ = sm100_mma_attention(qkv, 8)  # head_dim 32
+        assert torch.equal(B200.mma_attention(qkv, 8), want)
+        want, _ = sm100_simt_attention(qkv, 8)
         assert torch.equal(B200.simt_attention(qkv, 8), want)
 
         ctx = want
@@ -186,6 +192,7 @@ def test_opcheck_on_the_gpu() -> None:
     utils = ("test_schema", "test_faketensor")
     torch.library.opcheck(B200.flash_attention.default, (qkv, 2), test_utils=utils)
     torch.library.opcheck(B200.simt_attention.default, (qkv, 4), test_utils=utils)
+    torch.library.opcheck(B200.mma_attention.default, (qkv, 4), test_utils=utils)
     torch.library.opcheck(B200.linear.default, (ctx, w, bias, True), test_utils=utils)
     torch.library.opcheck(B200.residual_layer_norm.default,
                           (torch.randn(1, 130, 128, device=DEV), ctx, gamma, beta), test_utils=utils)

@@ -112,12 +112,18 @@ def test_masked_context_keeps_only_the_mask_reading_attention() -> None:
     assert tiles == {"512x64x6", "256x64x8", "256x64x4", None}
 
 
-def test_other_head_dims_search_only_the_cuda_core_attention() -> None:
+def test_other_head_dims_search_the_warp_mma_and_cuda_core_attention() -> None:
     from solution.config import AttentionBackend
 
     space = _space(d_model=128, num_heads=4)  # head_dim 32, as the reference's official shapes
-    assert {b.structure.attention for b in space.branches} == {AttentionBackend.SM100_SIMT}
+    assert {b.structure.attention for b in space.branches} == {
+        AttentionBackend.SM100_MMA,
+        AttentionBackend.SM100_SIMT,
+    }
     assert portable_config(head_dim=32) in list(space.configs())
+    assert portable_config(head_dim=32).program.attention is AttentionBackend.SM100_MMA
+    space = _space(d_model=512, num_heads=4)  # head_dim 128: the CUDA-core kernel only
+    assert {b.structure.attention for b in space.branches} == {AttentionBackend.SM100_SIMT}
 
 
 def test_trial_suggestion_and_structure_from_config() -> None:
