@@ -653,17 +653,21 @@ def run_official(args: argparse.Namespace) -> None:
     of its deployed program and of the official PyTorch baseline on one
     RTX 4080 (fp32 I/O; workloads.REFERENCE_PUBLISHED_MS).  This mode runs the
     same shapes (fp32 input from seed 0, weights from seed 0) through
-    ``UserOptimizedTransformer`` with its default eager config and with the
-    CUDA-graph schedule, each forward bracketed by CUDA events after an L2
+    ``UserOptimizedTransformer`` with its default eager config, with the
+    CUDA-graph schedule, and with the CUDA-graph schedule on the small-problem
+    GEMM variant, each forward bracketed by CUDA events after an L2
     flush, and reports the median of each schedule beside the published
     numbers.  official_14 (B32 S100000, the streamed capacity shape) runs its
     default streamed config with at most 2 timed forwards.
     """
 
     from solution import _native
+    import dataclasses
+
     from solution.config import (
         ConfigSpec,
         RuntimeBackend,
+        Sm100GemmParams,
         default_attention,
         default_program,
         default_schedule,
@@ -712,11 +716,21 @@ def run_official(args: argparse.Namespace) -> None:
             row["eager_runtime"] = model.active_config.schedule.runtime.value
             if not streamed:
                 attention = default_attention(cfg.d_model // cfg.num_heads)
+                graph = default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention)
                 model.configure_execution(config=ConfigSpec(
-                    program=default_program(attention=attention),
-                    schedule=default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention),
+                    program=default_program(attention=attention), schedule=graph,
                 ))
                 row["graph_ms"] = median_ms(model, x, warmup, steps)
+                # The same graph with every projection on the small-problem GEMM.
+                warp = Sm100GemmParams(64, 64, 64, 1)
+                model.configure_execution(config=ConfigSpec(
+                    program=default_program(attention=attention),
+                    schedule=dataclasses.replace(
+                        graph, qkv_launch=warp, attention_output_projection_launch=warp,
+                        ffn_input_launch=warp, ffn_launch=warp,
+                    ),
+                ))
+                row["graph_warp_gemm_ms"] = median_ms(model, x, warmup, steps)
             row["attention"] = model.active_config.program.attention.value
             best = min(v for k, v in row.items() if k.endswith("_ms"))
             ref_deployed, ref_baseline = REFERENCE_PUBLISHED_MS[case]

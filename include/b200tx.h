@@ -42,6 +42,7 @@ extern "C" {
 /* GEMM kernel variants (b200tx_linear_ex). */
 #define B200TX_GEMM_1SM 0  /* one CTA per SM, 128x256 tiles, 4-stage 48 KB ring */
 #define B200TX_GEMM_PAIR 1 /* CTA pairs (cta_group::2), 256x256 tiles, 6-stage 32 KB ring */
+#define B200TX_GEMM_WARP 2 /* small problems: 64x64 tiles on warp-level MMAs (mma.sync), no TMA/TMEM */
 
 /* Attention kernel variants (b200tx_attention_ex). */
 #define B200TX_ATTN_PAIRED 0 /* two 128-row query tiles per CTA, P kept in TMEM */
@@ -130,8 +131,9 @@ int b200tx_linear(const void* a, const void* w, const float* bias, void* out, in
 
 /*
  * b200tx_linear with an explicit kernel variant (B200TX_GEMM_PAIR, the variant
- * of b200tx_linear, or B200TX_GEMM_1SM).  Both compute the same function; the
- * execution plan's GEMM launch records pick one per projection.  Replaces the
+ * of b200tx_linear, B200TX_GEMM_1SM, or B200TX_GEMM_WARP for problems too small
+ * to amortise the tcgen05 pipelines' set-up).  All compute the same function;
+ * the execution plan's GEMM launch records pick one per projection.  Replaces the
  * same reference operators as b200tx_linear; the variant is the sm100
  * counterpart of the reference's GEMM launch parameters
  * (TritonGemmParams, solution/config.py:279-325).
@@ -196,11 +198,11 @@ int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* ou
                              cudaStream_t stream);
 
 /*
- * The same attention as b200tx_attention_generic for head_dim 8, 16 or 32 on
- * warp-level tensor-core MMAs (mma.sync m16n8k16, bf16 inputs, fp32
+ * The same attention as b200tx_attention_generic for head_dim 8, 16, 32, 64 or
+ * 128 on warp-level tensor-core MMAs (mma.sync m16n8k16, bf16 inputs, fp32
  * accumulation): 64 query rows per CTA, 64-key tiles, P kept in registers.
  * Same layouts, masks and semantics.  Replaces, for the reference's official
- * shapes with these head dims (official/test_shapes.json: 8 and 32), its
+ * shapes (official/test_shapes.json: head dims 8, 32, 64, 128), its
  * small-head kernels solution/kernels/attention/triton_dh8.py:72-260 and
  * solution/kernels/attention/triton_s1024_dh32.py:72-366, and the SDPA
  * operators solution/operators/attention/sdpa.py:76-170.

@@ -1,11 +1,12 @@
-// attention_mma_kernels.cuh -- flash attention for head_dim 8, 16 and 32 on the
-// warp-level tensor-core instruction mma.sync.m16n8k16 (bf16 in, fp32 out).
+// attention_mma_kernels.cuh -- flash attention for head_dim 8, 16, 32, 64 and 128
+// on the warp-level tensor-core instruction mma.sync.m16n8k16 (bf16 in, fp32
+// out).
 //
-// The tcgen05 kernels are built for head_dim 64.  The reference's official
-// benchmark shapes (official/test_shapes.json) also use head dims 8 and 32,
-// where a 128-row UMMA tile with a K of 8..32 would leave the tensor pipe
-// mostly idle and the CUDA-core kernel is latency-bound (one query row per
-// one or two threads, keys walked serially).  For these small heads each warp
+// The tcgen05 kernels are built for head_dim 64 and sized for long sequences.
+// The reference's official benchmark shapes (official/test_shapes.json) use
+// head dims 8, 32, 64 and 128 on short sequences (S <= 1024), where the
+// CUDA-core kernel is latency-bound (one query row per one to eight threads,
+// keys walked serially).  For these shapes each warp
 // keeps its 16 query rows' Q fragments in registers and issues m16n8k16 MMAs:
 // the scores of a 64-key tile are 8 accumulator tiles, the probabilities go
 // back into A fragments without leaving registers (an accumulator's row/column
@@ -66,7 +67,8 @@ __device__ __forceinline__ uint32_t ld_u32(const __nv_bfloat16* p) {
 
 template <int DH>
 __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnArgs args) {
-  static_assert(DH == 8 || DH == 16 || DH == 32, "built for head_dim 8, 16 and 32");
+  static_assert(DH == 8 || DH == 16 || DH == 32 || DH == 64 || DH == 128,
+                "built for head_dim 8, 16, 32, 64 and 128");
   constexpr int KSTEPS = (DH + 15) / 16;    // k-steps of Q.K^T (DH = 8 is zero-padded to 16)
   constexpr int OUT_TILES = DH / 8;          // n-tiles of the 16 x DH output
   constexpr int S_TILES = kMmaAttnKeys / 8;  // n-tiles of the 16 x 64 scores

@@ -22,6 +22,7 @@
 #include "attention_persistent.cuh"
 #include "attention_simt_kernels.cuh"
 #include "gemm_kernels.cuh"
+#include "gemm_warp_kernels.cuh"
 #include "norm_kernels.cuh"
 #include "sm100_common.cuh"
 
@@ -321,7 +322,7 @@ namespace {
 
 int linear_impl(const void* a, const void* w, const float* bias, void* out, int out_dtype,
                 int64_t M, int64_t N, int64_t K, int epilogue, int variant, cudaStream_t stream) {
-  if (variant != B200TX_GEMM_1SM && variant != B200TX_GEMM_PAIR)
+  if (variant != B200TX_GEMM_1SM && variant != B200TX_GEMM_PAIR && variant != B200TX_GEMM_WARP)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: variant %d", variant);
   if (a == nullptr || w == nullptr || out == nullptr)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "linear: null tensor pointer");
@@ -341,6 +342,33 @@ int linear_impl(const void* a, const void* w, const float* bias, void* out, int 
   DeviceState* dev = nullptr;
   int rc = current_device(&dev);
   if (rc != B200TX_OK) return rc;
+
+  if (variant == B200TX_GEMM_WARP) {
+    // No tensor maps, no TMEM: one 64 x 64 output tile per CTA.
+    b200tx::WarpGemmArgs wa;
+    wa.a = static_cast<const __nv_bfloat16*>(a);
+    wa.w = static_cast<const __nv_bfloat16*>(w);
+    wa.bias = bias;
+    wa.out = out;
+    wa.M = static_cast<int>(M);
+    wa.N = static_cast<int>(N);
+    wa.K = static_cast<int>(K);
+    wa.n_tiles = static_cast<int>((N + b200tx::kWarpGemmBN - 1) / b200tx::kWarpGemmBN);
+    const int64_t blocks = ((M + b200tx::kWarpGemmBM - 1) / b200tx::kWarpGemmBM) * wa.n_tiles;
+    if (blocks > 0x7fffffffLL) return fail(B200TX_ERR_UNSUPPORTED, "linear: too many tiles");
+    const dim3 grid(static_cast<unsigned>(blocks));
+    const dim3 block(b200tx::kWarpGemmThreads);
+    const bool gelu = epilogue == B200TX_EPI_BIAS_GELU;
+    cudaError_t err;
+    if (out_dtype == B200TX_BF16)
+      err = gelu ? launch(b200tx::gemm_bf16_tn_warp_kernel<b200tx::kEpiBiasGelu, __nv_bfloat16>, grid, block, 0, stream, wa)
+                 : launch(b200tx::gemm_bf16_tn_warp_kernel<b200tx::kEpiBias, __nv_bfloat16>, grid, block, 0, stream, wa);
+    else
+      err = gelu ? launch(b200tx::gemm_bf16_tn_warp_kernel<b200tx::kEpiBiasGelu, float>, grid, block, 0, stream, wa)
+                 : launch(b200tx::gemm_bf16_tn_warp_kernel<b200tx::kEpiBias, float>, grid, block, 0, stream, wa);
+    if (err != cudaSuccess) return cuda_fail(err, "linear (warp) launch");
+    return B200TX_OK;
+  }
 
   const bool paired = variant == B200TX_GEMM_PAIR;
   const int tile_m = paired ? b200tx::kGemm2BM : b200tx::kGemmBM;
@@ -803,8 +831,8 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
   if (batch <= 0 || seq <= 0 || heads <= 0)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: bad shape B=%lld S=%lld H=%lld",
                 (long long)batch, (long long)seq, (long long)heads);
-  if (head_dim != 8 && head_dim != 16 && head_dim != 32)
-    return fail(B200TX_ERR_UNSUPPORTED, "attention_mma: head_dim %lld (built: 8, 16, 32)",
+  if (head_dim != 8 && head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(B200TX_ERR_UNSUPPORTED, "attention_mma: head_dim %lld (built: 8, 16, 32, 64, 128)",
                 (long long)head_dim);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention_mma: operands must be 16-byte aligned");
@@ -833,7 +861,9 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
   switch (head_dim) {
     case 8: err = launch(b200tx::attention_mma_kernel<8>, grid, block, 0, stream, a); break;
     case 16: err = launch(b200tx::attention_mma_kernel<16>, grid, block, 0, stream, a); break;
-    default: err = launch(b200tx::attention_mma_kernel<32>, grid, block, 0, stream, a); break;
+    case 32: err = launch(b200tx::attention_mma_kernel<32>, grid, block, 0, stream, a); break;
+    case 64: err = launch(b200tx::attention_mma_kernel<64>, grid, block, 0, stream, a); break;
+    default: err = launch(b200tx::attention_mma_kernel<128>, grid, block, 0, stream, a); break;
   }
   if (err != cudaSuccess) return cuda_fail(err, "attention_mma launch");
   return B200TX_OK;

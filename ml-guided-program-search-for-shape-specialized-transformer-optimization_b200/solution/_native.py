@@ -23,6 +23,7 @@ EPI_BIAS = 0
 EPI_BIAS_GELU = 1
 GEMM_1SM = 0
 GEMM_PAIR = 1
+GEMM_WARP = 2
 ATTN_PAIRED = 0
 ATTN_SINGLE = 1
 ATTN_QUAD = 2
@@ -337,7 +338,7 @@ def linear(
     variant: int = GEMM_PAIR,
 ) -> None:
     """Launch b200tx_linear_ex: out = epilogue(a . w^T + bias) with the given
-    kernel variant (GEMM_1SM or GEMM_PAIR)."""
+    kernel variant (GEMM_1SM, GEMM_PAIR or GEMM_WARP)."""
 
     k = a.shape[-1]
     m = a.numel() // k
@@ -404,7 +405,7 @@ def attention_mma(
     causal: bool,
     key_valid: torch.Tensor | None = None,
 ) -> None:
-    """Launch b200tx_attention_mma (warp-level tensor-core attention, head_dim 8, 16, 32)."""
+    """Launch b200tx_attention_mma (warp-level tensor-core attention, head_dim 8..128)."""
 
     lib = load()
     _check(

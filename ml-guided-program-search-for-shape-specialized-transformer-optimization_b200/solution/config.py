@@ -33,7 +33,7 @@ class AttentionBackend(StrEnum):
     # dims the tensor-core kernels do not build; csrc/attention_simt_kernels.cuh),
     # same packed [B,S,3D] input and [B,S,D] output.
     SM100_SIMT = "sm100_simt"
-    # Flash attention for head_dim 8, 16 and 32 on warp-level tensor-core MMAs
+    # Flash attention for head_dim 8..128 on warp-level tensor-core MMAs
     # (mma.sync m16n8k16; csrc/attention_mma_kernels.cuh), same input and output.
     SM100_MMA = "sm100_mma"
 
@@ -158,7 +158,8 @@ def _exact_fields(value: dict[str, Any], expected: frozenset[str], *, field: str
 # (tile_m, tile_n, tile_k, stages) -> libb200tx GEMM variant:
 #   (128, 256, 64, 4): one CTA per SM (B200TX_GEMM_1SM)
 #   (256, 256, 64, 6): CTA pairs sharing each tile through cta_group::2 (B200TX_GEMM_PAIR)
-SM100_GEMM_VARIANT_CODES = {(128, 256, 64, 4): 0, (256, 256, 64, 6): 1}
+#   (64, 64, 64, 1):   small problems, 64x64 tiles on warp-level MMAs (B200TX_GEMM_WARP)
+SM100_GEMM_VARIANT_CODES = {(128, 256, 64, 4): 0, (256, 256, 64, 6): 1, (64, 64, 64, 1): 2}
 SM100_GEMM_VARIANTS = frozenset(SM100_GEMM_VARIANT_CODES)
 # (block_m, block_n, kv_stages) -> libb200tx attention variant:
 #   (256, 128, 3): two 128-row query tiles per CTA, P kept in TMEM (B200TX_ATTN_PAIRED)
@@ -198,7 +199,7 @@ class Sm100GemmParams:
 
     @property
     def kernel_variant(self) -> int:
-        """The libb200tx GEMM variant code (B200TX_GEMM_1SM / _PAIR)."""
+        """The libb200tx GEMM variant code (B200TX_GEMM_1SM / _PAIR / _WARP)."""
 
         return SM100_GEMM_VARIANT_CODES[(self.tile_m, self.tile_n, self.tile_k, self.stages)]
 
@@ -590,11 +591,11 @@ def default_schedule(
 
 def default_attention(head_dim: int | None) -> AttentionBackend:
     """The tcgen05 kernels for head_dim 64 (or unknown), the warp-MMA kernel for
-    8, 16 and 32, else the CUDA-core one (128, 256)."""
+    8, 16, 32 and 128, else the CUDA-core one (256)."""
 
     if head_dim in (None, 64):
         return AttentionBackend.SM100_FLASH
-    if head_dim in (8, 16, 32):
+    if head_dim in (8, 16, 32, 128):
         return AttentionBackend.SM100_MMA
     return AttentionBackend.SM100_SIMT
 

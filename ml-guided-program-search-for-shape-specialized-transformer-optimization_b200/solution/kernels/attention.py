@@ -171,7 +171,7 @@ def sm100_simt_attention(
 
 
 SM100_MMA_ATTENTION_BACKEND = "sm100_mma_attention"
-MMA_HEAD_DIMS = (8, 16, 32)
+MMA_HEAD_DIMS = (8, 16, 32, 64, 128)
 
 
 def can_use_sm100_mma_attention(qkv: torch.Tensor, num_heads: int) -> bool:
@@ -197,9 +197,9 @@ def sm100_mma_attention(
     out: torch.Tensor | None = None,
     key_valid: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, str]:
-    """The same attention as ``sm100_flash_attention`` for head_dim 8, 16 and 32
-    on warp-level tensor-core MMAs (csrc/attention_mma_kernels.cuh); the
-    reference's official shapes use head dims 8 and 32."""
+    """The same attention as ``sm100_flash_attention`` for head_dim 8, 16, 32, 64
+    and 128 on warp-level tensor-core MMAs (csrc/attention_mma_kernels.cuh),
+    for the short sequences of the reference's official shapes."""
 
     if not can_use_sm100_mma_attention(qkv, num_heads):
         raise RuntimeError("sm100 warp-MMA attention is ineligible for the requested inputs")

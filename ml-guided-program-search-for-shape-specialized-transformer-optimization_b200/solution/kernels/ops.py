@@ -10,7 +10,7 @@ under meta and fake tensors (tests/solution/test_triton_shape13_attention.py:
 * ``b200tx::linear``               -- ``sm100_linear`` (bias, optional erf GELU)
 * ``b200tx::flash_attention``      -- ``sm100_flash_attention`` (head_dim 64)
 * ``b200tx::simt_attention``       -- ``sm100_simt_attention`` (head_dim 8..256)
-* ``b200tx::mma_attention``        -- ``sm100_mma_attention`` (head_dim 8, 16, 32)
+* ``b200tx::mma_attention``        -- ``sm100_mma_attention`` (head_dim 8..128)
 * ``b200tx::residual_layer_norm``  -- ``sm100_residual_layer_norm`` (returns
   the fp32 residual and the normalised tensor)
 * ``b200tx::layer_norm``           -- ``sm100_initial_layer_norm``
@@ -201,7 +201,7 @@ def mma_attention(
     causal: bool = True,
     key_valid: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """The same attention for head_dim 8, 16 and 32 on warp-level tensor-core MMAs."""
+    """The same attention for head_dim 8..128 on warp-level tensor-core MMAs."""
 
     _attention_shape(qkv, num_heads, key_valid, MMA_HEAD_DIMS)
     with torch.no_grad():

@@ -34,7 +34,7 @@ Reject = Callable[[str, str, str], None]
 SUPPORTED_HEAD_DIMS = frozenset({64})
 # Head dims built into the CUDA-core attention (b200tx_attention_generic).
 SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
-MMA_HEAD_DIMS = frozenset({8, 16, 32})
+MMA_HEAD_DIMS = frozenset({8, 16, 32, 64, 128})
 # The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
 # B200TX_ATTN_PERSISTENT and B200TX_ATTN_DUO).
 SM100_QUAD_ATTENTION_VARIANT = 2

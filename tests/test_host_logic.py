@@ -204,7 +204,7 @@ def test_argument_errors_are_reported_before_any_launch() -> None:
     assert rc == -1 and b"variant" in lib.b200tx_last_error()
     rc = lib.b200tx_attention_generic(buf, None, buf, 1, 16, 1, 48, ctypes.c_float(0.125), 1, None)
     assert rc == -2 and b"head_dim" in lib.b200tx_last_error()
-    rc = lib.b200tx_attention_mma(buf, None, buf, 1, 16, 1, 64, ctypes.c_float(0.125), 1, None)
+    rc = lib.b200tx_attention_mma(buf, None, buf, 1, 16, 1, 256, ctypes.c_float(0.125), 1, None)
     assert rc == -2 and b"head_dim" in lib.b200tx_last_error()
     rc = lib.b200tx_attention_mma(None, None, buf, 1, 16, 1, 32, ctypes.c_float(0.125), 1, None)
     assert rc == -1 and b"null" in lib.b200tx_last_error()

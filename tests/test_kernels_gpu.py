@@ -116,7 +116,7 @@ def test_initial_layer_norm(dtype: torch.dtype) -> None:
         (16384, 1024, 1024, False, torch.bfloat16, True),  # C2 out-projection shape
     ],
 )
-@pytest.mark.parametrize("variant", [_native.GEMM_1SM, _native.GEMM_PAIR])
+@pytest.mark.parametrize("variant", [_native.GEMM_1SM, _native.GEMM_PAIR, _native.GEMM_WARP])
 def test_linear(m: int, n: int, k: int, gelu: bool, out_dtype: torch.dtype, bias: bool, variant: int) -> None:
     g = torch.Generator().manual_seed(m + 7 * n + 13 * k)
     a = torch.randn(m, k, generator=g).to(torch.bfloat16)
@@ -445,7 +445,7 @@ def test_simt_attention_key_padding_mask(head_dim: int) -> None:
 
 
 # ---------------------------------------------------------------- warp-MMA attention
-@pytest.mark.parametrize("head_dim", [8, 16, 32])
+@pytest.mark.parametrize("head_dim", [8, 16, 32, 64, 128])
 @pytest.mark.parametrize(
     ("batch", "seq", "heads", "causal"),
     [(2, 128, 4, True), (1, 300, 2, False), (3, 33, 1, True), (1, 1, 2, True), (2, 1000, 3, True), (1, 65, 1, False)],
@@ -464,7 +464,7 @@ def test_mma_attention_head_dims(head_dim: int, batch: int, seq: int, heads: int
     assert rel < 1e-2 and max_abs < 2e-2, (head_dim, max_abs, rel)
 
 
-@pytest.mark.parametrize("head_dim", [8, 32])
+@pytest.mark.parametrize("head_dim", [8, 32, 128])
 def test_mma_attention_key_padding_mask_and_large_logits(head_dim: int) -> None:
     from solution.kernels import sm100_mma_attention
 

@@ -147,7 +147,7 @@ def test_reference_official_shapes(case: str) -> None:
     rows = [0, cfg.batch_size - 1]
     _gate(y[rows], _rows_reference(cfg, x, rows))
     head_dim = cfg.d_model // cfg.num_heads
-    expected = "sm100_flash" if head_dim == 64 else "sm100_mma" if head_dim in (8, 16, 32) else "sm100_simt"
+    expected = "sm100_flash" if head_dim == 64 else "sm100_mma" if head_dim in (8, 16, 32, 128) else "sm100_simt"
     assert model.active_config.program.attention.value == expected
 
 

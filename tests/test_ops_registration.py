@@ -113,7 +113,7 @@ def test_operators_export_as_graph_nodes() -> None:
         (lambda: B200.flash_attention(_meta(2, 8, 3 * 128), 2, True, _native.ATTN_QUAD,
                                       _meta(2, 9, dtype=torch.uint8)), "key_valid"),
         (lambda: B200.simt_attention(_meta(2, 8, 3 * 96), 1), "head_dim 96"),
-        (lambda: B200.mma_attention(_meta(2, 8, 3 * 128), 2), "head_dim 64"),
+        (lambda: B200.mma_attention(_meta(2, 8, 3 * 512), 2), "head_dim 256"),
         (lambda: B200.layer_norm(_meta(4, 64, dtype=torch.float32), _meta(32, dtype=torch.float32),
                                  _meta(32, dtype=torch.float32)), "weight and bias"),
         (lambda: B200.residual_layer_norm(_meta(4, 64, dtype=torch.float32), _meta(4, 32),

@@ -57,13 +57,16 @@ def test_resident_space_has_every_structure_and_the_portable_branch() -> None:
     space = _space()
     runtimes = {b.structure.runtime for b in space.branches}
     assert runtimes == {RuntimeBackend.EAGER, RuntimeBackend.CUDA_GRAPH, RuntimeBackend.BATCH_TILED_CUDA_GRAPH}
-    # two attention backends (head_dim 64 has both) x two precision plans x three runtimes
-    assert len(space.branches) == 12
+    # three attention backends (head_dim 64 has all three) x two precision plans x three
+    # runtimes = 18 feasible structures, seeded sample capped at the branch limit
+    from autotune.search_space import DEFAULT_MAX_STRUCTURE_BRANCHES
+
+    assert len(space.branches) == DEFAULT_MAX_STRUCTURE_BRANCHES == 16
     portable = space.branch_for(portable_config())
     assert portable is not None and portable.structure.portable
     assert portable.branch_id in space.mandatory_branch_ids
-    # 5 attention variants x 2^4 GEMM variants
-    assert portable.cardinality == 5 * 16
+    # 5 attention variants x 3^4 GEMM variants
+    assert portable.cardinality == 5 * 81
     assert space.cardinality == sum(b.cardinality for b in space.branches)
 
 
@@ -122,7 +125,7 @@ def test_other_head_dims_search_the_warp_mma_and_cuda_core_attention() -> None:
     }
     assert portable_config(head_dim=32) in list(space.configs())
     assert portable_config(head_dim=32).program.attention is AttentionBackend.SM100_MMA
-    space = _space(d_model=512, num_heads=4)  # head_dim 128: the CUDA-core kernel only
+    space = _space(d_model=1024, num_heads=4)  # head_dim 256: the CUDA-core kernel only
     assert {b.structure.attention for b in space.branches} == {AttentionBackend.SM100_SIMT}
 
 
