@@ -655,8 +655,9 @@ def run_official(args: argparse.Namespace) -> None:
     same shapes (fp32 input from seed 0, weights from seed 0) through
     ``UserOptimizedTransformer`` with the config it resolves by itself (the
     deployed entry for this device and shape, else the eager default), with
-    the CUDA-graph schedule, and with the CUDA-graph schedule on the
-    small-problem GEMM variant, each forward bracketed by CUDA events after an L2
+    the CUDA-graph schedule, with the CUDA-graph schedule on the small-problem
+    GEMM variant and, for d_model <= 128, with the fused block boundaries, each
+    forward bracketed by CUDA events after an L2
     flush, and reports the median of each schedule beside the published
     numbers.  official_14 (B32 S100000, the streamed capacity shape) runs its
     default streamed config with at most 2 timed forwards.
@@ -734,6 +735,18 @@ def run_official(args: argparse.Namespace) -> None:
                     ),
                 ))
                 row["graph_warp_gemm_ms"] = median_ms(model, x, warmup, steps)
+                # Fused block boundaries (d_model 32/64/128): out-proj and FFN-out
+                # inside the residual LayerNorm, then the whole MLP as well.
+                if cfg.d_model in (32, 64, 128):
+                    fusions = ("linear", "mlp") if cfg.ffn_dim % 32 == 0 else ("linear",)
+                    for fusion in fusions:
+                        model.configure_execution(config=ConfigSpec(
+                            program=default_program(attention=attention, fused_boundary=fusion),
+                            schedule=default_schedule(
+                                RuntimeBackend.CUDA_GRAPH, attention=attention, fused_boundary=fusion
+                            ),
+                        ))
+                        row[f"graph_fused_{fusion}_ms"] = median_ms(model, x, warmup, steps)
             row["attention"] = model.active_config.program.attention.value
             best = min(v for k, v in row.items() if k.endswith("_ms"))
             ref_deployed, ref_baseline = REFERENCE_PUBLISHED_MS[case]

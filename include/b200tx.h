@@ -211,6 +211,44 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
                          int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
                          cudaStream_t stream);
 
+/*
+ * The projection that closes a block branch fused with the residual add and
+ * LayerNorm after it, for d_model (cols) 32, 64 or 128 (one row per warp
+ * row group; warp-level tensor-core MMAs):
+ *     u = x[rows, inner] . w[cols, inner]^T + bias[cols]   (rounded to update_dtype)
+ *     r = residual_in + u;  normed = LayerNorm(r) * gamma + beta
+ * x, w BF16 row-major; bias, gamma, beta F32; residual_in in_dtype (F32 or
+ * BF16); residual_out F32 or NULL (not kept); normed out_dtype; inner a
+ * multiple of 8.  row_valid (uint8 [rows] or NULL) and mask_mode as in
+ * b200tx_residual_layer_norm_masked.  The update is rounded to update_dtype
+ * (BF16 or F32) before the add, as the unfused program stores it.
+ * Replaces the reference's fused Linear residual-norm boundary
+ * solution/kernels/boundary/triton_linear_residual_norm.py:33-112 (D 32 and
+ * 128) for the out-projection and the FFN-out projection.
+ */
+int b200tx_linear_residual_layer_norm(const void* x, const void* w, const float* bias, int64_t inner,
+                                      const void* residual_in, int in_dtype, float* residual_out,
+                                      void* normed, int out_dtype, const float* gamma, const float* beta,
+                                      const uint8_t* row_valid, int mask_mode, int update_dtype,
+                                      int64_t rows, int64_t cols, float eps, cudaStream_t stream);
+
+/*
+ * The whole MLP fused through the same boundary, d_model 32, 64 or 128:
+ *     h = bf16(GELU_erf(x[rows, cols] . w1[ffn_dim, cols]^T + b1))   (never stored)
+ *     u = h . w2[cols, ffn_dim]^T + b2                              (rounded to update_dtype)
+ *     r = residual_in + u;  normed = LayerNorm(r) * gamma + beta
+ * ffn_dim a multiple of 32; the other arguments as in
+ * b200tx_linear_residual_layer_norm.  Replaces the reference's fused MLP
+ * boundary solution/kernels/boundary/triton_ffn_residual_norm.py:43-136
+ * (D = F = 128).
+ */
+int b200tx_mlp_residual_layer_norm(const void* x, const void* w1, const float* b1, const void* w2,
+                                   const float* b2, int64_t ffn_dim, const void* residual_in, int in_dtype,
+                                   float* residual_out, void* normed, int out_dtype, const float* gamma,
+                                   const float* beta, const uint8_t* row_valid, int mask_mode,
+                                   int update_dtype, int64_t rows, int64_t cols, float eps,
+                                   cudaStream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tensor-parallel reduction over NVLink peer memory.  The reference is
  * single-GPU; these entry points implement the head-sharded runtime's

@@ -21,6 +21,7 @@
 #include "attention_mma_kernels.cuh"
 #include "attention_persistent.cuh"
 #include "attention_simt_kernels.cuh"
+#include "boundary_kernels.cuh"
 #include "gemm_kernels.cuh"
 #include "gemm_warp_kernels.cuh"
 #include "norm_kernels.cuh"
@@ -867,6 +868,119 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
   }
   if (err != cudaSuccess) return cuda_fail(err, "attention_mma launch");
   return B200TX_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+template <bool MLP, int D, typename InT, typename OutT>
+cudaError_t launch_boundary_typed(const b200tx::BoundaryArgs& a, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>((a.M + b200tx::kBoundaryRows - 1) / b200tx::kBoundaryRows));
+  const dim3 block(b200tx::kBoundaryThreads);
+  if constexpr (MLP)
+    return launch(b200tx::mlp_residual_layernorm_kernel<D, InT, OutT>, grid, block, 0, stream, a);
+  else
+    return launch(b200tx::linear_residual_layernorm_kernel<D, InT, OutT>, grid, block, 0, stream, a);
+}
+
+template <bool MLP, int D>
+cudaError_t launch_boundary_d(const b200tx::BoundaryArgs& a, int in_dtype, int out_dtype, cudaStream_t stream) {
+  if (in_dtype == B200TX_F32)
+    return out_dtype == B200TX_BF16 ? launch_boundary_typed<MLP, D, float, __nv_bfloat16>(a, stream)
+                                    : launch_boundary_typed<MLP, D, float, float>(a, stream);
+  return out_dtype == B200TX_BF16 ? launch_boundary_typed<MLP, D, __nv_bfloat16, __nv_bfloat16>(a, stream)
+                                  : launch_boundary_typed<MLP, D, __nv_bfloat16, float>(a, stream);
+}
+
+// Shared checks and launch of the two fused boundary entry points.
+template <bool MLP>
+int boundary_impl(const char* name, b200tx::BoundaryArgs& a, int in_dtype, int out_dtype, int update_dtype,
+                  int64_t rows, int64_t cols, int64_t inner, cudaStream_t stream) {
+  if (a.x == nullptr || a.w == nullptr || a.bias == nullptr || a.residual_in == nullptr ||
+      a.normed == nullptr || a.gamma == nullptr || a.beta == nullptr ||
+      (MLP && (a.w2 == nullptr || a.bias2 == nullptr)))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (rows <= 0 || rows > 0x7fffffffLL || inner <= 0 || inner > 0x7fffffffLL)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: bad shape rows=%lld inner=%lld", name, (long long)rows,
+                (long long)inner);
+  if (cols != 32 && cols != 64 && cols != 128)
+    return fail(B200TX_ERR_UNSUPPORTED, "%s: cols (d_model) %lld (built: 32, 64, 128)", name, (long long)cols);
+  if (MLP ? inner % b200tx::kBoundaryHidden != 0 : inner % 8 != 0)
+    return fail(B200TX_ERR_UNSUPPORTED, "%s: inner dimension %lld must be a multiple of %d", name,
+                (long long)inner, MLP ? b200tx::kBoundaryHidden : 8);
+  if ((in_dtype != B200TX_F32 && in_dtype != B200TX_BF16) || (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16) ||
+      (update_dtype != B200TX_F32 && update_dtype != B200TX_BF16))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: dtype codes in=%d out=%d update=%d", name, in_dtype, out_dtype,
+                update_dtype);
+  if (!aligned16(a.x) || !aligned16(a.w) || (MLP && !aligned16(a.w2)) ||
+      (reinterpret_cast<uintptr_t>(a.residual_in) & 7u) != 0 || (reinterpret_cast<uintptr_t>(a.normed) & 7u) != 0 ||
+      (a.residual_out != nullptr && (reinterpret_cast<uintptr_t>(a.residual_out) & 7u) != 0))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: misaligned operand", name);
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  a.M = static_cast<int>(rows);
+  a.K = static_cast<int>(inner);
+  a.update_bf16 = update_dtype == B200TX_BF16 ? 1 : 0;
+  if (a.row_valid == nullptr) a.mask_mode = 0;
+  cudaError_t err;
+  switch (cols) {
+    case 32: err = launch_boundary_d<MLP, 32>(a, in_dtype, out_dtype, stream); break;
+    case 64: err = launch_boundary_d<MLP, 64>(a, in_dtype, out_dtype, stream); break;
+    default: err = launch_boundary_d<MLP, 128>(a, in_dtype, out_dtype, stream); break;
+  }
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return B200TX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200tx_linear_residual_layer_norm(const void* x, const void* w, const float* bias, int64_t inner,
+                                      const void* residual_in, int in_dtype, float* residual_out,
+                                      void* normed, int out_dtype, const float* gamma, const float* beta,
+                                      const uint8_t* row_valid, int mask_mode, int update_dtype,
+                                      int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  b200tx::BoundaryArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.w = static_cast<const __nv_bfloat16*>(w);
+  a.bias = bias;
+  a.residual_in = residual_in;
+  a.residual_out = residual_out;
+  a.normed = normed;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.row_valid = row_valid;
+  a.mask_mode = mask_mode;
+  a.eps = eps;
+  return boundary_impl<false>("linear_residual_layer_norm", a, in_dtype, out_dtype, update_dtype, rows, cols,
+                              inner, stream);
+}
+
+int b200tx_mlp_residual_layer_norm(const void* x, const void* w1, const float* b1, const void* w2,
+                                   const float* b2, int64_t ffn_dim, const void* residual_in, int in_dtype,
+                                   float* residual_out, void* normed, int out_dtype, const float* gamma,
+                                   const float* beta, const uint8_t* row_valid, int mask_mode,
+                                   int update_dtype, int64_t rows, int64_t cols, float eps,
+                                   cudaStream_t stream) {
+  b200tx::BoundaryArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.w = static_cast<const __nv_bfloat16*>(w1);
+  a.bias = b1;
+  a.w2 = static_cast<const __nv_bfloat16*>(w2);
+  a.bias2 = b2;
+  a.residual_in = residual_in;
+  a.residual_out = residual_out;
+  a.normed = normed;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.row_valid = row_valid;
+  a.mask_mode = mask_mode;
+  a.eps = eps;
+  return boundary_impl<true>("mlp_residual_layer_norm", a, in_dtype, out_dtype, update_dtype, rows, cols,
+                             ffn_dim, stream);
 }
 
 int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int64_t heads,

@@ -1,0 +1,278 @@
+// boundary_kernels.cuh -- the projection that closes a block branch, fused with
+// the residual add and the LayerNorm that follow it, for d_model 32, 64 or 128.
+//
+// The reference fuses these boundaries for its small official shapes
+// (solution/kernels/boundary/triton_linear_residual_norm.py:33-112, D in {32,
+// 128}: Linear + bias -> rounded update -> + fp32 residual -> LayerNorm;
+// solution/kernels/boundary/triton_ffn_residual_norm.py:43-136, D = F = 128:
+// the whole MLP through the same boundary, the hidden row never written to
+// memory).  At those shapes every launch costs more than its arithmetic, and
+// fusing takes the block from seven launches to four.  Two kernels:
+//
+//   linear:  r = residual_in + round(x[M,K] . W[D,K]^T + b);  normed = LN(r)
+//   MLP:     h = round_bf16(GELU(n[M,D] . W1[F,D]^T + b1))     (never stored)
+//            r = residual_in + round(h . W2[D,F]^T + b2);      normed = LN(r)
+//
+// "round" is the update dtype the unfused program writes between the GEMM and
+// the LayerNorm (bf16, or fp32 = no rounding), so both paths take the same
+// rounding points.  Padding-row behaviour (row_valid, mask_mode) is the
+// residual LayerNorm kernel's: drop the update, zero the residual, zero the
+// normalised output.
+//
+// A CTA of four warps owns 64 rows; warp w owns rows [16w, 16w + 16) and all D
+// output columns, accumulated by mma.sync.m16n8k16 (bf16 in, fp32 out; the
+// fragment layouts of attention_mma_kernels.cuh).  Operands are staged in
+// shared memory with 16-byte loads, rows padded by 8 elements (conflict-free
+// fragment loads).  A row's D values sit in the four lanes of its row group,
+// so the LayerNorm statistics are two xor shuffles.  No waits other than
+// __syncthreads.
+#pragma once
+
+#include "attention_mma_kernels.cuh"
+#include "gemm_kernels.cuh"
+#include "norm_kernels.cuh"
+
+namespace b200tx {
+
+constexpr int kBoundaryRows = 64;  // rows per CTA (4 warps x 16)
+constexpr int kBoundaryThreads = 128;
+constexpr int kBoundaryK = 64;       // K slice per iteration (linear)
+constexpr int kBoundaryHidden = 32;  // hidden columns per iteration (MLP)
+
+struct BoundaryArgs {
+  const __nv_bfloat16* x;   // linear: [M, K]; MLP: the normalised input [M, D]
+  const __nv_bfloat16* w;   // linear: [D, K]; MLP: W1 [F, D]
+  const float* bias;        // linear: [D]; MLP: b1 [F]
+  const __nv_bfloat16* w2;  // MLP: W2 [D, F]
+  const float* bias2;       // MLP: b2 [D]
+  const void* residual_in;  // [M, D] fp32 or bf16
+  float* residual_out;      // [M, D] fp32, or null when the sum is not kept
+  void* normed;             // [M, D] bf16 or fp32
+  const float* gamma;       // [D]
+  const float* beta;        // [D]
+  const uint8_t* row_valid; // [M] or null
+  int mask_mode;            // kNormMask* bits for rows whose flag is 0
+  int M;
+  int K;                    // linear: inner dimension; MLP: F
+  float eps;
+  int update_bf16;          // round the branch update to bf16 before the add
+};
+
+// Stage rows [row0, row0 + ROWS) x columns [c0, c0 + COLS) of a row-major bf16
+// matrix with `ld` columns into smem (row stride STR); zero outside
+// rows_total x cols_total.  COLS and the column bound are multiples of 8.
+template <int ROWS, int COLS, int STR>
+__device__ __forceinline__ void stage_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t ld,
+                                           int row0, int rows_total, int c0, int cols_total) {
+  constexpr int CPR = COLS / 8;  // 16-byte chunks per row
+  for (int i = threadIdx.x; i < ROWS * CPR; i += kBoundaryThreads) {
+    const int r = i / CPR;
+    const int c = (i % CPR) * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row0 + r < rows_total && c0 + c < cols_total)
+      v = *reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row0 + r) * ld + c0 + c);
+    *reinterpret_cast<uint4*>(dst + r * STR + c) = v;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const T* p);
+template <>
+__device__ __forceinline__ float2 load_pair<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
+template <typename T>
+__device__ __forceinline__ void store_pair_out(T* p, float v0, float v1);
+template <>
+__device__ __forceinline__ void store_pair_out<float>(float* p, float v0, float v1) {
+  *reinterpret_cast<float2*>(p) = make_float2(v0, v1);
+}
+template <>
+__device__ __forceinline__ void store_pair_out<__nv_bfloat16>(__nv_bfloat16* p, float v0, float v1) {
+  *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(v0, v1);
+}
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Residual add + LayerNorm of one row held by the four lanes of a row group:
+// this lane has columns n*8 + 2t, n*8 + 2t + 1 for n < D/8 in acc[n][h], acc[n][h+1]
+// (h = 0 for row g, 2 for row g + 8).
+template <int D, typename InT, typename OutT>
+__device__ __forceinline__ void boundary_row(const BoundaryArgs& a, const float (&acc)[D / 8][4], int h,
+                                             int row, const float* bias_out, int t) {
+  constexpr int NT = D / 8;
+  const bool in_range = row < a.M;
+  bool valid = true;
+  if (in_range && a.row_valid != nullptr) valid = a.row_valid[row] != 0;
+  const bool add_update = valid || !(a.mask_mode & kNormMaskDropUpdate);
+  const bool zero_residual = !valid && (a.mask_mode & kNormMaskZeroResidual);
+  const bool zero_normed = !valid && (a.mask_mode & kNormMaskZeroNormed);
+  const InT* rin = static_cast<const InT*>(a.residual_in) + static_cast<int64_t>(row) * D;
+  float v[NT][2];
+  float sum = 0.f;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int c = n * 8 + 2 * t;
+    float u0 = acc[n][h] + bias_out[c];
+    float u1 = acc[n][h + 1] + bias_out[c + 1];
+    if (a.update_bf16) {
+      u0 = round_bf16(u0);
+      u1 = round_bf16(u1);
+    }
+    float2 r = make_float2(0.f, 0.f);
+    if (in_range && !zero_residual) {
+      r = load_pair<InT>(rin + c);
+      if (add_update) {
+        r.x += u0;
+        r.y += u1;
+      }
+    }
+    v[n][0] = r.x;
+    v[n][1] = r.y;
+    sum += r.x + r.y;
+  }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  const float mean = sum * (1.0f / D);
+  float sq = 0.f;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const float d0 = v[n][0] - mean, d1 = v[n][1] - mean;
+    sq += d0 * d0 + d1 * d1;
+  }
+  sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+  sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+  const float rstd = rsqrtf(sq * (1.0f / D) + a.eps);
+  if (!in_range) return;
+  OutT* out = static_cast<OutT*>(a.normed) + static_cast<int64_t>(row) * D;
+  float* rout = a.residual_out != nullptr ? a.residual_out + static_cast<int64_t>(row) * D : nullptr;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int c = n * 8 + 2 * t;
+    if (rout != nullptr) *reinterpret_cast<float2*>(rout + c) = make_float2(v[n][0], v[n][1]);
+    float o0 = (v[n][0] - mean) * rstd * a.gamma[c] + a.beta[c];
+    float o1 = (v[n][1] - mean) * rstd * a.gamma[c + 1] + a.beta[c + 1];
+    if (zero_normed) o0 = o1 = 0.f;
+    store_pair_out<OutT>(out + c, o0, o1);
+  }
+}
+
+// out-proj / FFN-out + bias + rounding + residual add + LayerNorm.
+template <int D, typename InT, typename OutT>
+__global__ void __launch_bounds__(kBoundaryThreads) linear_residual_layernorm_kernel(BoundaryArgs a) {
+  constexpr int STR = kBoundaryK + 8;
+  __shared__ __align__(16) __nv_bfloat16 x_s[kBoundaryRows * STR];
+  __shared__ __align__(16) __nv_bfloat16 w_s[D * STR];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int row0 = static_cast<int>(blockIdx.x) * kBoundaryRows;
+
+  float acc[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  for (int k0 = 0; k0 < a.K; k0 += kBoundaryK) {
+    __syncthreads();
+    stage_bf16<kBoundaryRows, kBoundaryK, STR>(x_s, a.x, a.K, row0, a.M, k0, a.K);
+    stage_bf16<D, kBoundaryK, STR>(w_s, a.w, a.K, 0, D, k0, a.K);
+    __syncthreads();
+#pragma unroll
+    for (int ks = 0; ks < kBoundaryK / 16; ++ks) {
+      const __nv_bfloat16* x0 = &x_s[(warp * 16 + g) * STR + ks * 16 + 2 * t];
+      const __nv_bfloat16* x1 = x0 + 8 * STR;
+      const uint32_t af[4] = {ld_u32(x0), ld_u32(x1), ld_u32(x0 + 8), ld_u32(x1 + 8)};
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n) {
+        const __nv_bfloat16* wr = &w_s[(n * 8 + g) * STR + ks * 16 + 2 * t];
+        mma_m16n8k16_bf16(acc[n], af, ld_u32(wr), ld_u32(wr + 8));
+      }
+    }
+  }
+  const int r0 = row0 + warp * 16 + g;
+  boundary_row<D, InT, OutT>(a, acc, 0, r0, a.bias, t);
+  boundary_row<D, InT, OutT>(a, acc, 2, r0 + 8, a.bias, t);
+}
+
+// FFN-in + bias + GELU + bf16 hidden, FFN-out + bias + rounding + residual add
+// + LayerNorm; the hidden row stays in registers, 32 columns at a time.
+template <int D, typename InT, typename OutT>
+__global__ void __launch_bounds__(kBoundaryThreads) mlp_residual_layernorm_kernel(BoundaryArgs a) {
+  constexpr int XSTR = D + 8;
+  constexpr int HSTR = kBoundaryHidden + 8;
+  __shared__ __align__(16) __nv_bfloat16 x_s[kBoundaryRows * XSTR];
+  __shared__ __align__(16) __nv_bfloat16 w1_s[kBoundaryHidden * XSTR];
+  __shared__ __align__(16) __nv_bfloat16 w2_s[D * HSTR];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int row0 = static_cast<int>(blockIdx.x) * kBoundaryRows;
+  const int F = a.K;
+
+  stage_bf16<kBoundaryRows, D, XSTR>(x_s, a.x, D, row0, a.M, 0, D);
+  __syncthreads();
+  uint32_t xf[D / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const __nv_bfloat16* x0 = &x_s[(warp * 16 + g) * XSTR + ks * 16 + 2 * t];
+    const __nv_bfloat16* x1 = x0 + 8 * XSTR;
+    xf[ks][0] = ld_u32(x0);
+    xf[ks][1] = ld_u32(x1);
+    xf[ks][2] = ld_u32(x0 + 8);
+    xf[ks][3] = ld_u32(x1 + 8);
+  }
+
+  float acc[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  for (int h0 = 0; h0 < F; h0 += kBoundaryHidden) {
+    __syncthreads();
+    stage_bf16<kBoundaryHidden, D, XSTR>(w1_s, a.w, D, h0, F, 0, D);
+    stage_bf16<D, kBoundaryHidden, HSTR>(w2_s, a.w2, F, 0, D, h0, F);
+    __syncthreads();
+    float hacc[kBoundaryHidden / 8][4];
+#pragma unroll
+    for (int n = 0; n < kBoundaryHidden / 8; ++n) {
+      hacc[n][0] = hacc[n][1] = hacc[n][2] = hacc[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const __nv_bfloat16* wr = &w1_s[(n * 8 + g) * XSTR + ks * 16 + 2 * t];
+        mma_m16n8k16_bf16(hacc[n], xf[ks], ld_u32(wr), ld_u32(wr + 8));
+      }
+    }
+    // Bias, exact-erf GELU and the bf16 hidden rounding of the unfused program,
+    // packed straight into the A fragments of the second product.
+    uint32_t hf[kBoundaryHidden / 8][2];
+#pragma unroll
+    for (int n = 0; n < kBoundaryHidden / 8; ++n) {
+      const int c = h0 + n * 8 + 2 * t;
+      const float b0 = a.bias[c], b1 = a.bias[c + 1];
+      hf[n][0] = pack_bf16x2(gelu_erf(hacc[n][0] + b0), gelu_erf(hacc[n][1] + b1));
+      hf[n][1] = pack_bf16x2(gelu_erf(hacc[n][2] + b0), gelu_erf(hacc[n][3] + b1));
+    }
+#pragma unroll
+    for (int kk = 0; kk < kBoundaryHidden / 16; ++kk) {
+      const uint32_t af[4] = {hf[2 * kk][0], hf[2 * kk][1], hf[2 * kk + 1][0], hf[2 * kk + 1][1]};
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n) {
+        const __nv_bfloat16* wr = &w2_s[(n * 8 + g) * HSTR + kk * 16 + 2 * t];
+        mma_m16n8k16_bf16(acc[n], af, ld_u32(wr), ld_u32(wr + 8));
+      }
+    }
+  }
+  const int r0 = row0 + warp * 16 + g;
+  boundary_row<D, InT, OutT>(a, acc, 0, r0, a.bias2, t);
+  boundary_row<D, InT, OutT>(a, acc, 2, r0 + 8, a.bias2, t);
+}
+
+}  // namespace b200tx

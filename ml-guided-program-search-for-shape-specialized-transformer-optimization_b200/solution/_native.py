@@ -88,6 +88,40 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_float,  # eps
         _c_void_p,  # stream
     ]
+    _tail = [
+        _c_void_p,  # residual_in
+        ctypes.c_int,  # in_dtype
+        _c_void_p,  # residual_out
+        _c_void_p,  # normed
+        ctypes.c_int,  # out_dtype
+        _c_void_p,  # gamma
+        _c_void_p,  # beta
+        _c_void_p,  # row_valid
+        ctypes.c_int,  # mask_mode
+        ctypes.c_int,  # update_dtype
+        _c_int64,  # rows
+        _c_int64,  # cols
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_linear_residual_layer_norm.restype = ctypes.c_int
+    lib.b200tx_linear_residual_layer_norm.argtypes = [
+        _c_void_p,  # x
+        _c_void_p,  # w
+        _c_void_p,  # bias
+        _c_int64,  # inner
+        *_tail,
+    ]
+    lib.b200tx_mlp_residual_layer_norm.restype = ctypes.c_int
+    lib.b200tx_mlp_residual_layer_norm.argtypes = [
+        _c_void_p,  # x
+        _c_void_p,  # w1
+        _c_void_p,  # b1
+        _c_void_p,  # w2
+        _c_void_p,  # b2
+        _c_int64,  # ffn_dim
+        *_tail,
+    ]
     lib.b200tx_linear.restype = ctypes.c_int
     lib.b200tx_linear.argtypes = [
         _c_void_p,  # a
@@ -326,6 +360,96 @@ def residual_layer_norm(
             *common, row_valid.data_ptr(), int(mask_mode), rows, cols, float(eps), stream
         ),
         "b200tx_residual_layer_norm_masked",
+    )
+
+
+def _boundary_tail(
+    residual_in: torch.Tensor,
+    residual_out: torch.Tensor | None,
+    normed: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    row_valid: torch.Tensor | None,
+    mask_mode: int,
+    update_dtype: torch.dtype,
+) -> tuple:
+    cols = residual_in.shape[-1]
+    return (
+        residual_in.data_ptr(),
+        dtype_code(residual_in.dtype),
+        None if residual_out is None else residual_out.data_ptr(),
+        normed.data_ptr(),
+        dtype_code(normed.dtype),
+        gamma.data_ptr(),
+        beta.data_ptr(),
+        None if row_valid is None else row_valid.data_ptr(),
+        int(mask_mode),
+        dtype_code(update_dtype),
+        residual_in.numel() // cols,
+        cols,
+        float(eps),
+        _stream(residual_in.device),
+    )
+
+
+def linear_residual_layer_norm(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor,
+    residual_in: torch.Tensor,
+    residual_out: torch.Tensor | None,
+    normed: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    row_valid: torch.Tensor | None = None,
+    mask_mode: int = 0,
+    update_dtype: torch.dtype = torch.bfloat16,
+) -> None:
+    """Launch b200tx_linear_residual_layer_norm: LN(residual_in + round(x . w^T + bias))."""
+
+    _check(
+        load().b200tx_linear_residual_layer_norm(
+            x.data_ptr(),
+            w.data_ptr(),
+            bias.data_ptr(),
+            x.shape[-1],
+            *_boundary_tail(residual_in, residual_out, normed, gamma, beta, eps, row_valid, mask_mode, update_dtype),
+        ),
+        "b200tx_linear_residual_layer_norm",
+    )
+
+
+def mlp_residual_layer_norm(
+    x: torch.Tensor,
+    w1: torch.Tensor,
+    b1: torch.Tensor,
+    w2: torch.Tensor,
+    b2: torch.Tensor,
+    residual_in: torch.Tensor,
+    residual_out: torch.Tensor | None,
+    normed: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    row_valid: torch.Tensor | None = None,
+    mask_mode: int = 0,
+    update_dtype: torch.dtype = torch.bfloat16,
+) -> None:
+    """Launch b200tx_mlp_residual_layer_norm: LN(residual_in + round(GELU(x . w1^T + b1) . w2^T + b2))."""
+
+    _check(
+        load().b200tx_mlp_residual_layer_norm(
+            x.data_ptr(),
+            w1.data_ptr(),
+            b1.data_ptr(),
+            w2.data_ptr(),
+            b2.data_ptr(),
+            w1.shape[0],
+            *_boundary_tail(residual_in, residual_out, normed, gamma, beta, eps, row_valid, mask_mode, update_dtype),
+        ),
+        "b200tx_mlp_residual_layer_norm",
     )
 
 

@@ -75,6 +75,10 @@ class FFNBackend(StrEnum):
 
     # FFN-in GEMM with a bias + exact-erf GELU epilogue, then the FFN-out GEMM.
     SM100_LINEAR_GELU = "sm100_linear_gelu"
+    # The whole MLP fused through its residual + LayerNorm boundary, d_model
+    # 32/64/128 (csrc/boundary_kernels.cuh; reference value
+    # "triton_fused_mlp_boundary").  Requires the SM100_LINEAR_MIXED boundary.
+    SM100_FUSED_MLP_BOUNDARY = "sm100_fused_mlp_boundary"
 
 
 class ResidualNormBackend(StrEnum):
@@ -82,6 +86,10 @@ class ResidualNormBackend(StrEnum):
 
     # fp32 residual stream, bf16 normalised output (fp32 at the final boundary).
     SM100_MIXED = "sm100_mixed"
+    # The same boundary fused with the projection before it (out-projection and
+    # FFN-out), d_model 32/64/128 (csrc/boundary_kernels.cuh; reference value
+    # "triton_linear_mixed").
+    SM100_LINEAR_MIXED = "sm100_linear_mixed"
 
 
 class InitialNormBackend(StrEnum):
@@ -492,15 +500,19 @@ class ConfigSpec:
         # Every sm100 primitive is a parameterised kernel: its launch record
         # must be present (reference rule: launch present exactly for a
         # parameterised backend, solution/config.py:713-758).
+        # A fused boundary runs the row-parallel projections itself: their
+        # GEMM launch records are absent (reference: solution/config.py:706-717).
+        fused = self.program.residual_norm is ResidualNormBackend.SM100_LINEAR_MIXED
         required = {
             "attention_launch": self.program.attention is AttentionBackend.SM100_FLASH,
             "qkv_launch": self.program.qkv_projection is ProjectionBackend.SM100_BF16,
             "attention_output_projection_launch": (
-                self.program.attention_output_projection is ProjectionBackend.SM100_BF16
+                self.program.attention_output_projection is ProjectionBackend.SM100_BF16 and not fused
             ),
             "ffn_input_launch": self.program.ffn is FFNBackend.SM100_LINEAR_GELU,
-            "ffn_launch": self.program.ffn_output_projection is ProjectionBackend.SM100_BF16,
-            "residual_norm_launch": self.program.residual_norm is ResidualNormBackend.SM100_MIXED,
+            "ffn_launch": self.program.ffn_output_projection is ProjectionBackend.SM100_BF16 and not fused,
+            "residual_norm_launch": self.program.residual_norm
+            in (ResidualNormBackend.SM100_MIXED, ResidualNormBackend.SM100_LINEAR_MIXED),
             "initial_norm_launch": self.program.initial_norm is InitialNormBackend.SM100_BF16,
         }
         for name, needed in required.items():
@@ -544,12 +556,27 @@ class ConfigSpec:
         )
 
 
+# Boundary fusion choices of default_program / default_schedule: None (the
+# unfused program), "linear" (SM100_LINEAR_MIXED: out-projection and FFN-out
+# fused with their residual LayerNorm) or "mlp" (SM100_LINEAR_MIXED plus the
+# whole MLP fused, SM100_FUSED_MLP_BOUNDARY).
+BOUNDARY_FUSIONS = (None, "linear", "mlp")
+
+
+def _check_fusion(fused_boundary: str | None) -> None:
+    if fused_boundary not in BOUNDARY_FUSIONS:
+        raise ValueError(f"fused_boundary must be one of {BOUNDARY_FUSIONS}")
+
+
 def default_program(
     precision_plan: PrecisionPlan = PrecisionPlan.BF16_CORE,
     attention: AttentionBackend = AttentionBackend.SM100_FLASH,
+    *,
+    fused_boundary: str | None = None,
 ) -> ProgramConfig:
     """The sm100 program: every primitive is a libb200tx kernel."""
 
+    _check_fusion(fused_boundary)
     return ProgramConfig(
         attention=attention,
         qkv_projection=ProjectionBackend.SM100_BF16,
@@ -559,8 +586,10 @@ def default_program(
         precision_plan=precision_plan,
         qkv_materialization=QKVMaterialization.PACKED_BSD,
         attention_output_bridge=AttentionOutputBridge.ATTENTION_DIRECT_BSD,
-        ffn=FFNBackend.SM100_LINEAR_GELU,
-        residual_norm=ResidualNormBackend.SM100_MIXED,
+        ffn=FFNBackend.SM100_FUSED_MLP_BOUNDARY if fused_boundary == "mlp" else FFNBackend.SM100_LINEAR_GELU,
+        residual_norm=(
+            ResidualNormBackend.SM100_MIXED if fused_boundary is None else ResidualNormBackend.SM100_LINEAR_MIXED
+        ),
         initial_norm=InitialNormBackend.SM100_BF16,
     )
 
@@ -572,17 +601,19 @@ def default_schedule(
     microbatch_size: int | None = None,
     reuse_unchanged_input: bool = False,
     attention: AttentionBackend = AttentionBackend.SM100_FLASH,
+    fused_boundary: str | None = None,
 ) -> ScheduleConfig:
+    _check_fusion(fused_boundary)
     gemm = Sm100GemmParams()
     return ScheduleConfig(
         runtime=runtime,
         attention_launch=Sm100AttentionParams() if attention is AttentionBackend.SM100_FLASH else None,
         qkv_launch=gemm,
-        attention_output_projection_launch=gemm,
+        attention_output_projection_launch=None if fused_boundary else gemm,
         residual_norm_launch=Sm100NormParams(),
         initial_norm_launch=Sm100NormParams(),
-        ffn_launch=gemm,
-        ffn_input_launch=gemm,
+        ffn_launch=None if fused_boundary else gemm,
+        ffn_input_launch=None if fused_boundary == "mlp" else gemm,
         batch_tile_size=batch_tile_size,
         microbatch_size=microbatch_size,
         reuse_unchanged_input=reuse_unchanged_input,
@@ -632,6 +663,7 @@ __all__ = [
     "AttentionOutputBridge",
     "AttentionOutputLayout",
     "ConfigSpec",
+    "BOUNDARY_FUSIONS",
     "FFNBackend",
     "InitialNormBackend",
     "PrecisionPlan",

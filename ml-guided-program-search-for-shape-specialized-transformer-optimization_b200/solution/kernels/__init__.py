@@ -22,6 +22,14 @@ from .attention import (
     sm100_flash_attention,
     sm100_flash_attention_available,
 )
+from .boundary import (
+    SM100_LINEAR_RESIDUAL_NORM_BACKEND,
+    SM100_MLP_RESIDUAL_NORM_BACKEND,
+    can_use_sm100_linear_residual_norm,
+    can_use_sm100_mlp_residual_norm,
+    sm100_linear_residual_norm,
+    sm100_mlp_residual_norm,
+)
 from .norm import (
     MASK_DROP_UPDATE,
     MASK_ZERO_NORMED,
@@ -54,6 +62,12 @@ __all__ = [
     "can_use_sm100_simt_attention",
     "sm100_simt_attention",
     "SM100_INITIAL_LAYER_NORM_BACKEND",
+    "SM100_LINEAR_RESIDUAL_NORM_BACKEND",
+    "SM100_MLP_RESIDUAL_NORM_BACKEND",
+    "can_use_sm100_linear_residual_norm",
+    "can_use_sm100_mlp_residual_norm",
+    "sm100_linear_residual_norm",
+    "sm100_mlp_residual_norm",
     "SM100_LINEAR_BACKEND",
     "SM100_LINEAR_GELU_BACKEND",
     "SM100_RESIDUAL_LAYER_NORM_BACKEND",

@@ -23,7 +23,9 @@ from . import _native
 from .config import (
     AttentionBackend,
     ConfigSpec,
+    FFNBackend,
     PrecisionPlan,
+    ResidualNormBackend,
     RuntimeBackend,
     fp32_update_roles,
 )
@@ -35,6 +37,7 @@ SUPPORTED_HEAD_DIMS = frozenset({64})
 # Head dims built into the CUDA-core attention (b200tx_attention_generic).
 SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
 MMA_HEAD_DIMS = frozenset({8, 16, 32, 64, 128})
+BOUNDARY_WIDTHS = frozenset({32, 64, 128})
 # The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
 # B200TX_ATTN_PERSISTENT and B200TX_ATTN_DUO).
 SM100_QUAD_ATTENTION_VARIANT = 2
@@ -323,6 +326,30 @@ class PlanBuilder:
                 "ffn_dim",
                 "ffn_dim must be a multiple of 8 (16-byte TMA row pitch)",
             )
+        # Fused block boundaries (reference rules: solution/plan_builder.py:669-697,
+        # 783-805): a whole row of d_model in a warp's registers.
+        program = config.program
+        if program.residual_norm is ResidualNormBackend.SM100_LINEAR_MIXED:
+            if context.d_model not in BOUNDARY_WIDTHS:
+                reject(
+                    "unsupported_shape",
+                    "program.residual_norm",
+                    f"the fused Linear residual-norm boundary is built for d_model {sorted(BOUNDARY_WIDTHS)}, "
+                    f"not {context.d_model}",
+                )
+        if program.ffn is FFNBackend.SM100_FUSED_MLP_BOUNDARY:
+            if program.residual_norm is not ResidualNormBackend.SM100_LINEAR_MIXED:
+                reject(
+                    "backend_incompatible",
+                    "program.residual_norm",
+                    "the fused MLP boundary requires the fused Linear residual-norm boundary",
+                )
+            if ffn_dim is not None and ffn_dim > 0 and ffn_dim % 32:
+                reject(
+                    "unsupported_shape",
+                    "ffn_dim",
+                    "the fused MLP boundary streams the hidden row 32 columns at a time: ffn_dim % 32 == 0",
+                )
         if context.num_layers is None or context.num_layers <= 0:
             reject("non_positive", "num_layers", "num_layers must be positive")
         tokens = context.batch_size * context.seq_len

@@ -29,7 +29,14 @@ from typing import Any
 import torch
 from torch import nn
 
-from .config import AttentionBackend, ConfigSpec, RuntimeBackend, portable_config
+from .config import (
+    AttentionBackend,
+    ConfigSpec,
+    FFNBackend,
+    ResidualNormBackend,
+    RuntimeBackend,
+    portable_config,
+)
 from .kernels import (
     MASK_DROP_UPDATE,
     MASK_ZERO_NORMED,
@@ -47,6 +54,12 @@ from .kernels import (
     sm100_initial_layer_norm,
     sm100_linear,
     sm100_residual_layer_norm,
+)
+from .kernels.boundary import (
+    SM100_LINEAR_RESIDUAL_NORM_BACKEND,
+    SM100_MLP_RESIDUAL_NORM_BACKEND,
+    sm100_linear_residual_norm,
+    sm100_mlp_residual_norm,
 )
 from .plan import ExecutionContext, ExecutionPlan
 from .plan_builder import PlanBuilder
@@ -566,6 +579,13 @@ class UserOptimizedTransformer(nn.Module):
             else SM100_FLASH_ATTENTION_BACKEND
         )
 
+        # Fused block boundaries (small d_model): the out-projection and the
+        # FFN-out run inside the residual-LayerNorm kernel, and with the fused
+        # MLP so do the FFN-in and GELU (reference: solution/transformer.py:844,
+        # 1410-1440).
+        fused_boundary = plan.residual_norm_backend is ResidualNormBackend.SM100_LINEAR_MIXED
+        fused_mlp = plan.ffn_backend is FFNBackend.SM100_FUSED_MLP_BOUNDARY
+
         def gemm_variant(launch: Any) -> int:
             return launch.kernel_variant if launch is not None else 1  # the CTA-pair GEMM
 
@@ -611,10 +631,16 @@ class UserOptimizedTransformer(nn.Module):
         normalized = torch.empty((rows, d_model), dtype=torch.bfloat16, device=device)
         qkv = torch.empty((batch, seq, 3 * d_model), dtype=torch.bfloat16, device=device)
         context = torch.empty((batch, seq, d_model), dtype=torch.bfloat16, device=device)
-        attn_update = torch.empty((rows, d_model), dtype=out_update, device=device)
-        hidden = torch.empty((rows, self.config.ffn_dim), dtype=torch.bfloat16, device=device)
+        attn_update = (
+            None if fused_boundary else torch.empty((rows, d_model), dtype=out_update, device=device)
+        )
+        hidden = (
+            None if fused_mlp else torch.empty((rows, self.config.ffn_dim), dtype=torch.bfloat16, device=device)
+        )
         ffn_out = (
-            attn_update
+            None
+            if fused_boundary
+            else attn_update
             if ffn_update == out_update
             else torch.empty((rows, d_model), dtype=ffn_update, device=device)
         )
@@ -663,60 +689,63 @@ class UserOptimizedTransformer(nn.Module):
                 planned_backend=plan.attention_backend.value,
             )
             w_o, b_o = attention.out_proj.shadow_parameters()
-            token = rec.start("attention_output_projection")
-            _, marker = sm100_linear(
-                context_flat, w_o, b_o, out_dtype=out_update, out=attn_update, variant=out_proj_variant
-            )
-            rec.stop(token)
-            _strict_backend_marker(
-                marker,
-                expected_marker=SM100_LINEAR_BACKEND,
-                planned_backend=plan.attention_output_projection_backend.value,
-            )
-            token = rec.start("residual_norm")
-            _, _, marker = sm100_residual_layer_norm(
-                residual_source,
-                attn_update,
-                layer.norm2.kernel_norm(),
-                final_boundary=False,
-                residual_out=residual,
-                normalized_out=normalized,
-                row_valid=row_valid,
-                mask_mode=MASK_DROP_UPDATE,
-            )
-            rec.stop(token)
-            _strict_backend_marker(
-                marker,
-                expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
-                planned_backend=plan.residual_norm_backend.value,
-            )
+            if fused_boundary:
+                token = rec.start("residual_norm")
+                _, _, marker = sm100_linear_residual_norm(
+                    context_flat,
+                    w_o,
+                    b_o,
+                    residual_source,
+                    layer.norm2.kernel_norm(),
+                    final_boundary=False,
+                    update_dtype=out_update,
+                    residual_out=residual,
+                    normalized_out=normalized,
+                    row_valid=row_valid,
+                    mask_mode=MASK_DROP_UPDATE,
+                )
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_LINEAR_RESIDUAL_NORM_BACKEND,
+                    planned_backend=plan.residual_norm_backend.value,
+                )
+            else:
+                token = rec.start("attention_output_projection")
+                _, marker = sm100_linear(
+                    context_flat, w_o, b_o, out_dtype=out_update, out=attn_update, variant=out_proj_variant
+                )
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_LINEAR_BACKEND,
+                    planned_backend=plan.attention_output_projection_backend.value,
+                )
+                token = rec.start("residual_norm")
+                _, _, marker = sm100_residual_layer_norm(
+                    residual_source,
+                    attn_update,
+                    layer.norm2.kernel_norm(),
+                    final_boundary=False,
+                    residual_out=residual,
+                    normalized_out=normalized,
+                    row_valid=row_valid,
+                    mask_mode=MASK_DROP_UPDATE,
+                )
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
+                    planned_backend=plan.residual_norm_backend.value,
+                )
             residual_source = residual
             w_1, b_1 = layer.ffn_in.shadow_parameters()
-            token = rec.start("ffn_input_projection")
-            _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden, variant=ffn_in_variant)
-            rec.stop(token)
-            _strict_backend_marker(
-                marker,
-                expected_marker=SM100_LINEAR_GELU_BACKEND,
-                planned_backend=plan.ffn_input_projection_backend.value,
-            )
             w_2, b_2 = layer.ffn_out.shadow_parameters()
-            token = rec.start("ffn_output_projection")
-            _, marker = sm100_linear(hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out, variant=ffn_out_variant)
-            rec.stop(token)
-            _strict_backend_marker(
-                marker,
-                expected_marker=SM100_LINEAR_BACKEND,
-                planned_backend=plan.ffn_output_projection_backend.value,
-            )
             last = index == n_layers - 1
             next_norm = self.final_norm if last else self.layers[index + 1].norm1
-            token = rec.start("residual_norm")
-            _, _, marker = sm100_residual_layer_norm(
-                residual,
-                ffn_out,
-                next_norm.kernel_norm(),
+            boundary = dict(
                 final_boundary=last,
+                update_dtype=ffn_update,
                 out_dtype=value.dtype if last else torch.bfloat16,
                 residual_out=None if last else residual,
                 keep_residual=not last,
@@ -724,12 +753,60 @@ class UserOptimizedTransformer(nn.Module):
                 row_valid=row_valid,
                 mask_mode=MASK_ZERO_RESIDUAL | (MASK_ZERO_NORMED if last else 0),
             )
-            rec.stop(token)
-            _strict_backend_marker(
-                marker,
-                expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
-                planned_backend=plan.residual_norm_backend.value,
-            )
+            if fused_mlp:
+                # Each CTA stages its rows of `normalized` before it writes
+                # them back normalised, so the in-place output is safe.
+                token = rec.start("residual_norm")
+                _, _, marker = sm100_mlp_residual_norm(
+                    normalized, w_1, b_1, w_2, b_2, residual, next_norm.kernel_norm(), **boundary
+                )
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_MLP_RESIDUAL_NORM_BACKEND,
+                    planned_backend=plan.ffn_backend.value,
+                )
+            else:
+                token = rec.start("ffn_input_projection")
+                _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden, variant=ffn_in_variant)
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_LINEAR_GELU_BACKEND,
+                    planned_backend=plan.ffn_input_projection_backend.value,
+                )
+                if fused_boundary:
+                    token = rec.start("residual_norm")
+                    _, _, marker = sm100_linear_residual_norm(
+                        hidden, w_2, b_2, residual, next_norm.kernel_norm(), **boundary
+                    )
+                    rec.stop(token)
+                    _strict_backend_marker(
+                        marker,
+                        expected_marker=SM100_LINEAR_RESIDUAL_NORM_BACKEND,
+                        planned_backend=plan.residual_norm_backend.value,
+                    )
+                else:
+                    token = rec.start("ffn_output_projection")
+                    _, marker = sm100_linear(
+                        hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out, variant=ffn_out_variant
+                    )
+                    rec.stop(token)
+                    _strict_backend_marker(
+                        marker,
+                        expected_marker=SM100_LINEAR_BACKEND,
+                        planned_backend=plan.ffn_output_projection_backend.value,
+                    )
+                    token = rec.start("residual_norm")
+                    _, _, marker = sm100_residual_layer_norm(residual, ffn_out, next_norm.kernel_norm(), **{
+                        k: v for k, v in boundary.items() if k != "update_dtype"
+                    })
+                    rec.stop(token)
+                    _strict_backend_marker(
+                        marker,
+                        expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
+                        planned_backend=plan.residual_norm_backend.value,
+                    )
             if observation is not None:
                 observation.record("qkv_projection", plan.qkv_projection_backend.value, qkv.dtype)
                 observation.record("attention", plan.attention_backend.value, qkv.dtype)
@@ -743,9 +820,9 @@ class UserOptimizedTransformer(nn.Module):
                 observation.record(
                     "ffn_input_projection", plan.ffn_input_projection_backend.value, normalized.dtype
                 )
-                observation.record("ffn_activation", "gelu", hidden.dtype)
+                observation.record("ffn_activation", "gelu", torch.bfloat16)
                 observation.record(
-                    "ffn_output_projection", plan.ffn_output_projection_backend.value, hidden.dtype
+                    "ffn_output_projection", plan.ffn_output_projection_backend.value, torch.bfloat16
                 )
                 observation.record("residual_norm", plan.residual_norm_backend.value)
         if observation is not None:

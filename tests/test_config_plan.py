@@ -240,3 +240,68 @@ def test_type_errors() -> None:
         PlanBuilder().evaluate("not a config", _context(), B200)  # type: ignore[arg-type]
     with pytest.raises(TypeError):
         PlanBuilder().evaluate(portable_config(), "ctx", B200)  # type: ignore[arg-type]
+
+
+# ---------------------------------------------------------------- fused block boundaries
+
+
+def _fused(fusion: str, **schedule_overrides: object) -> ConfigSpec:
+    from solution.config import AttentionBackend
+
+    mma = AttentionBackend.SM100_MMA  # head dims 8..128, as the small official shapes use
+    return ConfigSpec(
+        program=default_program(attention=mma, fused_boundary=fusion),
+        schedule=replace(default_schedule(attention=mma, fused_boundary=fusion), **schedule_overrides),
+    )
+
+
+@pytest.mark.parametrize("fusion", ["linear", "mlp"])
+def test_fused_boundaries_drop_the_fused_projections_launch_records(fusion: str) -> None:
+    from solution.config import FFNBackend, ResidualNormBackend
+
+    config = _fused(fusion)
+    assert config.program.residual_norm is ResidualNormBackend.SM100_LINEAR_MIXED
+    assert (config.program.ffn is FFNBackend.SM100_FUSED_MLP_BOUNDARY) == (fusion == "mlp")
+    assert config.schedule.attention_output_projection_launch is None
+    assert config.schedule.ffn_launch is None
+    assert (config.schedule.ffn_input_launch is None) == (fusion == "mlp")
+    assert ConfigSpec.from_dict(json.loads(config.canonical_json())) == config
+    with pytest.raises(ValueError, match="attention_output_projection_launch"):
+        _fused(fusion, attention_output_projection_launch=Sm100GemmParams())
+    with pytest.raises(ValueError, match="fused_boundary"):
+        default_program(fused_boundary="everything")
+
+
+@pytest.mark.parametrize("fusion", ["linear", "mlp"])
+def test_fused_boundaries_accepted_for_small_d_model_only(fusion: str) -> None:
+    for width in (32, 64, 128):
+        context = _context(d_model=width, num_heads=width // 32 if width > 32 else 1, ffn_dim=4 * width)
+        assert PlanBuilder().evaluate(_fused(fusion), context, B200).accepted, width
+    result = PlanBuilder().evaluate(_fused(fusion), _context(), B200)  # d_model 256
+    assert not result.accepted and "unsupported_shape" in _codes(result)
+    fields = {v.field for v in result.violations}
+    assert "program.residual_norm" in fields
+
+
+def test_fused_mlp_needs_the_fused_linear_boundary_and_ffn_dim_multiple_of_32() -> None:
+    from solution.config import FFNBackend
+
+    ok = _fused("mlp")
+    assert PlanBuilder().evaluate(ok, _context(d_model=128, ffn_dim=128), B200).accepted
+    result = PlanBuilder().evaluate(ok, _context(d_model=128, ffn_dim=136), B200)
+    assert not result.accepted and {v.field for v in result.violations} == {"ffn_dim"}
+    unfused_norm = ConfigSpec(
+        program=replace(default_program(), ffn=FFNBackend.SM100_FUSED_MLP_BOUNDARY),
+        schedule=replace(default_schedule(), ffn_input_launch=None),
+    )
+    result = PlanBuilder().evaluate(unfused_norm, _context(d_model=128, ffn_dim=128), B200)
+    assert not result.accepted and "backend_incompatible" in _codes(result)
+
+
+def test_fused_plan_keeps_the_expected_trace_roles() -> None:
+    plan = PlanBuilder().build(_fused("mlp"), _context(d_model=128, ffn_dim=128), B200)
+    trace = plan.expected_trace
+    assert trace.residual_norm_backend.value == "sm100_linear_mixed"
+    assert trace.ffn_backend.value == "sm100_fused_mlp_boundary"
+    assert trace.attention_output_projection_calls == trace.ffn_output_projection_calls == 2
+    assert trace.residual_norm_calls == 4

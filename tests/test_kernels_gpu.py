@@ -511,3 +511,131 @@ def test_simt_and_tensor_core_attention_agree_at_head_dim_64() -> None:
         b, _ = sm100_simt_attention(qkv, 4)
     max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
     assert rel < 5e-3 and max_abs < 4e-2, (max_abs, rel)
+
+
+# ---------------------------------------------------------------- fused block boundaries
+def _bf16_round(x: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def _boundary_reference(
+    resid: np.ndarray, update: np.ndarray, gamma: np.ndarray, beta: np.ndarray, update_bf16: bool,
+    valid: np.ndarray | None, mask_mode: int,
+) -> tuple[np.ndarray, np.ndarray]:
+    u = _bf16_round(update) if update_bf16 else update.astype(np.float32)
+    r = resid.astype(np.float32) + u
+    if valid is not None:
+        bad = ~valid
+        if mask_mode & 1:
+            r[bad] = resid[bad]
+        if mask_mode & 2:
+            r[bad] = 0.0
+    n = layer_norm(r, gamma, beta)
+    if valid is not None and mask_mode & 4:
+        n[~valid] = 0.0
+    return r, n
+
+
+@pytest.mark.parametrize(
+    ("rows", "width", "inner", "in_dtype", "out_dtype", "update_bf16", "mask_mode"),
+    [
+        (1, 32, 32, torch.float32, torch.bfloat16, True, 0),
+        (63, 64, 72, torch.float32, torch.bfloat16, True, 0),  # inner % 16 != 0: zero-padded k-step
+        (1000, 128, 128, torch.float32, torch.float32, False, 0),
+        (129, 128, 512, torch.bfloat16, torch.bfloat16, True, 0),  # FFN-out shape, bf16 residual input
+        (200, 128, 128, torch.float32, torch.bfloat16, True, 1),  # drop the update of padding rows
+        (200, 32, 32, torch.float32, torch.float32, True, 2 | 4),  # zero residual and output
+    ],
+)
+def test_linear_residual_norm(rows, width, inner, in_dtype, out_dtype, update_bf16, mask_mode) -> None:  # noqa: ANN001
+    from solution.kernels import sm100_linear_residual_norm
+
+    g = torch.Generator().manual_seed(rows + width + inner)
+    x = torch.randn(rows, inner, generator=g).to(torch.bfloat16)
+    w = (torch.randn(width, inner, generator=g) / inner**0.5).to(torch.bfloat16)
+    b = torch.randn(width, generator=g)
+    resid = (torch.randn(rows, width, generator=g) * 2).to(in_dtype)
+    norm = torch.nn.LayerNorm(width)
+    with torch.no_grad():
+        norm.weight.normal_(generator=g)
+        norm.bias.normal_(generator=g)
+    valid = (torch.rand(rows, generator=g) > 0.3) if mask_mode else None
+    update = x.float().numpy() @ w.float().numpy().T + b.numpy()
+    r_ref, n_ref = _boundary_reference(
+        resid.float().numpy(), update, norm.weight.detach().numpy(), norm.bias.detach().numpy(), update_bf16,
+        None if valid is None else valid.numpy(), mask_mode,
+    )
+    with torch.inference_mode():
+        r, n, marker = sm100_linear_residual_norm(
+            x.to(DEV), w.to(DEV), b.to(DEV), resid.to(DEV), norm.to(DEV), final_boundary=out_dtype == torch.float32,
+            update_dtype=torch.bfloat16 if update_bf16 else torch.float32, out_dtype=out_dtype,
+            row_valid=None if valid is None else valid.to(DEV).view(torch.uint8), mask_mode=mask_mode,
+        )
+    assert marker == "sm100_linear_residual_norm" and n.dtype == out_dtype
+    max_abs, rel = parity_errors(r.cpu().numpy(), r_ref)
+    assert rel < 4e-3 and max_abs < 5e-2, ("residual", max_abs, rel)
+    max_abs, rel = parity_errors(n.float().cpu().numpy(), n_ref)
+    assert rel < 8e-3 and max_abs < 8e-2, ("normed", max_abs, rel)
+    if valid is not None and mask_mode & 4:
+        assert not n.cpu()[~valid].any()
+
+
+@pytest.mark.parametrize(
+    ("rows", "width", "hidden", "in_dtype", "out_dtype", "keep"),
+    [
+        (64, 128, 128, torch.float32, torch.bfloat16, True),  # the reference's D = F = 128
+        (1000, 32, 32, torch.float32, torch.float32, False),  # official_07 widths, final boundary
+        (77, 64, 256, torch.bfloat16, torch.bfloat16, True),
+        (3, 128, 512, torch.float32, torch.bfloat16, True),
+    ],
+)
+def test_mlp_residual_norm(rows, width, hidden, in_dtype, out_dtype, keep) -> None:  # noqa: ANN001
+    from solution.kernels import sm100_mlp_residual_norm
+
+    g = torch.Generator().manual_seed(rows * 3 + width + hidden)
+    x = torch.randn(rows, width, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(hidden, width, generator=g) / width**0.5).to(torch.bfloat16)
+    b1 = torch.randn(hidden, generator=g) * 0.5
+    w2 = (torch.randn(width, hidden, generator=g) / hidden**0.5).to(torch.bfloat16)
+    b2 = torch.randn(width, generator=g)
+    resid = (torch.randn(rows, width, generator=g) * 2).to(in_dtype)
+    norm = torch.nn.LayerNorm(width)
+    h = _bf16_round(gelu_erf((x.float().numpy() @ w1.float().numpy().T + b1.numpy()).astype(np.float32)))
+    update = h @ w2.float().numpy().T + b2.numpy()
+    r_ref, n_ref = _boundary_reference(
+        resid.float().numpy(), update, norm.weight.detach().numpy(), norm.bias.detach().numpy(), True, None, 0
+    )
+    with torch.inference_mode():
+        r, n, marker = sm100_mlp_residual_norm(
+            x.to(DEV), w1.to(DEV), b1.to(DEV), w2.to(DEV), b2.to(DEV), resid.to(DEV), norm.to(DEV),
+            final_boundary=not keep, out_dtype=out_dtype, keep_residual=keep,
+        )
+    assert marker == "sm100_mlp_residual_norm" and (r is None) == (not keep)
+    if keep:
+        max_abs, rel = parity_errors(r.cpu().numpy(), r_ref)
+        assert rel < 4e-3 and max_abs < 5e-2, ("residual", max_abs, rel)
+    max_abs, rel = parity_errors(n.float().cpu().numpy(), n_ref)
+    assert rel < 8e-3 and max_abs < 8e-2, ("normed", max_abs, rel)
+
+
+def test_mlp_boundary_in_place_output_and_determinism() -> None:
+    """The model writes the normalised output over the MLP's own input."""
+    from solution.kernels import sm100_mlp_residual_norm
+
+    g = torch.Generator().manual_seed(11)
+    rows, width, hidden = 300, 128, 128
+    x = torch.randn(rows, width, generator=g).to(torch.bfloat16).to(DEV)
+    w1 = (torch.randn(hidden, width, generator=g) / width**0.5).to(torch.bfloat16).to(DEV)
+    w2 = (torch.randn(width, hidden, generator=g) / hidden**0.5).to(torch.bfloat16).to(DEV)
+    b1, b2 = torch.randn(hidden, generator=g).to(DEV), torch.randn(width, generator=g).to(DEV)
+    resid = torch.randn(rows, width, generator=g).to(DEV)
+    norm = torch.nn.LayerNorm(width).to(DEV)
+    with torch.inference_mode():
+        r1, n1, _ = sm100_mlp_residual_norm(x, w1, b1, w2, b2, resid, norm, final_boundary=False)
+        r2, n2, _ = sm100_mlp_residual_norm(x, w1, b1, w2, b2, resid, norm, final_boundary=False)
+        buf = x.clone()
+        r3 = resid.clone()
+        sm100_mlp_residual_norm(buf, w1, b1, w2, b2, r3, norm, final_boundary=False, residual_out=r3,
+                                normalized_out=buf)
+    assert torch.equal(n1, n2) and torch.equal(r1, r2)
+    assert torch.equal(buf, n1) and torch.equal(r3, r1)

@@ -238,3 +238,67 @@ def test_baseline_c5_streamed_rows() -> None:
     _gate(y1[:, :1024], _rows_reference(cfg, x, [0, 1], prefix=1024))
     y2 = _run(_model(cfg, portable_streamed_config(microbatch_size=2)), x)
     assert torch.equal(y1, y2)
+
+
+# ---------------------------------------------------------------- fused block boundaries
+@pytest.mark.parametrize("case", ["official_01", "official_07", "official_10"])
+@pytest.mark.parametrize("fusion", ["linear", "mlp"])
+def test_fused_boundaries_match_the_oracle_and_the_unfused_program(case: str, fusion: str) -> None:
+    """The fused Linear / MLP residual-norm boundaries (d_model 128 and 32) give
+    the oracle's output within the gate, agree with the unfused program, and
+    the observed execution signature equals the plan's."""
+
+    from solution.config import default_attention
+
+    cfg = OFFICIAL_SHAPES[case]
+    x = official_input(cfg, 7)
+    attention = default_attention(cfg.d_model // cfg.num_heads)
+    rows = [0, cfg.batch_size - 1]
+    ref = _rows_reference(cfg, x, rows)
+    unfused = _run(
+        _model(cfg, ConfigSpec(program=default_program(attention=attention), schedule=default_schedule(attention=attention))),
+        x,
+    )
+    for runtime in (RuntimeBackend.EAGER, RuntimeBackend.CUDA_GRAPH):
+        config = ConfigSpec(
+            program=default_program(attention=attention, fused_boundary=fusion),
+            schedule=default_schedule(runtime, attention=attention, fused_boundary=fusion),
+        )
+        model = _model(cfg, config)
+        if runtime is RuntimeBackend.EAGER:
+            model.set_execution_observation(True)
+        y = _run(model, x)
+        _gate(y[rows], ref)
+        max_abs, rel = parity_errors(y.float().cpu().numpy(), unfused.float().cpu().numpy())
+        assert max_abs < 2e-2 and rel < 5e-3, (runtime, max_abs, rel)
+        if runtime is RuntimeBackend.EAGER:
+            description = model.describe_execution_path()
+            assert dict(description["observed_execution_signature"]) == dict(
+                description["expected_execution_signature"]
+            )
+        assert torch.equal(_run(model, x), y)  # replays give the same bits
+
+
+@pytest.mark.parametrize("fusion", ["linear", "mlp"])
+def test_fused_boundaries_with_a_padding_mask(fusion: str) -> None:
+    from solution.config import AttentionBackend
+
+    cfg = OfficialConfig(3, 200, 128, 4, 128, 2)
+    x = official_input(cfg, 12)
+    mask = torch.ones(3, 200, dtype=torch.bool)
+    mask[0, :50] = False
+    mask[1, 150:] = False
+    mask[2, ::4] = False
+    state = state_to_numpy(official_state_dict(cfg, seed=0))
+    with np.errstate(invalid="ignore"):
+        ref = transformer_forward(
+            x.numpy(), state, num_heads=4, num_layers=2, causal=True, valid_token_mask=mask.numpy()
+        )
+    mma = AttentionBackend.SM100_MMA
+    model = _model(cfg, ConfigSpec(
+        program=default_program(attention=mma, fused_boundary=fusion),
+        schedule=default_schedule(attention=mma, fused_boundary=fusion),
+    ))
+    y = _run(model, x, mask)
+    _gate(y, ref)
+    assert not y.cpu()[~mask].any(), "padding rows must be exactly zero"
