@@ -65,6 +65,27 @@ __device__ __forceinline__ uint32_t ld_u32(const __nv_bfloat16* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
 
+// Copy N 16-byte chunks with THREADS threads, every load of this thread in
+// flight before its first store: load(i) returns chunk i (zero-filled out of
+// range), store(i, v) writes it.  A loop that stores each chunk right after
+// loading it waits one memory round trip per chunk, since the store stalls on
+// its load and instructions issue in order.
+template <int N, int THREADS, typename Load, typename Store>
+__device__ __forceinline__ void copy_chunks(Load load, Store store) {
+  constexpr int PER = (N + THREADS - 1) / THREADS;
+  uint4 v[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = static_cast<int>(threadIdx.x) + j * THREADS;
+    v[j] = (N % THREADS == 0 || i < N) ? load(i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = static_cast<int>(threadIdx.x) + j * THREADS;
+    if (N % THREADS == 0 || i < N) store(i, v[j]);
+  }
+}
+
 template <int DH>
 __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnArgs args) {
   static_assert(DH == 8 || DH == 16 || DH == 32 || DH == 64 || DH == 128,
@@ -125,20 +146,30 @@ __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnA
   for (int j = 0; j <= last_tile; ++j) {
     const int k0 = j * kMmaAttnKeys;
     __syncthreads();  // the previous tile's fragments have been read
-    for (int i = threadIdx.x; i < CHUNKS; i += kMmaAttnThreads) {
-      const int key = i / (DH / 8);
-      const int c = (i % (DH / 8)) * 8;
-      uint4 kv = make_uint4(0u, 0u, 0u, 0u);
-      uint4 vv = make_uint4(0u, 0u, 0u, 0u);
-      if (k0 + key < S) {
-        kv = *reinterpret_cast<const uint4*>(k_base + static_cast<int64_t>(k0 + key) * tok + c);
-        vv = *reinterpret_cast<const uint4*>(v_base + static_cast<int64_t>(k0 + key) * tok + c);
-      }
-      *reinterpret_cast<uint4*>(&k_s[key * KSTR + c]) = kv;
-      const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&vv);
+    // Chunk i < CHUNKS is K's, i >= CHUNKS is V's (same key / column split).
+    copy_chunks<2 * CHUNKS, kMmaAttnThreads>(
+        [&](int i) {
+          const bool is_v = i >= CHUNKS;
+          const int ci = is_v ? i - CHUNKS : i;
+          const int key = ci / (DH / 8);
+          const int c = (ci % (DH / 8)) * 8;
+          if (k0 + key >= S) return make_uint4(0u, 0u, 0u, 0u);
+          return *reinterpret_cast<const uint4*>((is_v ? v_base : k_base) +
+                                                 static_cast<int64_t>(k0 + key) * tok + c);
+        },
+        [&](int i, uint4 v) {
+          const bool is_v = i >= CHUNKS;
+          const int ci = is_v ? i - CHUNKS : i;
+          const int key = ci / (DH / 8);
+          const int c = (ci % (DH / 8)) * 8;
+          if (!is_v) {
+            *reinterpret_cast<uint4*>(&k_s[key * KSTR + c]) = v;
+          } else {
+            const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) vt_s[(c + e) * VSTR + key] = ve[e];
-    }
+            for (int e = 0; e < 8; ++e) vt_s[(c + e) * VSTR + key] = ve[e];
+          }
+        });
     if (threadIdx.x < kMmaAttnKeys) {
       const int key = k0 + threadIdx.x;
       const bool ok = key < S && (valid == nullptr || valid[key] != 0);

@@ -65,14 +65,14 @@ template <int ROWS, int COLS, int STR>
 __device__ __forceinline__ void stage_bf16(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t ld,
                                            int row0, int rows_total, int c0, int cols_total) {
   constexpr int CPR = COLS / 8;  // 16-byte chunks per row
-  for (int i = threadIdx.x; i < ROWS * CPR; i += kBoundaryThreads) {
-    const int r = i / CPR;
-    const int c = (i % CPR) * 8;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (row0 + r < rows_total && c0 + c < cols_total)
-      v = *reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row0 + r) * ld + c0 + c);
-    *reinterpret_cast<uint4*>(dst + r * STR + c) = v;
-  }
+  copy_chunks<ROWS * CPR, kBoundaryThreads>(
+      [&](int i) {
+        const int r = i / CPR;
+        const int c = (i % CPR) * 8;
+        if (row0 + r >= rows_total || c0 + c >= cols_total) return make_uint4(0u, 0u, 0u, 0u);
+        return *reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row0 + r) * ld + c0 + c);
+      },
+      [&](int i, uint4 v) { *reinterpret_cast<uint4*>(dst + (i / CPR) * STR + (i % CPR) * 8) = v; });
 }
 
 template <typename T>
@@ -168,6 +168,9 @@ __global__ void __launch_bounds__(kBoundaryThreads) linear_residual_layernorm_ke
   constexpr int STR = kBoundaryK + 8;
   __shared__ __align__(16) __nv_bfloat16 x_s[kBoundaryRows * STR];
   __shared__ __align__(16) __nv_bfloat16 w_s[D * STR];
+  // The weights do not depend on the previous kernel: their first slice is
+  // fetched while that kernel drains (programmatic dependent launch).
+  stage_bf16<D, kBoundaryK, STR>(w_s, a.w, a.K, 0, D, 0, a.K);
   griddep_wait();
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
@@ -180,9 +183,11 @@ __global__ void __launch_bounds__(kBoundaryThreads) linear_residual_layernorm_ke
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   for (int k0 = 0; k0 < a.K; k0 += kBoundaryK) {
-    __syncthreads();
+    if (k0 > 0) {
+      __syncthreads();  // the previous slice's fragments have been read
+      stage_bf16<D, kBoundaryK, STR>(w_s, a.w, a.K, 0, D, k0, a.K);
+    }
     stage_bf16<kBoundaryRows, kBoundaryK, STR>(x_s, a.x, a.K, row0, a.M, k0, a.K);
-    stage_bf16<D, kBoundaryK, STR>(w_s, a.w, a.K, 0, D, k0, a.K);
     __syncthreads();
 #pragma unroll
     for (int ks = 0; ks < kBoundaryK / 16; ++ks) {
@@ -210,6 +215,11 @@ __global__ void __launch_bounds__(kBoundaryThreads) mlp_residual_layernorm_kerne
   __shared__ __align__(16) __nv_bfloat16 x_s[kBoundaryRows * XSTR];
   __shared__ __align__(16) __nv_bfloat16 w1_s[kBoundaryHidden * XSTR];
   __shared__ __align__(16) __nv_bfloat16 w2_s[D * HSTR];
+  const int F = a.K;
+  // The first hidden chunk's weights are fetched before waiting for the
+  // previous kernel (they do not depend on it).
+  stage_bf16<kBoundaryHidden, D, XSTR>(w1_s, a.w, D, 0, F, 0, D);
+  stage_bf16<D, kBoundaryHidden, HSTR>(w2_s, a.w2, F, 0, D, 0, F);
   griddep_wait();
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
@@ -217,7 +227,6 @@ __global__ void __launch_bounds__(kBoundaryThreads) mlp_residual_layernorm_kerne
   const int g = lane >> 2;
   const int t = lane & 3;
   const int row0 = static_cast<int>(blockIdx.x) * kBoundaryRows;
-  const int F = a.K;
 
   stage_bf16<kBoundaryRows, D, XSTR>(x_s, a.x, D, row0, a.M, 0, D);
   __syncthreads();
@@ -236,10 +245,12 @@ __global__ void __launch_bounds__(kBoundaryThreads) mlp_residual_layernorm_kerne
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   for (int h0 = 0; h0 < F; h0 += kBoundaryHidden) {
-    __syncthreads();
-    stage_bf16<kBoundaryHidden, D, XSTR>(w1_s, a.w, D, h0, F, 0, D);
-    stage_bf16<D, kBoundaryHidden, HSTR>(w2_s, a.w2, F, 0, D, h0, F);
-    __syncthreads();
+    if (h0 > 0) {
+      __syncthreads();  // the previous chunk's fragments have been read
+      stage_bf16<kBoundaryHidden, D, XSTR>(w1_s, a.w, D, h0, F, 0, D);
+      stage_bf16<D, kBoundaryHidden, HSTR>(w2_s, a.w2, F, 0, D, h0, F);
+      __syncthreads();
+    }
     float hacc[kBoundaryHidden / 8][4];
 #pragma unroll
     for (int n = 0; n < kBoundaryHidden / 8; ++n) {

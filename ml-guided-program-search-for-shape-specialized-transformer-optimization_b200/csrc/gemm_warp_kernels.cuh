@@ -54,9 +54,6 @@ __global__ void __launch_bounds__(kWarpGemmThreads) gemm_bf16_tn_warp_kernel(War
   __shared__ __align__(16) __nv_bfloat16 a_s[kWarpGemmBM * STR];
   __shared__ __align__(16) __nv_bfloat16 w_s[kWarpGemmBN * STR];
 
-  griddep_wait();
-  griddep_launch_dependents();
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
@@ -64,26 +61,47 @@ __global__ void __launch_bounds__(kWarpGemmThreads) gemm_bf16_tn_warp_kernel(War
   const int m0 = static_cast<int>(blockIdx.x / args.n_tiles) * kWarpGemmBM;
   const int n0 = static_cast<int>(blockIdx.x % args.n_tiles) * kWarpGemmBN;
   const int M = args.M, N = args.N, K = args.K;
+  // W is not written by the previous kernel: its first slice is fetched while
+  // that kernel drains (programmatic dependent launch).
+  copy_chunks<CHUNKS, kWarpGemmThreads>(
+      [&](int i) {
+        const int row = i / (kWarpGemmBK / 8);
+        const int c = (i % (kWarpGemmBK / 8)) * 8;
+        if (c >= K || n0 + row >= N) return make_uint4(0u, 0u, 0u, 0u);
+        return *reinterpret_cast<const uint4*>(args.w + static_cast<int64_t>(n0 + row) * K + c);
+      },
+      [&](int i, uint4 v) {
+        *reinterpret_cast<uint4*>(&w_s[(i / (kWarpGemmBK / 8)) * STR + (i % (kWarpGemmBK / 8)) * 8]) = v;
+      });
+  griddep_wait();
+  griddep_launch_dependents();
 
   float acc[kWarpGemmBN / 8][4];
 #pragma unroll
   for (int n = 0; n < kWarpGemmBN / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 
   for (int k0 = 0; k0 < K; k0 += kWarpGemmBK) {
-    __syncthreads();  // the previous slice's fragments have been read
-    for (int i = threadIdx.x; i < CHUNKS; i += kWarpGemmThreads) {
-      const int row = i / (kWarpGemmBK / 8);
-      const int c = (i % (kWarpGemmBK / 8)) * 8;
-      const bool k_ok = k0 + c < K;  // K is a multiple of 8: a chunk is all in or all out
-      uint4 av = make_uint4(0u, 0u, 0u, 0u);
-      uint4 wv = make_uint4(0u, 0u, 0u, 0u);
-      if (k_ok && m0 + row < M)
-        av = *reinterpret_cast<const uint4*>(args.a + static_cast<int64_t>(m0 + row) * K + k0 + c);
-      if (k_ok && n0 + row < N)
-        wv = *reinterpret_cast<const uint4*>(args.w + static_cast<int64_t>(n0 + row) * K + k0 + c);
-      *reinterpret_cast<uint4*>(&a_s[row * STR + c]) = av;
-      *reinterpret_cast<uint4*>(&w_s[row * STR + c]) = wv;
-    }
+    if (k0 > 0) __syncthreads();  // the previous slice's fragments have been read
+    // Chunks [0, CHUNKS) are A's, [CHUNKS, 2 CHUNKS) W's (W's first slice is
+    // already staged); K is a multiple of 8, so a chunk is all inside K or all
+    // outside.
+    copy_chunks<2 * CHUNKS, kWarpGemmThreads>(
+        [&](int i) {
+          const bool is_w = i >= CHUNKS;
+          const int ci = is_w ? i - CHUNKS : i;
+          const int row = ci / (kWarpGemmBK / 8);
+          const int c = (ci % (kWarpGemmBK / 8)) * 8;
+          const int grow = (is_w ? n0 : m0) + row;
+          if ((is_w && k0 == 0) || k0 + c >= K || grow >= (is_w ? N : M)) return make_uint4(0u, 0u, 0u, 0u);
+          return *reinterpret_cast<const uint4*>((is_w ? args.w : args.a) + static_cast<int64_t>(grow) * K + k0 + c);
+        },
+        [&](int i, uint4 v) {
+          const bool is_w = i >= CHUNKS;
+          if (is_w && k0 == 0) return;  // staged before the wait
+          const int ci = is_w ? i - CHUNKS : i;
+          __nv_bfloat16* dst = is_w ? w_s : a_s;
+          *reinterpret_cast<uint4*>(&dst[(ci / (kWarpGemmBK / 8)) * STR + (ci % (kWarpGemmBK / 8)) * 8]) = v;
+        });
     __syncthreads();
 #pragma unroll
     for (int ks = 0; ks < kWarpGemmBK / 16; ++ks) {
