@@ -118,8 +118,9 @@ __device__ __forceinline__ void boundary_row(const BoundaryArgs& a, const float 
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int c = n * 8 + 2 * t;
-    float u0 = acc[n][h] + bias_out[c];
-    float u1 = acc[n][h + 1] + bias_out[c + 1];
+    const float2 bo = make_float2(__ldg(bias_out + c), __ldg(bias_out + c + 1));
+    float u0 = acc[n][h] + bo.x;
+    float u1 = acc[n][h + 1] + bo.y;
     if (a.update_bf16) {
       u0 = round_bf16(u0);
       u1 = round_bf16(u1);
@@ -150,16 +151,24 @@ __device__ __forceinline__ void boundary_row(const BoundaryArgs& a, const float 
   const float rstd = rsqrtf(sq * (1.0f / D) + a.eps);
   if (!in_range) return;
   OutT* out = static_cast<OutT*>(a.normed) + static_cast<int64_t>(row) * D;
-  float* rout = a.residual_out != nullptr ? a.residual_out + static_cast<int64_t>(row) * D : nullptr;
+  if (a.residual_out != nullptr) {
+    float* rout = a.residual_out + static_cast<int64_t>(row) * D;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) *reinterpret_cast<float2*>(rout + n * 8 + 2 * t) = make_float2(v[n][0], v[n][1]);
+  }
+  // All gamma / beta loads (read-only path) before any store of the row: a
+  // load that follows a store through a pointer that may alias it cannot be
+  // hoisted, and would wait a memory round trip per column pair.
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
     const int c = n * 8 + 2 * t;
-    if (rout != nullptr) *reinterpret_cast<float2*>(rout + c) = make_float2(v[n][0], v[n][1]);
-    float o0 = (v[n][0] - mean) * rstd * a.gamma[c] + a.beta[c];
-    float o1 = (v[n][1] - mean) * rstd * a.gamma[c + 1] + a.beta[c + 1];
-    if (zero_normed) o0 = o1 = 0.f;
-    store_pair_out<OutT>(out + c, o0, o1);
+    const float2 gm = make_float2(__ldg(a.gamma + c), __ldg(a.gamma + c + 1));
+    const float2 bt = make_float2(__ldg(a.beta + c), __ldg(a.beta + c + 1));
+    v[n][0] = zero_normed ? 0.f : (v[n][0] - mean) * rstd * gm.x + bt.x;
+    v[n][1] = zero_normed ? 0.f : (v[n][1] - mean) * rstd * gm.y + bt.y;
   }
+#pragma unroll
+  for (int n = 0; n < NT; ++n) store_pair_out<OutT>(out + n * 8 + 2 * t, v[n][0], v[n][1]);
 }
 
 // out-proj / FFN-out + bias + rounding + residual add + LayerNorm.
@@ -267,7 +276,8 @@ __global__ void __launch_bounds__(kBoundaryThreads) mlp_residual_layernorm_kerne
 #pragma unroll
     for (int n = 0; n < kBoundaryHidden / 8; ++n) {
       const int c = h0 + n * 8 + 2 * t;
-      const float b0 = a.bias[c], b1 = a.bias[c + 1];
+      const float2 bb = make_float2(__ldg(a.bias + c), __ldg(a.bias + c + 1));
+      const float b0 = bb.x, b1 = bb.y;
       hf[n][0] = pack_bf16x2(gelu_erf(hacc[n][0] + b0), gelu_erf(hacc[n][1] + b1));
       hf[n][1] = pack_bf16x2(gelu_erf(hacc[n][2] + b0), gelu_erf(hacc[n][3] + b1));
     }

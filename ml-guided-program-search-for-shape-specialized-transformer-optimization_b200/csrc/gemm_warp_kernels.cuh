@@ -119,19 +119,28 @@ __global__ void __launch_bounds__(kWarpGemmThreads) gemm_bf16_tn_warp_kernel(War
   OutT* out = static_cast<OutT*>(args.out);
   const int r0 = m0 + warp * 16 + g;
   const int r1 = r0 + 8;
+  // Bias (read-only path) and epilogue for every column before the first
+  // store: loads after a possibly aliasing store could not be hoisted.
+#pragma unroll
+  for (int n = 0; n < kWarpGemmBN / 8; ++n) {
+    const int col = n0 + n * 8 + 2 * t;
+    float2 bb = make_float2(0.f, 0.f);
+    if (args.bias != nullptr && col < N) bb = make_float2(__ldg(args.bias + col), __ldg(args.bias + col + 1));
+    acc[n][0] += bb.x;
+    acc[n][1] += bb.y;
+    acc[n][2] += bb.x;
+    acc[n][3] += bb.y;
+    if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[n][e] = gelu_erf(acc[n][e]);
+    }
+  }
 #pragma unroll
   for (int n = 0; n < kWarpGemmBN / 8; ++n) {
     const int col = n0 + n * 8 + 2 * t;
     if (col >= N) continue;  // N is a multiple of 8: col + 1 < N whenever col < N
-    const float b0 = args.bias != nullptr ? args.bias[col] : 0.f;
-    const float b1 = args.bias != nullptr ? args.bias[col + 1] : 0.f;
-    float v[4] = {acc[n][0] + b0, acc[n][1] + b1, acc[n][2] + b0, acc[n][3] + b1};
-    if constexpr (EPI == kEpiBiasGelu) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = gelu_erf(v[e]);
-    }
-    if (r0 < M) store_pair<OutT>(out + static_cast<int64_t>(r0) * N + col, v[0], v[1]);
-    if (r1 < M) store_pair<OutT>(out + static_cast<int64_t>(r1) * N + col, v[2], v[3]);
+    if (r0 < M) store_pair<OutT>(out + static_cast<int64_t>(r0) * N + col, acc[n][0], acc[n][1]);
+    if (r1 < M) store_pair<OutT>(out + static_cast<int64_t>(r1) * N + col, acc[n][2], acc[n][3]);
   }
 }
 
