@@ -33,16 +33,20 @@ from dataclasses import dataclass, field, replace
 from typing import Any, Protocol, Union
 
 from solution.config import (
+    BOUNDARY_FUSIONS,
     SM100_ATTENTION_VARIANTS,
     AttentionBackend,
     SM100_GEMM_VARIANTS,
     ConfigSpec,
+    FFNBackend,
     PrecisionPlan,
+    ResidualNormBackend,
     RuntimeBackend,
     Sm100AttentionParams,
     Sm100GemmParams,
     default_program,
     default_schedule,
+    portable_config,
 )
 
 Scalar = Union[str, int, bool]
@@ -156,18 +160,25 @@ class StructureSpec:
     precision_plan: PrecisionPlan
     runtime: RuntimeBackend
     attention: AttentionBackend = AttentionBackend.SM100_FLASH
+    # Block-boundary fusion (None, "linear", "mlp"; see default_program).
+    boundary: str | None = None
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "precision_plan", PrecisionPlan(self.precision_plan))
         object.__setattr__(self, "runtime", RuntimeBackend(self.runtime))
         object.__setattr__(self, "attention", AttentionBackend(self.attention))
+        if self.boundary not in BOUNDARY_FUSIONS:
+            raise ValueError(f"boundary must be one of {BOUNDARY_FUSIONS}")
 
     def to_dict(self) -> dict[str, str]:
-        return {
+        value = {
             "attention": self.attention.value,
             "precision_plan": self.precision_plan.value,
             "runtime": self.runtime.value,
         }
+        if self.boundary is not None:  # unfused structures keep their earlier identity
+            value["boundary"] = self.boundary
+        return value
 
     @property
     def branch_id(self) -> str:
@@ -181,11 +192,27 @@ class StructureSpec:
             self.precision_plan is PrecisionPlan.BF16_CORE
             and self.runtime is RuntimeBackend.EAGER
             and self.attention is AttentionBackend.SM100_FLASH
+            and self.boundary is None
         )
 
     @classmethod
     def from_config(cls, config: ConfigSpec) -> StructureSpec:
-        return cls(config.program.precision_plan, config.schedule.runtime, config.program.attention)
+        program = config.program
+        boundary = None
+        if program.residual_norm is ResidualNormBackend.SM100_LINEAR_MIXED:
+            boundary = "mlp" if program.ffn is FFNBackend.SM100_FUSED_MLP_BOUNDARY else "linear"
+        return cls(program.precision_plan, config.schedule.runtime, program.attention, boundary)
+
+
+def _fused_launches(boundary: str | None) -> frozenset[str]:
+    """Schedule launch fields a fused boundary makes absent."""
+
+    if boundary is None:
+        return frozenset()
+    fused = {"attention_output_projection_launch", "ffn_launch"}
+    if boundary == "mlp":
+        fused.add("ffn_input_launch")
+    return frozenset(fused)
 
 
 def _divisors(n: int, *, below: int | None = None) -> tuple[int, ...]:
@@ -197,7 +224,11 @@ def _domains_for_structure(structure: StructureSpec, context: SearchContext) -> 
     domains = []
     if structure.attention is AttentionBackend.SM100_FLASH:
         domains.append(ParameterDomain("attention_tile", _ATTENTION_CHOICES, _DEFAULT_ATTENTION))
-    domains += [ParameterDomain(name, _GEMM_CHOICES, _DEFAULT_GEMM) for name, _ in _GEMM_ROLES]
+    domains += [
+        ParameterDomain(name, _GEMM_CHOICES, _DEFAULT_GEMM)
+        for name, launch_field in _GEMM_ROLES
+        if launch_field not in _fused_launches(structure.boundary)
+    ]
     batch = context.batch_size
     if structure.runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH:
         tiles = tuple(d for d in _divisors(batch) if d < batch)
@@ -214,12 +245,13 @@ def _domains_for_structure(structure: StructureSpec, context: SearchContext) -> 
 def _structure_specs(context: SearchContext) -> tuple[StructureSpec, ...]:
     runtimes = (RuntimeBackend.STREAMED,) if context.scope == "streamed" else _RESIDENT_RUNTIMES
     specs = []
-    for attention in AttentionBackend:
-        for plan in PrecisionPlan:
-            for runtime in runtimes:
-                if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH and context.batch_size < 2:
-                    continue
-                specs.append(StructureSpec(plan, runtime, attention))
+    for boundary in BOUNDARY_FUSIONS:
+        for attention in AttentionBackend:
+            for plan in PrecisionPlan:
+                for runtime in runtimes:
+                    if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH and context.batch_size < 2:
+                        continue
+                    specs.append(StructureSpec(plan, runtime, attention, boundary))
     return tuple(specs)
 
 
@@ -306,16 +338,21 @@ class BranchSpace:
             microbatch_size=parameters.get("microbatch_size") if runtime is RuntimeBackend.STREAMED else None,
             reuse_unchanged_input=bool(parameters.get("reuse_unchanged_input", False)),
             attention=self.structure.attention,
+            fused_boundary=self.structure.boundary,
         )
         updates: dict[str, Any] = {}
         if "attention_tile" in parameters:
             m, n, stages = _tile_key(parameters["attention_tile"])
             updates["attention_launch"] = Sm100AttentionParams(block_m=m, block_n=n, kv_stages=stages)
         for name, launch_field in _GEMM_ROLES:
+            if name not in parameters:  # a projection the fused boundary runs itself
+                continue
             tm, tn, tk, st = _tile_key(parameters[name])
             updates[launch_field] = Sm100GemmParams(tile_m=tm, tile_n=tn, tile_k=tk, stages=st)
         return ConfigSpec(
-            program=default_program(self.structure.precision_plan, self.structure.attention),
+            program=default_program(
+                self.structure.precision_plan, self.structure.attention, fused_boundary=self.structure.boundary
+            ),
             schedule=replace(schedule, **updates),
         )
 
@@ -330,6 +367,8 @@ class BranchSpace:
                 return None
             values["attention_tile"] = _tile_name((a.block_m, a.block_n, a.kv_stages))
         for name, launch_field in _GEMM_ROLES:
+            if name not in self.parameter_names:
+                continue
             g = getattr(schedule, launch_field)
             if g is None:
                 return None
@@ -388,7 +427,10 @@ class ProgramSearchSpace:
             if witnessed is not None:
                 candidates.append(witnessed)
         required_ids = [b.branch_id for b in candidates if b.structure.portable]
-        for config in required_configs:
+        # The default program for this head dim (its attention chosen by
+        # head_dim) is always searched, as the portable branch is.
+        head_dim = getattr(context.execution_context, "head_dim", None)
+        for config in (portable_config(head_dim=head_dim), *required_configs):
             match = next((b for b in candidates if b.parameters_for(config) is not None), None)
             if match is not None and self.accepted(config):
                 required_ids.append(match.branch_id)

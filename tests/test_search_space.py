@@ -47,9 +47,10 @@ def _context(**overrides: object) -> ExecutionContext:
     return ExecutionContext(**base)  # type: ignore[arg-type]
 
 
-def _space(scope: str = "resident", **overrides: object) -> ProgramSearchSpace:
+def _space(scope: str = "resident", max_branches: int | None = None, **overrides: object) -> ProgramSearchSpace:
+    extra = {} if max_branches is None else {"max_branches": max_branches}
     return ProgramSearchSpace(
-        plan_builder=PlanBuilder(), context=SearchContext(_context(**overrides), scope, B200)
+        plan_builder=PlanBuilder(), context=SearchContext(_context(**overrides), scope, B200), **extra
     )
 
 
@@ -191,3 +192,21 @@ def test_sweep_times_every_candidate_and_publishes_the_winner(tmp_path) -> None:
     shape = ShapeFingerprint(4, 256, 4, 256, 2, True, 1024, "float32", 0.0, 1.0)
     resolved = resolve_deployed_config(hardware=EnvironmentFingerprint.detect(x.device), shape=shape, path=target)
     assert resolved == results[0].config
+
+
+def test_small_d_model_searches_the_fused_boundaries() -> None:
+    space = _space(d_model=128, num_heads=2, ffn_dim=128, max_branches=64)  # official_10: head_dim 64
+    boundaries = {b.structure.boundary for b in space.branches}
+    assert boundaries == {None, "linear", "mlp"}
+    for branch in space.branches:
+        if branch.structure.boundary is None:
+            continue
+        config = branch.default_config()
+        assert space.accepted(config)
+        assert branch.index_for(config) is not None
+        assert space.branch_for(config) is branch
+        # the fused projections have no GEMM tile parameter
+        assert "attention_output_projection_tile" not in branch.parameter_names
+        assert ("ffn_input_tile" in branch.parameter_names) == (branch.structure.boundary == "linear")
+    # d_model 256 builds no fused boundary
+    assert {b.structure.boundary for b in _space(max_branches=64).branches} == {None}
