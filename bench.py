@@ -738,7 +738,7 @@ def run_official(args: argparse.Namespace) -> None:
                 # Fused block boundaries (d_model 32/64/128): out-proj and FFN-out
                 # inside the residual LayerNorm, then the whole MLP as well.
                 if cfg.d_model in (32, 64, 128):
-                    fusions = ("linear", "mlp") if cfg.ffn_dim % 32 == 0 else ("linear",)
+                    fusions = ("linear", "mlp") if cfg.ffn_dim % 16 == 0 else ("linear",)
                     for fusion in fusions:
                         model.configure_execution(config=ConfigSpec(
                             program=default_program(attention=attention, fused_boundary=fusion),

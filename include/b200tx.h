@@ -237,7 +237,7 @@ int b200tx_linear_residual_layer_norm(const void* x, const void* w, const float*
  *     h = bf16(GELU_erf(x[rows, cols] . w1[ffn_dim, cols]^T + b1))   (never stored)
  *     u = h . w2[cols, ffn_dim]^T + b2                              (rounded to update_dtype)
  *     r = residual_in + u;  normed = LayerNorm(r) * gamma + beta
- * ffn_dim a multiple of 32; the other arguments as in
+ * ffn_dim a multiple of 16; the other arguments as in
  * b200tx_linear_residual_layer_norm.  Replaces the reference's fused MLP
  * boundary solution/kernels/boundary/triton_ffn_residual_norm.py:43-136
  * (D = F = 128).

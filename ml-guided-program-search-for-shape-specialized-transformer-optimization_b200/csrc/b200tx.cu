@@ -906,9 +906,9 @@ int boundary_impl(const char* name, b200tx::BoundaryArgs& a, int in_dtype, int o
                 (long long)inner);
   if (cols != 32 && cols != 64 && cols != 128)
     return fail(B200TX_ERR_UNSUPPORTED, "%s: cols (d_model) %lld (built: 32, 64, 128)", name, (long long)cols);
-  if (MLP ? inner % b200tx::kBoundaryHidden != 0 : inner % 8 != 0)
+  if (MLP ? inner % 16 != 0 : inner % 8 != 0)
     return fail(B200TX_ERR_UNSUPPORTED, "%s: inner dimension %lld must be a multiple of %d", name,
-                (long long)inner, MLP ? b200tx::kBoundaryHidden : 8);
+                (long long)inner, MLP ? 16 : 8);
   if ((in_dtype != B200TX_F32 && in_dtype != B200TX_BF16) || (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16) ||
       (update_dtype != B200TX_F32 && update_dtype != B200TX_BF16))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: dtype codes in=%d out=%d update=%d", name, in_dtype, out_dtype,

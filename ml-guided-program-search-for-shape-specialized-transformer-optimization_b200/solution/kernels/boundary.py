@@ -23,7 +23,7 @@ from ._common import is_sm100_cuda, launch, library_ready, require
 SM100_LINEAR_RESIDUAL_NORM_BACKEND = "sm100_linear_residual_norm"
 SM100_MLP_RESIDUAL_NORM_BACKEND = "sm100_mlp_residual_norm"
 BOUNDARY_WIDTHS = (32, 64, 128)
-MLP_HIDDEN_MULTIPLE = 32
+MLP_HIDDEN_MULTIPLE = 16
 
 _IO = (torch.float32, torch.bfloat16)
 

@@ -344,11 +344,11 @@ class PlanBuilder:
                     "program.residual_norm",
                     "the fused MLP boundary requires the fused Linear residual-norm boundary",
                 )
-            if ffn_dim is not None and ffn_dim > 0 and ffn_dim % 32:
+            if ffn_dim is not None and ffn_dim > 0 and ffn_dim % 16:
                 reject(
                     "unsupported_shape",
                     "ffn_dim",
-                    "the fused MLP boundary streams the hidden row 32 columns at a time: ffn_dim % 32 == 0",
+                    "the fused MLP boundary gives each warp 16 hidden columns at a time: ffn_dim % 16 == 0",
                 )
         if context.num_layers is None or context.num_layers <= 0:
             reject("non_positive", "num_layers", "num_layers must be positive")

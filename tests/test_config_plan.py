@@ -283,12 +283,12 @@ def test_fused_boundaries_accepted_for_small_d_model_only(fusion: str) -> None:
     assert "program.residual_norm" in fields
 
 
-def test_fused_mlp_needs_the_fused_linear_boundary_and_ffn_dim_multiple_of_32() -> None:
+def test_fused_mlp_needs_the_fused_linear_boundary_and_ffn_dim_multiple_of_16() -> None:
     from solution.config import FFNBackend
 
     ok = _fused("mlp")
     assert PlanBuilder().evaluate(ok, _context(d_model=128, ffn_dim=128), B200).accepted
-    result = PlanBuilder().evaluate(ok, _context(d_model=128, ffn_dim=136), B200)
+    result = PlanBuilder().evaluate(ok, _context(d_model=128, ffn_dim=136), B200)  # 136 % 16 != 0
     assert not result.accepted and {v.field for v in result.violations} == {"ffn_dim"}
     unfused_norm = ConfigSpec(
         program=replace(default_program(), ffn=FFNBackend.SM100_FUSED_MLP_BOUNDARY),

@@ -587,6 +587,7 @@ def test_linear_residual_norm(rows, width, inner, in_dtype, out_dtype, update_bf
         (1000, 32, 32, torch.float32, torch.float32, False),  # official_07 widths, final boundary
         (77, 64, 256, torch.bfloat16, torch.bfloat16, True),
         (3, 128, 512, torch.float32, torch.bfloat16, True),
+        (50, 64, 48, torch.float32, torch.bfloat16, True),  # the last warp's hidden slice past F
     ],
 )
 def test_mlp_residual_norm(rows, width, hidden, in_dtype, out_dtype, keep) -> None:  # noqa: ANN001
