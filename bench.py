@@ -740,13 +740,18 @@ def run_official(args: argparse.Namespace) -> None:
                 if cfg.d_model in (32, 64, 128):
                     fusions = ("linear", "mlp") if cfg.ffn_dim % 16 == 0 else ("linear",)
                     for fusion in fusions:
-                        model.configure_execution(config=ConfigSpec(
-                            program=default_program(attention=attention, fused_boundary=fusion),
-                            schedule=default_schedule(
-                                RuntimeBackend.CUDA_GRAPH, attention=attention, fused_boundary=fusion
-                            ),
-                        ))
+                        fused = default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention, fused_boundary=fusion)
+                        program = default_program(attention=attention, fused_boundary=fusion)
+                        model.configure_execution(config=ConfigSpec(program=program, schedule=fused))
                         row[f"graph_fused_{fusion}_ms"] = median_ms(model, x, warmup, steps)
+                        # ... with the remaining unfused projections on the small-problem GEMM
+                        warp_rest = {"qkv_launch": warp}
+                        if fusion == "linear":
+                            warp_rest["ffn_input_launch"] = warp
+                        model.configure_execution(config=ConfigSpec(
+                            program=program, schedule=dataclasses.replace(fused, **warp_rest)
+                        ))
+                        row[f"graph_fused_{fusion}_warp_gemm_ms"] = median_ms(model, x, warmup, steps)
             row["attention"] = model.active_config.program.attention.value
             best = min(v for k, v in row.items() if k.endswith("_ms"))
             ref_deployed, ref_baseline = REFERENCE_PUBLISHED_MS[case]
