@@ -14,6 +14,9 @@ under meta and fake tensors (tests/solution/test_triton_shape13_attention.py:
 * ``b200tx::residual_layer_norm``  -- ``sm100_residual_layer_norm`` (returns
   the fp32 residual and the normalised tensor)
 * ``b200tx::layer_norm``           -- ``sm100_initial_layer_norm``
+* ``b200tx::linear_residual_layer_norm`` / ``b200tx::mlp_residual_layer_norm``
+  -- the fused block boundaries (``sm100_linear_residual_norm`` /
+  ``sm100_mlp_residual_norm``), returning ``(residual, normalised)``
 
 Each operator is functional: it allocates its outputs and launches on the
 current stream of the inputs' CUDA device.  The kernels are inference-only
@@ -54,6 +57,8 @@ OPERATORS = (
     "mma_attention",
     "residual_layer_norm",
     "layer_norm",
+    "linear_residual_layer_norm",
+    "mlp_residual_layer_norm",
 )
 
 _IO = (torch.float32, torch.bfloat16)
@@ -298,6 +303,119 @@ def _residual_layer_norm_fake(value, update, weight, bias, eps=1e-5,  # noqa: AN
 residual_layer_norm.register_kernel("cpu")(_no_cpu("residual_layer_norm"))
 
 
+# ---------------------------------------------------------------- fused block boundaries
+
+
+def _boundary_check(
+    x: torch.Tensor,
+    value: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    update_dtype: torch.dtype,
+    out_dtype: torch.dtype,
+) -> int:
+    _norm_check(value, None, gamma, beta, out_dtype, None)
+    width = value.shape[-1]
+    _require(width in (32, 64, 128), f"the fused boundaries are built for d_model 32, 64, 128, not {width}")
+    _require(x.dtype == torch.bfloat16 and x.numel() // x.shape[-1] == value.numel() // width,
+             "x must be bfloat16 with one row per row of value")
+    _require(update_dtype in _IO, "update_dtype must be float32 or bfloat16")
+    return width
+
+
+def _boundary_outputs(value: torch.Tensor, out_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    return (
+        torch.empty(value.shape, dtype=torch.float32, device=value.device),
+        torch.empty(value.shape, dtype=out_dtype, device=value.device),
+    )
+
+
+@torch.library.custom_op(f"{NAMESPACE}::linear_residual_layer_norm", mutates_args=(), device_types="cuda")
+def linear_residual_layer_norm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor,
+    value: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float = 1e-5,
+    update_dtype: torch.dtype = torch.bfloat16,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``r = value + round(x . weight^T + bias)``, ``LN(r)`` in one kernel
+    (d_model 32/64/128); returns ``(r, LN(r))``."""
+
+    width = _boundary_check(x, value, gamma, beta, update_dtype, out_dtype)
+    _require(tuple(weight.shape) == (width, x.shape[-1]) and tuple(bias.shape) == (width,),
+             "weight must be [D, K] and bias [D]")
+    residual, normed = _boundary_outputs(value, out_dtype)
+    _native.linear_residual_layer_norm(
+        x.contiguous(), weight.contiguous(), bias.contiguous(), value.contiguous(), residual, normed,
+        gamma.contiguous(), beta.contiguous(), eps, None, 0, update_dtype,
+    )
+    return residual, normed
+
+
+@linear_residual_layer_norm.register_fake
+def _linear_residual_layer_norm_fake(x, weight, bias, value, gamma, beta, eps=1e-5,  # noqa: ANN001
+                                     update_dtype=torch.bfloat16, out_dtype=torch.bfloat16):  # noqa: ANN001, ANN202, ARG001
+    width = _boundary_check(x, value, gamma, beta, update_dtype, out_dtype)
+    _require(tuple(weight.shape) == (width, x.shape[-1]) and tuple(bias.shape) == (width,),
+             "weight must be [D, K] and bias [D]")
+    return value.new_empty(value.shape, dtype=torch.float32), value.new_empty(value.shape, dtype=out_dtype)
+
+
+linear_residual_layer_norm.register_kernel("cpu")(_no_cpu("linear_residual_layer_norm"))
+
+
+def _mlp_weights_check(x, w1, b1, w2, b2, width):  # noqa: ANN001, ANN202
+    hidden = w1.shape[0] if w1.ndim == 2 else -1
+    _require(
+        hidden > 0 and hidden % 16 == 0 and x.shape[-1] == width
+        and tuple(w1.shape) == (hidden, width) and tuple(w2.shape) == (width, hidden)
+        and tuple(b1.shape) == (hidden,) and tuple(b2.shape) == (width,),
+        "the MLP weights must be w1 [F, D], w2 [D, F], b1 [F], b2 [D] with F a multiple of 16",
+    )
+
+
+@torch.library.custom_op(f"{NAMESPACE}::mlp_residual_layer_norm", mutates_args=(), device_types="cuda")
+def mlp_residual_layer_norm(
+    x: torch.Tensor,
+    w1: torch.Tensor,
+    b1: torch.Tensor,
+    w2: torch.Tensor,
+    b2: torch.Tensor,
+    value: torch.Tensor,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float = 1e-5,
+    update_dtype: torch.dtype = torch.bfloat16,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``r = value + round(bf16(GELU(x . w1^T + b1)) . w2^T + b2)``, ``LN(r)`` in
+    one kernel (d_model 32/64/128); returns ``(r, LN(r))``."""
+
+    width = _boundary_check(x, value, gamma, beta, update_dtype, out_dtype)
+    _mlp_weights_check(x, w1, b1, w2, b2, width)
+    residual, normed = _boundary_outputs(value, out_dtype)
+    _native.mlp_residual_layer_norm(
+        x.contiguous(), w1.contiguous(), b1.contiguous(), w2.contiguous(), b2.contiguous(), value.contiguous(),
+        residual, normed, gamma.contiguous(), beta.contiguous(), eps, None, 0, update_dtype,
+    )
+    return residual, normed
+
+
+@mlp_residual_layer_norm.register_fake
+def _mlp_residual_layer_norm_fake(x, w1, b1, w2, b2, value, gamma, beta, eps=1e-5,  # noqa: ANN001
+                                  update_dtype=torch.bfloat16, out_dtype=torch.bfloat16):  # noqa: ANN001, ANN202, ARG001
+    width = _boundary_check(x, value, gamma, beta, update_dtype, out_dtype)
+    _mlp_weights_check(x, w1, b1, w2, b2, width)
+    return value.new_empty(value.shape, dtype=torch.float32), value.new_empty(value.shape, dtype=out_dtype)
+
+
+mlp_residual_layer_norm.register_kernel("cpu")(_no_cpu("mlp_residual_layer_norm"))
+
+
 @torch.library.custom_op(f"{NAMESPACE}::layer_norm", mutates_args=(), device_types="cuda")
 def layer_norm(
     value: torch.Tensor,
@@ -327,6 +445,8 @@ __all__ = [
     "flash_attention",
     "layer_norm",
     "linear",
+    "linear_residual_layer_norm",
+    "mlp_residual_layer_norm",
     "mma_attention",
     "residual_layer_norm",
     "simt_attention",

@@ -63,6 +63,15 @@ def test_operators_trace_on_meta_tensors() -> None:
     n = B200.layer_norm(_meta(9, 768, dtype=torch.float32), gamma, beta)
     assert (tuple(n.shape), n.dtype) == ((9, 768), torch.bfloat16)
 
+    g128, b128 = _meta(128, dtype=torch.float32), _meta(128, dtype=torch.float32)
+    r, n = B200.linear_residual_layer_norm(_meta(40, 512), _meta(128, 512), g128,
+                                           _meta(40, 128, dtype=torch.float32), g128, b128)
+    assert (tuple(r.shape), r.dtype, n.dtype) == ((40, 128), torch.float32, torch.bfloat16)
+    r, n = B200.mlp_residual_layer_norm(_meta(2, 20, 128), _meta(256, 128), _meta(256, dtype=torch.float32),
+                                        _meta(128, 256), g128, _meta(2, 20, 128, dtype=torch.float32),
+                                        g128, b128, out_dtype=torch.float32)
+    assert (tuple(n.shape), n.dtype) == ((2, 20, 128), torch.float32)
+
 
 def test_operators_trace_under_fake_tensor_mode() -> None:
     with FakeTensorMode():
@@ -114,6 +123,13 @@ def test_operators_export_as_graph_nodes() -> None:
                                       _meta(2, 9, dtype=torch.uint8)), "key_valid"),
         (lambda: B200.simt_attention(_meta(2, 8, 3 * 96), 1), "head_dim 96"),
         (lambda: B200.mma_attention(_meta(2, 8, 3 * 512), 2), "head_dim 256"),
+        (lambda: B200.linear_residual_layer_norm(_meta(4, 256), _meta(256, 256), _meta(256, dtype=torch.float32),
+                                                 _meta(4, 256, dtype=torch.float32), _meta(256, dtype=torch.float32),
+                                                 _meta(256, dtype=torch.float32)), "d_model 32, 64, 128"),
+        (lambda: B200.mlp_residual_layer_norm(_meta(4, 64), _meta(40, 64), _meta(40, dtype=torch.float32),
+                                              _meta(64, 40), _meta(64, dtype=torch.float32),
+                                              _meta(4, 64, dtype=torch.float32), _meta(64, dtype=torch.float32),
+                                              _meta(64, dtype=torch.float32)), "multiple of 16"),
         (lambda: B200.layer_norm(_meta(4, 64, dtype=torch.float32), _meta(32, dtype=torch.float32),
                                  _meta(32, dtype=torch.float32)), "weight and bias"),
         (lambda: B200.residual_layer_norm(_meta(4, 64, dtype=torch.float32), _meta(4, 32),
@@ -197,3 +213,20 @@ def test_opcheck_on_the_gpu() -> None:
     torch.library.opcheck(B200.residual_layer_norm.default,
                           (torch.randn(1, 130, 128, device=DEV), ctx, gamma, beta), test_utils=utils)
     torch.library.opcheck(B200.layer_norm.default, (ctx, gamma, beta), test_utils=utils)
+    residual = torch.randn(1, 130, 128, device=DEV, generator=g)
+    torch.library.opcheck(B200.linear_residual_layer_norm.default, (ctx, w, bias, residual, gamma, beta),
+                          test_utils=utils)
+    w2 = (torch.randn(128, 128, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    torch.library.opcheck(B200.mlp_residual_layer_norm.default,
+                          (ctx, w, bias, w2, bias, residual, gamma, beta), test_utils=utils)
+    # the operators and the wrappers launch the same kernels: equal bits
+    from solution.kernels import sm100_linear_residual_norm, sm100_mlp_residual_norm
+
+    ln = torch.nn.LayerNorm(128).to(DEV)
+    with torch.inference_mode():
+        r_op, n_op = B200.linear_residual_layer_norm(ctx, w, bias, residual, ln.weight, ln.bias)
+        r_w, n_w, _ = sm100_linear_residual_norm(ctx, w, bias, residual, ln, final_boundary=False)
+        assert torch.equal(r_op, r_w) and torch.equal(n_op, n_w)
+        r_op, n_op = B200.mlp_residual_layer_norm(ctx, w, bias, w2, bias, residual, ln.weight, ln.bias)
+        r_w, n_w, _ = sm100_mlp_residual_norm(ctx, w, bias, w2, bias, residual, ln, final_boundary=False)
+        assert torch.equal(r_op, r_w) and torch.equal(n_op, n_w)
