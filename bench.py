@@ -646,6 +646,51 @@ def run_kernel(args: argparse.Namespace) -> None:
     }), flush=True)
 
 
+def official_schedules(cfg, eager: bool = False) -> list[tuple[str, object]]:  # noqa: ANN001
+    """The named schedules the official-shapes table times for one shape:
+    ``graph`` (the default program under the CUDA-graph runtime),
+    ``graph_warp_gemm`` (every projection on the small-problem GEMM) and, for
+    d_model 32/64/128, ``graph_fused_{linear,mlp}[_warp_gemm]`` (the fused
+    block boundaries, optionally with the remaining projections on the
+    small-problem GEMM).  ``eager`` runs the same programs under the eager
+    runtime (one launch per kernel, for ncu launch lists)."""
+
+    import dataclasses
+
+    from solution.config import (
+        ConfigSpec,
+        RuntimeBackend,
+        Sm100GemmParams,
+        default_attention,
+        default_program,
+        default_schedule,
+    )
+
+    runtime = RuntimeBackend.EAGER if eager else RuntimeBackend.CUDA_GRAPH
+    attention = default_attention(cfg.d_model // cfg.num_heads)
+    warp = Sm100GemmParams(64, 64, 64, 1)
+    graph = default_schedule(runtime, attention=attention)
+    out = [
+        ("graph", ConfigSpec(program=default_program(attention=attention), schedule=graph)),
+        ("graph_warp_gemm", ConfigSpec(
+            program=default_program(attention=attention),
+            schedule=dataclasses.replace(
+                graph, qkv_launch=warp, attention_output_projection_launch=warp, ffn_input_launch=warp,
+                ffn_launch=warp,
+            ),
+        )),
+    ]
+    if cfg.d_model in (32, 64, 128):
+        for fusion in ("linear", "mlp") if cfg.ffn_dim % 16 == 0 else ("linear",):
+            fused = default_schedule(runtime, attention=attention, fused_boundary=fusion)
+            program = default_program(attention=attention, fused_boundary=fusion)
+            out.append((f"graph_fused_{fusion}", ConfigSpec(program=program, schedule=fused)))
+            rest = {"qkv_launch": warp, **({"ffn_input_launch": warp} if fusion == "linear" else {})}
+            out.append((f"graph_fused_{fusion}_warp_gemm",
+                        ConfigSpec(program=program, schedule=dataclasses.replace(fused, **rest))))
+    return out
+
+
 def run_official(args: argparse.Namespace) -> None:
     """The reference's headline table on one B200: its official shapes.
 
@@ -664,16 +709,6 @@ def run_official(args: argparse.Namespace) -> None:
     """
 
     from solution import _native
-    import dataclasses
-
-    from solution.config import (
-        ConfigSpec,
-        RuntimeBackend,
-        Sm100GemmParams,
-        default_attention,
-        default_program,
-        default_schedule,
-    )
     from workloads import OFFICIAL_SHAPES, REFERENCE_PUBLISHED_MS, seeded_input, seeded_row
 
     device = torch.device("cuda", 0)
@@ -716,44 +751,20 @@ def run_official(args: argparse.Namespace) -> None:
                          "F": cfg.ffn_dim, "L": cfg.num_layers}
             # The config the model resolves by itself: its deployed entry for this
             # device and shape, else the default (eager) program.
-            row["default_ms"] = median_ms(model, x, warmup, steps)
-            row["default_runtime"] = model.active_config.schedule.runtime.value
+            if args.schedule in (None, "default"):
+                row["default_ms"] = median_ms(model, x, warmup, steps)
+                row["default_runtime"] = model.active_config.schedule.runtime.value
             if not streamed:
-                attention = default_attention(cfg.d_model // cfg.num_heads)
-                graph = default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention)
-                model.configure_execution(config=ConfigSpec(
-                    program=default_program(attention=attention), schedule=graph,
-                ))
-                row["graph_ms"] = median_ms(model, x, warmup, steps)
-                # The same graph with every projection on the small-problem GEMM.
-                warp = Sm100GemmParams(64, 64, 64, 1)
-                model.configure_execution(config=ConfigSpec(
-                    program=default_program(attention=attention),
-                    schedule=dataclasses.replace(
-                        graph, qkv_launch=warp, attention_output_projection_launch=warp,
-                        ffn_input_launch=warp, ffn_launch=warp,
-                    ),
-                ))
-                row["graph_warp_gemm_ms"] = median_ms(model, x, warmup, steps)
-                # Fused block boundaries (d_model 32/64/128): out-proj and FFN-out
-                # inside the residual LayerNorm, then the whole MLP as well.
-                if cfg.d_model in (32, 64, 128):
-                    fusions = ("linear", "mlp") if cfg.ffn_dim % 16 == 0 else ("linear",)
-                    for fusion in fusions:
-                        fused = default_schedule(RuntimeBackend.CUDA_GRAPH, attention=attention, fused_boundary=fusion)
-                        program = default_program(attention=attention, fused_boundary=fusion)
-                        model.configure_execution(config=ConfigSpec(program=program, schedule=fused))
-                        row[f"graph_fused_{fusion}_ms"] = median_ms(model, x, warmup, steps)
-                        # ... with the remaining unfused projections on the small-problem GEMM
-                        warp_rest = {"qkv_launch": warp}
-                        if fusion == "linear":
-                            warp_rest["ffn_input_launch"] = warp
-                        model.configure_execution(config=ConfigSpec(
-                            program=program, schedule=dataclasses.replace(fused, **warp_rest)
-                        ))
-                        row[f"graph_fused_{fusion}_warp_gemm_ms"] = median_ms(model, x, warmup, steps)
+                for name, config in official_schedules(cfg, args.eager_runtime):
+                    if args.schedule not in (None, name):
+                        continue
+                    model.configure_execution(config=config)
+                    row[f"{name}_ms"] = median_ms(model, x, warmup, steps)
             row["attention"] = model.active_config.program.attention.value
-            best = min(v for k, v in row.items() if k.endswith("_ms"))
+            timed = [v for k, v in row.items() if k.endswith("_ms")]
+            if not timed:
+                raise SystemExit(f"--schedule {args.schedule!r} is not timed for {case}")
+            best = min(timed)
             ref_deployed, ref_baseline = REFERENCE_PUBLISHED_MS[case]
             row.update(
                 best_ms=best,
@@ -805,6 +816,12 @@ def main() -> None:
                              "or 'official' for the reference's official-shapes table")
     parser.add_argument("--cases", default=None,
                         help="--workload official: comma-separated case ids (default: all 14)")
+    parser.add_argument("--schedule", default=None,
+                        help="--workload official: time only this schedule (default, graph, graph_warp_gemm, "
+                             "graph_fused_linear, graph_fused_mlp, ..._warp_gemm)")
+    parser.add_argument("--eager-runtime", action="store_true",
+                        help="--workload official: run the named schedules under the eager runtime "
+                             "(one launch per kernel, for ncu launch lists)")
     parser.add_argument("--tp", type=int, default=0,
                         help="c4 under torchrun: tensor-parallel group size (default: max(2, N / B))")
     parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer"), default="auto",
