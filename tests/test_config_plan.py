@@ -305,3 +305,25 @@ def test_fused_plan_keeps_the_expected_trace_roles() -> None:
     assert trace.ffn_backend.value == "sm100_fused_mlp_boundary"
     assert trace.attention_output_projection_calls == trace.ffn_output_projection_calls == 2
     assert trace.residual_norm_calls == 4
+
+
+def test_official_bench_schedules_are_accepted_for_every_official_shape() -> None:
+    """Every schedule `bench.py --workload official` times compiles for its shape."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from workloads import OFFICIAL_SHAPES
+
+    for case, cfg in OFFICIAL_SHAPES.items():
+        if case == "official_14":
+            continue
+        context = _context(
+            batch_size=cfg.batch_size, seq_len=cfg.seq_len, d_model=cfg.d_model, num_heads=cfg.num_heads,
+            ffn_dim=cfg.ffn_dim, num_layers=cfg.num_layers,
+        )
+        for eager in (False, True):
+            for name, config in bench.official_schedules(cfg, eager):
+                result = PlanBuilder().evaluate(config, context, B200)
+                assert result.accepted, (case, name, [v.message for v in result.violations])
