@@ -20,10 +20,10 @@
 // [B, S, H, Dh].  A query that sees no valid key writes a zero row.
 //
 // Layout: CTA = 64 query rows (4 warps x 16) of one (batch, head); KV tiles of
-// 64 keys are staged in shared memory, K row-major (key, dim) and V transposed
-// (dim, key) so that both MMA B fragments are single 32-bit loads.  Row
-// strides are padded by 8 elements, which makes the fragment loads free of
-// bank conflicts.  The grid lists all heads' last query blocks first, so that
+// 64 keys are staged in shared memory, K and V row-major (key, dim): K's B
+// fragments are single 32-bit loads, V's come transposed from ldmatrix .trans.
+// Row strides are padded by 8 elements, which makes both free of bank
+// conflicts.  The grid lists all heads' last query blocks first, so that
 // under a causal mask the longest blocks start first.  There are no waits on
 // other CTAs or on asynchronous copies: only __syncthreads.
 //
@@ -94,10 +94,9 @@ __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnA
   constexpr int OUT_TILES = DH / 8;          // n-tiles of the 16 x DH output
   constexpr int S_TILES = kMmaAttnKeys / 8;  // n-tiles of the 16 x 64 scores
   constexpr int KSTR = DH + 8;               // K row stride (elements)
-  constexpr int VSTR = kMmaAttnKeys + 8;     // transposed-V row stride (elements)
   constexpr int CHUNKS = kMmaAttnKeys * DH / 8;  // 16-byte chunks per K (or V) tile
   __shared__ __align__(16) __nv_bfloat16 k_s[kMmaAttnKeys * KSTR];
-  __shared__ __align__(16) __nv_bfloat16 vt_s[DH * VSTR];
+  __shared__ __align__(16) __nv_bfloat16 v_s[kMmaAttnKeys * KSTR];
   __shared__ float key_bias[kMmaAttnKeys];  // 0, or -inf for a padding key or one past S
 
   griddep_wait();
@@ -162,13 +161,7 @@ __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnA
           const int ci = is_v ? i - CHUNKS : i;
           const int key = ci / (DH / 8);
           const int c = (ci % (DH / 8)) * 8;
-          if (!is_v) {
-            *reinterpret_cast<uint4*>(&k_s[key * KSTR + c]) = v;
-          } else {
-            const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) vt_s[(c + e) * VSTR + key] = ve[e];
-          }
+          *reinterpret_cast<uint4*>(&(is_v ? v_s : k_s)[key * KSTR + c]) = v;
         });
     if (threadIdx.x < kMmaAttnKeys) {
       const int key = k0 + threadIdx.x;
@@ -248,8 +241,15 @@ __global__ void __launch_bounds__(kMmaAttnThreads) attention_mma_kernel(MmaAttnA
       const uint32_t a[4] = {pf[2 * kk][0], pf[2 * kk][1], pf[2 * kk + 1][0], pf[2 * kk + 1][1]};
 #pragma unroll
       for (int i = 0; i < OUT_TILES; ++i) {
-        const __nv_bfloat16* vrow = &vt_s[(i * 8 + g) * VSTR + kk * 16];
-        mma_m16n8k16_bf16(o[i], a, ld_u32(vrow + 2 * t), ld_u32(vrow + 8 + 2 * t));
+        // V is row-major (key, dim) in shared memory; ldmatrix .trans hands each
+        // lane the (2t, 2t+1; g) key pairs of the B fragment.  Lanes 0-7 give the
+        // rows of keys kk*16 + 0..7, lanes 8-15 those of kk*16 + 8..15.
+        uint32_t b0, b1;
+        const uint32_t addr = smem_u32(&v_s[(kk * 16 + (lane & 15)) * KSTR + i * 8]);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];\n"
+                     : "=r"(b0), "=r"(b1)
+                     : "r"(addr));
+        mma_m16n8k16_bf16(o[i], a, b0, b1);
       }
     }
   }
