@@ -49,7 +49,6 @@ for _p in (str(PACKAGE_DIR), str(REPO)):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 WORKLOAD = dict(batch_size=8, seq_len=2048, d_model=1024, num_heads=16, ffn_dim=4096, num_layers=2, causal=True)
