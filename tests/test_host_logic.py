@@ -167,6 +167,30 @@ def test_shipped_registry_parses() -> None:
             ConfigSpec.from_dict(entry["config"])
 
 
+def test_every_deployed_entry_compiles_for_its_shape() -> None:
+    """A deployed config the plan builder rejects would silently fall back to
+    the default program on the device it was measured on."""
+    import json
+
+    from solution.plan import ExecutionContext
+    from solution.plan_builder import HardwareCapabilities, PlanBuilder
+
+    document = json.loads((PACKAGE_DIR / "deployment" / "deployed_configs.json").read_text())
+    for bundle in document["bundles"]:
+        for entry in bundle["entries"]:
+            shape = ShapeFingerprint.from_dict(entry["shape"])
+            config = ConfigSpec.from_dict(entry["config"])
+            context = ExecutionContext(
+                batch_size=shape.batch_size, seq_len=shape.seq_len, d_model=shape.qkv_dim,
+                num_heads=shape.heads, causal=shape.causal, device=torch.device("cuda", 0),
+                dtype=getattr(torch, shape.dtype), training=False, grad_enabled=False,
+                input_contiguous=True, has_valid_token_mask=False, mask_compatible=True,
+                ffn_dim=shape.ffn_dim, num_layers=shape.layers,
+            )
+            result = PlanBuilder().evaluate(config, context, HardwareCapabilities.sm100())
+            assert result.accepted, (shape, [v.message for v in result.violations])
+
+
 # ------------------------------------------------------------------ C ABI
 
 def _header_functions() -> list[str]:
