@@ -208,6 +208,22 @@ def test_library_loads_and_exports_every_declared_symbol() -> None:
     assert lib.b200tx_abi_version() == _native.ABI_VERSION
 
 
+def test_ctypes_declarations_match_the_header_arity() -> None:
+    """Every declared entry point is bound with as many arguments as the header
+    gives it (a missing or extra ctypes argument would shift every later one)."""
+
+    text = (REPO / "include" / "b200tx.h").read_text()
+    lib = _native.load()
+    declared = re.findall(r"\bint\s+(b200tx_[a-z0-9_]+)\s*\(([^;]*?)\);", text, flags=re.S)
+    assert len(declared) >= 15
+    for name, params in declared:
+        params = params.strip()
+        arity = 0 if params in ("", "void") else params.count(",") + 1
+        argtypes = getattr(lib, name).argtypes
+        assert argtypes is not None, name
+        assert len(argtypes) == arity, (name, len(argtypes), arity)
+
+
 def test_argument_errors_are_reported_before_any_launch() -> None:
     lib = _native.load()
     rc = lib.b200tx_linear(None, None, None, None, 1, 128, 256, 64, 0, None)
