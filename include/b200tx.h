@@ -213,8 +213,8 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
 
 /*
  * The projection that closes a block branch fused with the residual add and
- * LayerNorm after it, for d_model (cols) 32, 64 or 128 (one row per warp
- * row group; warp-level tensor-core MMAs):
+ * LayerNorm after it, for d_model (cols) 32, 64 or 128 (CTAs of 16 rows whose
+ * four warps split the columns; warp-level tensor-core MMAs):
  *     u = x[rows, inner] . w[cols, inner]^T + bias[cols]   (rounded to update_dtype)
  *     r = residual_in + u;  normed = LayerNorm(r) * gamma + beta
  * x, w BF16 row-major; bias, gamma, beta F32; residual_in in_dtype (F32 or
