@@ -17,10 +17,21 @@ rank's time.
                in pinned host memory: H2D copy of x, forward, D2H copy of the
                whole output, every step, on three overlapping CUDA streams.
 ``roofline``   the dominant kernel (by time) of the step, timed live with
-               CUDA events around its launches inside the timed region.
-``cpu_baseline`` the CPU oracle (numpy fp32 restatement of the reference
-               forward) on one batch row, on this host's cores.
-``--impl reference`` times that CPU restatement alone, as the reference arm.
+               CUDA events around its launches; peak = the measured burst
+               bf16 GEMM rate (tensor-bound) or copy bandwidth (HBM-bound).
+``workloads``  the other BASELINE configs on the same N GPUs, each with its
+               own ms_per_step, clocks and peak memory: C3 (batch-sharded,
+               weak), C4 (1 GPU, else head-sharded tp2 groups x batch
+               replicas), C5 (the 32 x 100 000-token rows split over the
+               ranks, streamed).
+``tp_parity``  (N >= 2) the head-sharded forward (NCCL and peer-memory
+               reductions) against the reference's CPU forward.
+``cpu_baseline`` the reference's own PyTorch CPU forward
+               (official.BaselineTransformer, installed in baseline/_ref) on
+               one batch row, on all host cores; ``reference_parity`` compares
+               this run's GPU output row with it.  Without the install, the
+               numpy restatement in oracle/ (kind "port").
+``--impl reference`` times that CPU forward alone, as the reference arm.
 ``--kernel NAME`` times one libb200tx kernel alone on its C2-shaped operands
                (attention, qkv, out_proj, ffn_in, ffn_out, residual_norm) and
                prints its own JSON line; ncu profiles in profiles/ use this mode.
@@ -185,47 +196,126 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(steps: int = 1, warmup: int = 0) -> dict:
-    """The oracle forward on one batch row of the workload, on this host's cores."""
+REFERENCE_INSTALL = REPO / "baseline" / "_ref"
+# The head-sharded parity check of N >= 2 runs (groups of two ranks): small
+# enough that the reference's CPU forward takes well under a second.
+TP_PARITY_SPEC = dict(batch_size=2, seq_len=256, d_model=512, num_heads=8, ffn_dim=2048, num_layers=2, causal=True)
+TP_PARITY_SEED = 11
+PARITY_MAX_ABS = 2e-2
+PARITY_REL_L2 = 1e-2
 
-    from oracle import OfficialConfig, official_input, official_state_dict
-    from oracle.reference_forward import transformer_forward
-    from oracle.weights import state_to_numpy
 
-    try:
-        from threadpoolctl import threadpool_info
+def _host_threads() -> int:
+    """Use every host core for the CPU legs, whatever torchrun's
+    OMP_NUM_THREADS=1 says; returns the thread count."""
 
-        threads = max((info.get("num_threads", 1) for info in threadpool_info()), default=1)
-    except Exception:  # noqa: BLE001
-        threads = os.cpu_count() or 1
-    cfg = OfficialConfig(**WORKLOAD)
-    state = state_to_numpy(official_state_dict(cfg, seed=WEIGHT_SEED))
-    x = official_input(cfg, INPUT_SEED, batch_rows=slice(0, 1)).numpy()
-    kwargs = dict(num_heads=cfg.num_heads, num_layers=cfg.num_layers, causal=cfg.causal)
-    for _ in range(warmup):
-        transformer_forward(x, state, **kwargs)
-    times = []
-    for _ in range(max(1, steps)):
-        start = time.perf_counter()
-        transformer_forward(x, state, **kwargs)
-        times.append(time.perf_counter() - start)
-    per_step = statistics.median(times)
-    tokens = cfg.seq_len
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    return threads
+
+
+def _reference_module():  # noqa: ANN202
+    """The reference's official harness (official/torch_transformer_benchmark.py)
+    from its install in baseline/_ref, or None when it is not installed.  Only
+    the CPU legs below use it."""
+
+    if not (REFERENCE_INSTALL / "official" / "torch_transformer_benchmark.py").exists():
+        return None
+    path = str(REFERENCE_INSTALL)
+    if path not in sys.path:
+        # Appended: the package's own `solution` and `deployment` stay first;
+        # `official` exists only in the reference install.
+        sys.path.append(path)
+    import importlib
+
+    return importlib.import_module("official.torch_transformer_benchmark")
+
+
+def reference_cpu_forward(spec: dict, x: torch.Tensor, steps: int, warmup: int) -> dict:
+    """Time the reference's own CPU forward on ``x`` ([rows, S, D] fp32).
+
+    ``official.BaselineTransformer`` built after ``torch.manual_seed(0)`` (the
+    weights of every GPU run here), timed by the reference's own
+    ``benchmark_once`` (perf_counter_ns around each forward on CPU, official
+    :477-506) on all host cores.  Without the reference install the numpy
+    restatement of the same forward (oracle/) is timed instead (kind "port").
+    Returns the timing and the output of the forward.
+    """
+
+    threads = _host_threads()
+    rows, seq = int(x.shape[0]), int(x.shape[1])
+    ref = _reference_module()
+    if ref is not None:
+        config = ref.TransformerConfig(**{**spec, "batch_size": rows})
+        saved = torch.get_rng_state()
+        torch.manual_seed(WEIGHT_SEED)
+        model = ref.BaselineTransformer(config).eval()
+        torch.set_rng_state(saved)
+        mask = torch.ones(rows, seq, dtype=torch.bool)
+        with torch.inference_mode():
+            output = model(x, mask)
+        if warmup > 1:
+            ref.benchmark_once(model, x, mask, warmup - 1, torch.device("cpu"))
+        samples_ms = ref.benchmark_once(model, x, mask, max(1, steps), torch.device("cpu"))
+        kind = "reference"
+        what = "official.BaselineTransformer fp32 forward (the reference's PyTorch CPU path, from baseline/_ref)"
+        output = output.numpy()
+    else:
+        from threadpoolctl import threadpool_limits
+
+        from oracle import OfficialConfig, official_state_dict
+        from oracle.reference_forward import transformer_forward
+        from oracle.weights import state_to_numpy
+
+        cfg = OfficialConfig(**{**spec, "batch_size": rows})
+        state = state_to_numpy(official_state_dict(cfg, seed=WEIGHT_SEED))
+        kwargs = dict(num_heads=cfg.num_heads, num_layers=cfg.num_layers, causal=cfg.causal)
+        xs = x.numpy()
+        with threadpool_limits(threads):
+            output = transformer_forward(xs, state, **kwargs)
+            for _ in range(max(0, warmup - 1)):
+                transformer_forward(xs, state, **kwargs)
+            samples_ms = []
+            for _ in range(max(1, steps)):
+                start = time.perf_counter_ns()
+                transformer_forward(xs, state, **kwargs)
+                samples_ms.append((time.perf_counter_ns() - start) / 1e6)
+        kind = "port"
+        what = "numpy fp32 restatement of the reference forward (reference install absent)"
+    per_step = statistics.median(samples_ms) / 1000.0
     return {
-        "value": tokens / per_step,
+        "value": rows * seq / per_step,
         "unit": UNIT,
-        "cores": int(threads),
-        "kind": "port",
-        "sample": f"oracle (numpy fp32) forward of 1 of the 8 batch rows ({tokens} tokens), median of {len(times)}",
+        "cores": threads,
+        "kind": kind,
+        "sample": f"{what}: {rows} batch row(s) x {seq} tokens per sample, median of {len(samples_ms)}",
         "seconds_per_sample": per_step,
+        "output": output,
     }
 
 
+def _errors(got: torch.Tensor | object, ref: object) -> dict:
+    import numpy as np
+
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    diff = got - ref
+    max_abs = float(np.abs(diff).max())
+    rel = float(np.linalg.norm(diff) / max(np.linalg.norm(ref), 1e-30))
+    return {"max_abs": max_abs, "rel_l2": rel, "ok": max_abs <= PARITY_MAX_ABS and rel <= PARITY_REL_L2}
+
+
 def run_reference(args: argparse.Namespace) -> None:
+    """The reference arm: the reference's own CPU forward on one batch row of
+    the C2 workload per step (rank 0 only under torchrun)."""
+
     rank = _env_int("RANK", 0)
     if rank != 0:
         return
-    base = cpu_baseline(steps=args.steps, warmup=min(args.warmup, 1))
+    from workloads import WorkloadConfig, seeded_input
+
+    x = seeded_input(WorkloadConfig(**WORKLOAD), INPUT_SEED)[:1].contiguous()
+    base = reference_cpu_forward(WORKLOAD, x, steps=args.steps, warmup=min(args.warmup, 2))
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -271,21 +361,21 @@ def _c4_tp(args: argparse.Namespace, batch: int, world: int) -> int:
     return tp if world % tp == 0 else world
 
 
-def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, world: int):
+def _workload_input(name: str, args: argparse.Namespace, spec: dict, seed: int, rank: int, world: int):
     """This rank's input rows and the parallel mode of the workload."""
 
     from solution.runtimes.sharded import batch_shard_bounds
     from workloads import WorkloadConfig, seeded_input, seeded_row
 
     cfg = WorkloadConfig(**spec)
-    if args.workload == "c4" and world > 1:
+    if name == "c4" and world > 1:
         # Head-sharded tensor parallel over groups of --tp ranks; the
         # world // tp replicas split the batch rows between them.
         tp = _c4_tp(args, cfg.batch_size, world)
         start, stop = batch_shard_bounds(cfg.batch_size, rank // tp, world // tp)
         x = seeded_input(cfg, seed)[start:stop].contiguous()
         return x, "heads", "strong", cfg.batch_size * cfg.seq_len
-    if args.workload == "c5":
+    if name == "c5":
         # Batch-sharded capacity run: the 32 rows (seed 4 + row) split over ranks.
         start, stop = batch_shard_bounds(cfg.batch_size, rank, world)
         rows = [seeded_row(cfg, seed, r) for r in range(start, stop)]
@@ -295,33 +385,68 @@ def _workload_input(args: argparse.Namespace, spec: dict, seed: int, rank: int, 
     return seeded_input(cfg, seed + rank), "batch", "weak", world * cfg.batch_size * cfg.seq_len
 
 
-def run_gpu(args: argparse.Namespace) -> None:
-    world = _env_int("WORLD_SIZE", 1)
-    rank = _env_int("RANK", 0)
-    local_rank = _env_int("LOCAL_RANK", 0)
-    if args.gpus != world and world > 1:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import datetime
+GEMM_VARIANT_NAMES = {0: "1SM", 1: "PAIR", 2: "WARP"}
+ATTENTION_VARIANT_NAMES = {0: "PAIRED", 1: "SINGLE", 2: "QUAD", 3: "PERSISTENT", 4: "DUO"}
 
-        import torch.distributed as dist_mod
 
-        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-        dist = dist_mod
+def _program(model, runner) -> dict:  # noqa: ANN001
+    """The program that ran: its config id, where the config came from
+    (a deployed entry for this environment and shape, or the default), the
+    runtime and the kernel variant of each launch."""
 
-    from solution import _native
+    config = model.active_config
+    schedule = config.schedule
+
+    def gemm(launch) -> str:  # noqa: ANN001
+        return GEMM_VARIANT_NAMES[launch.kernel_variant if launch is not None else 1]
+
+    program = {
+        "config_id": config.config_id,
+        "source": model.active_config_source,
+        "runtime": schedule.runtime.value,
+        "attention": config.program.attention.value,
+        "attention_variant": (
+            ATTENTION_VARIANT_NAMES[schedule.attention_launch.kernel_variant]
+            if schedule.attention_launch is not None
+            else None
+        ),
+        "gemm": {
+            "qkv": gemm(schedule.qkv_launch),
+            "out_proj": gemm(schedule.attention_output_projection_launch),
+            "ffn_in": gemm(schedule.ffn_input_launch),
+            "ffn_out": gemm(schedule.ffn_launch),
+        },
+    }
+    if runner is not model:
+        # The head-sharded runner launches its own fixed program.
+        program = {"runner": type(runner).__name__, "reduction": runner.reduction,
+                   "attention_variant": "QUAD", "gemm": "PAIR", "runtime": "eager"}
+    return program
+
+
+class _Context(SimpleNamespace):
+    """What every workload of one bench run shares: flags, ranks, device."""
+
+
+def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bool) -> dict:
+    """Time ``steps`` forwards of one BASELINE workload on every rank.
+
+    Every rank takes the same collective steps in the same order.  With
+    ``full`` (the headline workload) it also runs the per-kernel event pass
+    for the roofline and the end-to-end host pipeline; the other workloads
+    run a one-step kernel pass (single-GPU program only) for their attention
+    time.  Returns rank-local results and the max-over-ranks times.
+    """
+
     from solution.runtimes.sharded import TensorParallelTransformer
     from solution.transformer import KernelEventRecorder
     from workloads import WorkloadConfig
 
-    _native.device_check()
-    spec, seed, workload_name = WORKLOADS[args.workload]
+    args, dist, rank, world, device = ctx.args, ctx.dist, ctx.rank, ctx.world, ctx.device
+    spec, seed, title = WORKLOADS[name]
     cfg = WorkloadConfig(**spec)
     model = build_model(device, spec)
-    x_cpu, parallel, scaling, total_tokens = _workload_input(args, spec, seed, rank, world)
+    x_cpu, parallel, scaling, total_tokens = _workload_input(name, args, spec, seed, rank, world)
     tp = 1
     if parallel == "heads":
         from solution.runtimes.sharded import tensor_parallel_groups
@@ -329,18 +454,21 @@ def run_gpu(args: argparse.Namespace) -> None:
         tp = _c4_tp(args, cfg.batch_size, world)
         group, _, _ = tensor_parallel_groups(tp)
         partials = torch.bfloat16 if args.tp_partials == "bf16" else torch.float32
-        if args.tp_reduction == "auto":
-            args.tp_reduction = "peer" if tp == 2 else "nccl"
+        reduction = args.tp_reduction if args.tp_reduction != "auto" else ("peer" if tp == 2 else "nccl")
+        # The error word is read once after all steps (device_error below),
+        # not after every step, so the host keeps running ahead of the GPU.
         runner = TensorParallelTransformer(
-            model, group=group, partial_dtype=partials, reduction=args.tp_reduction
+            model, group=group, partial_dtype=partials, reduction=reduction, check_peer_errors=False
         )
     else:
+        reduction = None
         runner = model
-    x_host = x_cpu.pin_memory()
+    x_host = x_cpu.pin_memory() if full else None
+    x_dev = (x_host if full else x_cpu).to(device)
     del x_cpu
-    x_dev = x_host.to(device)
     big_input = x_dev.numel() * x_dev.element_size() > 2 * L2_FLUSH_BYTES
     flush = None if big_input else torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    torch.cuda.synchronize(device)
     torch.cuda.reset_peak_memory_stats(device)
 
     def barrier() -> None:
@@ -348,18 +476,22 @@ def run_gpu(args: argparse.Namespace) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
+    first_row = None
     with torch.inference_mode():
-        for _ in range(max(3, args.warmup)):
-            runner(x_dev)
+        for i in range(warmup):
+            y = runner(x_dev)
+            if i == 0 and full and rank == 0 and world == 1:
+                first_row = y[:1].float().cpu()
+            del y
         torch.cuda.synchronize()
 
         # Timed steps: nothing but the forward between the step's two events,
         # so consecutive kernels keep their programmatic launch overlap.
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         barrier()
-        with ClockSampler(local_rank) as clocks:
-            for i in range(args.steps):
+        with ClockSampler(ctx.local_rank) as clocks:
+            for i in range(steps):
                 if flush is not None:
                     flush.zero_()
                 starts[i].record()
@@ -372,72 +504,77 @@ def run_gpu(args: argparse.Namespace) -> None:
         peak_gb = torch.cuda.max_memory_allocated(device) / 2**30
 
         # Per-kernel times for the kernel table and the roofline: the same
-        # steps again with CUDA events around every launch (these events sit
-        # between kernels, so this pass is not the step time).
-        # A graph runtime replays its launches where the events cannot sit, so
-        # this pass runs the same program with the eager runtime.
-        from dataclasses import replace as _replace
-
-        from solution.config import RuntimeBackend
-
-        graph_config = None
-        if runner is model and model.active_config.schedule.runtime in (
-            RuntimeBackend.CUDA_GRAPH,
-            RuntimeBackend.BATCH_TILED_CUDA_GRAPH,
-        ):
-            graph_config = model.active_config
-            model.configure_execution(
-                config=_replace(
-                    graph_config,
-                    schedule=_replace(graph_config.schedule, runtime=RuntimeBackend.EAGER, batch_tile_size=None),
-                )
-            )
-        recorder = KernelEventRecorder()
+        # program again with CUDA events around every launch (these events sit
+        # between kernels, so this pass is not the step time).  A graph
+        # runtime replays its launches where the events cannot sit, so this
+        # pass runs the same program under the eager runtime.
+        kernel_ms: dict[str, list[float]] = {}
+        kernel_steps = steps if full else 1
         if runner is model:
+            from dataclasses import replace as _replace
+
+            from solution.config import RuntimeBackend
+
+            graph_config = None
+            if model.active_config.schedule.runtime in (
+                RuntimeBackend.CUDA_GRAPH,
+                RuntimeBackend.BATCH_TILED_CUDA_GRAPH,
+            ):
+                graph_config = model.active_config
+                graph_source = model.active_config_source
+                model.configure_execution(
+                    config=_replace(
+                        graph_config,
+                        schedule=_replace(graph_config.schedule, runtime=RuntimeBackend.EAGER, batch_tile_size=None),
+                    )
+                )
+            recorder = KernelEventRecorder()
             model.kernel_events = recorder
-        for _ in range(args.steps):
-            if flush is not None:
-                flush.zero_()
-            runner(x_dev)
-        torch.cuda.synchronize()
-        model.kernel_events = None
-        kernel_ms = recorder.durations_ms()
-        if graph_config is not None:
-            model.configure_execution(config=graph_config)
+            for _ in range(kernel_steps):
+                if flush is not None:
+                    flush.zero_()
+                runner(x_dev)
+            torch.cuda.synchronize()
+            model.kernel_events = None
+            kernel_ms = recorder.durations_ms()
+            if graph_config is not None:
+                model.configure_execution(config=graph_config)
+                model.active_config_source = graph_source
 
-        # End to end through the public host-batch API (HostPipeline) from
-        # pinned host memory: every step copies its input H2D, runs the
-        # forward and copies the whole output D2H; the three run on separate
-        # streams, so step i's forward overlaps step i+1's copy-in and step
-        # i-1's copy-out.  Timed by CUDA events from before the first copy-in
-        # to after the last copy-out.
-        from solution.runtimes.host_pipeline import HostPipeline
+        e2e_ms = 0.0
+        out_host = None
+        if full:
+            # End to end through the public host-batch API (HostPipeline) from
+            # pinned host memory: every step copies its input H2D, runs the
+            # forward and copies the whole output D2H; the three run on
+            # separate streams, so step i's forward overlaps step i+1's
+            # copy-in and step i-1's copy-out.  Timed by CUDA events from
+            # before the first copy-in to after the last copy-out.
+            from solution.runtimes.host_pipeline import HostPipeline
 
-        pipe = HostPipeline(runner, device, depth=3)
-        outs_host = [torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory() for _ in range(2)]
-        for i in range(3):
-            pipe.submit(x_host, outs_host[i % 2])
-        pipe.synchronize()
-        barrier()
-        e2e_start = torch.cuda.Event(enable_timing=True)
-        e2e_end = torch.cuda.Event(enable_timing=True)
-        e2e_start.record(pipe.copy_in)
-        for i in range(args.steps):
-            pipe.submit(x_host, outs_host[i % 2])
-        e2e_end.record(pipe.copy_out)
-        pipe.synchronize()
-        barrier()
-        e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
-        out_host = outs_host[0]
+            pipe = HostPipeline(runner, device, depth=3)
+            outs_host = [torch.empty(x_host.shape, dtype=x_host.dtype).pin_memory() for _ in range(2)]
+            for i in range(3):
+                pipe.submit(x_host, outs_host[i % 2])
+            pipe.synchronize()
+            barrier()
+            e2e_start = torch.cuda.Event(enable_timing=True)
+            e2e_end = torch.cuda.Event(enable_timing=True)
+            e2e_start.record(pipe.copy_in)
+            for i in range(steps):
+                pipe.submit(x_host, outs_host[i % 2])
+            e2e_end.record(pipe.copy_out)
+            pipe.synchronize()
+            barrier()
+            e2e_ms = e2e_start.elapsed_time(e2e_end) / steps
+            out_host = outs_host[0]
 
     total_ms = sum(step_ms)
     stats = torch.tensor([total_ms, e2e_ms, peak_gb], dtype=torch.float64, device=device)
     if dist is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     total_ms_max, e2e_ms_max, peak_gb_max = stats.tolist()
-    ms_per_step = total_ms_max / args.steps
-    value = total_tokens * args.steps / (total_ms_max / 1000.0)
-    e2e_value = total_tokens / (e2e_ms_max / 1000.0)
+    ms_per_step = total_ms_max / steps
 
     b_loc = x_dev.shape[0]
     s, d, f, layers = cfg.seq_len, cfg.d_model, cfg.ffn_dim, cfg.num_layers
@@ -462,96 +599,223 @@ def run_gpu(args: argparse.Namespace) -> None:
         "residual_norm": ((2 * layers - 1) * 12.0 + 6.0 + io_bytes) * m * d,
         "initial_norm": (io_bytes + 2.0) * m * d,
     }
-    per_role = {role: sum(v) / args.steps for role, v in kernel_ms.items()}
-    launches = {role: len(v) // args.steps for role, v in kernel_ms.items()}
+    per_role = {role: sum(v) / kernel_steps for role, v in kernel_ms.items()}
+    launches = {role: len(v) // kernel_steps for role, v in kernel_ms.items()}
+    peaks, peak_source = _peaks()
     roofline = None
     if per_role:
         dominant = max(per_role, key=per_role.get)
-        peaks, peak_source = _peaks()
         role_s = per_role[dominant] / 1000.0
         n_launch = max(1, launches[dominant])
         if dominant in flops_per_step:
             achieved = flops_per_step[dominant] / role_s / 1e12
-            peak = float(peaks["bf16_tflops_sustained"])
+            # Kernels timed inside a step of a few milliseconds: the burst
+            # GEMM peak (the sustained figure is for seconds-long loops).
+            peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "unit": "TFLOP/s", "kernel": dominant,
                         "algorithmic_per_launch": flops_per_step[dominant] / n_launch}
+            peak_name = "bf16_tflops (burst)"
         else:
             achieved = bytes_per_step[dominant] / role_s / 1e9
             peak = float(peaks["hbm_gbs"])
             roofline = {"bound": "hbm", "unit": "GB/s", "kernel": dominant,
                         "algorithmic_per_launch": bytes_per_step[dominant] / n_launch}
+            peak_name = "hbm_gbs"
         roofline.update(
             achieved=achieved,
             peak=peak,
-            peak_source=f"{peak_source} ({'bf16_tflops_sustained' if roofline['bound'] == 'tensor' else 'hbm_gbs'})",
+            peak_source=f"{peak_source} ({peak_name})",
             frac=achieved / peak,
-            traffic=_profile_traffic(dominant) if args.workload == "c2" else None,
+            traffic=_profile_traffic(dominant) if name == "c2" else None,
             avg_launch_ms=per_role[dominant] / n_launch,
         )
     attention_s = per_role.get("attention", 0.0) / 1000.0
-    kernel_table = {
-        role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]} for role in sorted(per_role)
-    }
+    attention_tflops = flops_per_step["attention"] / attention_s / 1e12 if attention_s else None
     model_flops = (total_tokens / cfg.seq_len) * layers * (2.0 * s * s * d + 8.0 * s * d * d + 4.0 * s * d * f)
-    launches_per_step = 1 + 7 * layers
+    parallelism = (
+        (f"dp{world // tp} x " if tp < world else "")
+        + (
+            f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials after out-proj and FFN-down)"
+            if reduction == "nccl"
+            else f"tp{tp} (head-sharded, bf16 partials summed over NVLink peer memory inside the residual "
+            "LayerNorm after out-proj and FFN-down)"
+        )
+        if parallel == "heads"
+        else f"dp{world} (batch-sharded, no collective)"
+    )
+    result = {
+        "workload": title,
+        "value": total_tokens * steps / (total_ms_max / 1000.0),
+        "unit": UNIT,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": ms_per_step,
+        "p50_latency_ms": statistics.median(step_ms),
+        "scaling": scaling,
+        "global_batch": cfg.batch_size * (world if scaling == "weak" else 1),
+        "seq_len": cfg.seq_len,
+        "parallelism": parallelism,
+        "l2": "inputs larger than L2" if big_input else "flushed (256 MB write) before every timed step",
+        "program": _program(model, runner),
+        "attention_tflops": attention_tflops,
+        "attention_frac_of_burst": attention_tflops / float(peaks["bf16_tflops"]) if attention_tflops else None,
+        "model_tflops": model_flops / (ms_per_step / 1000.0) / 1e12,
+        "peak_memory_gb_per_gpu": peak_gb_max,
+        "clocks": clocks.summary(),
+        # rank-local extras for the headline line
+        "_kernels": {role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]}
+                     for role in sorted(per_role)},
+        "_roofline": roofline,
+        "_launches": int(sum(len(v) for v in kernel_ms.values())),
+        "_e2e_ms": e2e_ms_max,
+        "_total_tokens": total_tokens,
+        "_first_row": first_row,
+        "_h2d": int(x_host.numel() * x_host.element_size()) if x_host is not None else 0,
+        "_d2h": int(out_host.numel() * out_host.element_size()) if out_host is not None else 0,
+    }
+    if hasattr(runner, "close"):
+        runner.close()
+    del runner, model, x_dev, x_host, flush
+    torch.cuda.empty_cache()
+    barrier()
+    return result
+
+
+def tensor_parallel_parity(ctx: _Context) -> dict:
+    """Head-sharded forward (groups of two ranks, NCCL and peer reductions)
+    of a small workload against the reference's CPU forward on the same
+    seeded input and weights.  Every rank runs its group's forward; rank 0
+    compares its result.  Returns rank 0's report (empty elsewhere)."""
+
+    from solution.runtimes.sharded import TensorParallelTransformer, tensor_parallel_groups
+    from workloads import WorkloadConfig, seeded_input
+
+    dist, rank, device = ctx.dist, ctx.rank, ctx.device
+    cfg = WorkloadConfig(**TP_PARITY_SPEC)
+    group, _, _ = tensor_parallel_groups(2)
+    model = build_model(device, TP_PARITY_SPEC)
+    x = seeded_input(cfg, TP_PARITY_SEED)
+    outputs = {}
+    for reduction in ("nccl", "peer"):
+        runner = TensorParallelTransformer(model, group=group, partial_dtype=torch.bfloat16, reduction=reduction)
+        with torch.inference_mode():
+            outputs[reduction] = runner(x.to(device)).float().cpu()
+        torch.cuda.synchronize()
+        runner.close()
+    dist.barrier()
+    del model
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return {}
+    reference = reference_cpu_forward(TP_PARITY_SPEC, x, steps=1, warmup=1)
+    report = {
+        "workload": "B2 S256 D512 H8(Dh64) F2048 L2 causal, x seed 11, fp32 I/O",
+        "group": "tp2 (ranks 0-1)",
+        "against": reference["kind"],
+        "tolerance": {"max_abs": PARITY_MAX_ABS, "rel_l2": PARITY_REL_L2},
+    }
+    for reduction, y in outputs.items():
+        report[reduction] = _errors(y.numpy(), reference["output"])
+    return report
+
+
+def run_gpu(args: argparse.Namespace) -> None:
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local_rank = _env_int("LOCAL_RANK", 0)
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        dist = dist_mod
+
+    from solution import _native
+
+    _native.device_check()
+    ctx = _Context(args=args, dist=dist, rank=rank, world=world, local_rank=local_rank, device=device)
+    warmup = max(3, args.warmup)
+    main = measure_workload(ctx, args.workload, args.steps, warmup, full=True)
+    extras: dict[str, dict] = {}
+    if args.workload == "c2" and args.extras != "none":
+        for name in args.extras.split(","):
+            steps = {"c3": args.steps, "c4": min(args.steps, 10), "c5": min(args.steps, 3)}.get(name, args.steps)
+            extras[name] = measure_workload(ctx, name, steps, 3, full=False)
+    tp_parity = tensor_parallel_parity(ctx) if world >= 2 and not args.skip_tp_parity else None
+    device_error = _native.device_error(clear=True)
+
     if rank == 0:
+        spec = WORKLOADS[args.workload][0]
+        launches_per_step = 1 + 7 * spec["num_layers"]
         line = {
             "metric": METRIC,
-            "value": value,
+            "value": main["value"],
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
-            "warmup": max(3, args.warmup),
-            "ms_per_step": ms_per_step,
-            "p50_latency_ms": statistics.median(step_ms),
+            "warmup": warmup,
+            "ms_per_step": main["ms_per_step"],
+            "p50_latency_ms": main["p50_latency_ms"],
             "higher_is_better": True,
-            "scaling": scaling,
+            "scaling": main["scaling"],
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: x ~ N(0,1) from the BASELINE seeds (CPU generator), reference default-init weights seed 0",
             "config": {
-                "workload": workload_name,
-                "global_batch": cfg.batch_size * (world if scaling == "weak" else 1),
-                "seq_len": cfg.seq_len,
-                "parallelism": (
-                    (f"dp{world // tp} x " if tp < world else "")
-                    + (
-                        f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials"
-                        " after out-proj and FFN-down)"
-                        if args.tp_reduction == "nccl"
-                        else f"tp{tp} (head-sharded, bf16 partials summed over NVLink peer memory"
-                        " inside the residual LayerNorm after out-proj and FFN-down)"
-                    )
-                    if parallel == "heads"
-                    else f"dp{world} (batch-sharded, no collective)"
-                ),
+                "workload": main["workload"],
+                "global_batch": main["global_batch"],
+                "seq_len": main["seq_len"],
+                "parallelism": main["parallelism"],
                 "io_dtype": "float32 in/out, bf16 GEMM/attention operands, fp32 accumulation and residual",
-                "l2": "inputs larger than L2" if big_input else "flushed (256 MB write) before every timed step",
-                "runtime": model.active_config.schedule.runtime.value,
+                "l2": main["l2"],
+                "runtime": main["program"].get("runtime"),
+                "program": main["program"],
             },
-            "attention_tflops": flops_per_step["attention"] / attention_s / 1e12 if attention_s else None,
-            "model_tflops": model_flops / (ms_per_step / 1000.0) / 1e12,
-            "peak_memory_gb_per_gpu": peak_gb_max,
-            "kernels": kernel_table,
-            "roofline": roofline,
+            "attention_tflops": main["attention_tflops"],
+            "attention_frac_of_burst": main["attention_frac_of_burst"],
+            "model_tflops": main["model_tflops"],
+            "peak_memory_gb_per_gpu": main["peak_memory_gb_per_gpu"],
+            "kernels": main["_kernels"],
+            "roofline": main["_roofline"],
             "e2e": {
-                "value": e2e_value,
+                "value": main["_total_tokens"] / (main["_e2e_ms"] / 1000.0),
                 "unit": UNIT,
-                "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
-                "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
-                "ms_per_step": e2e_ms_max,
+                "h2d_bytes_per_step": main["_h2d"],
+                "d2h_bytes_per_step": main["_d2h"],
+                "ms_per_step": main["_e2e_ms"],
             },
-            "gpu_launches": int(sum(len(v) for v in kernel_ms.values())) or launches_per_step * args.steps,
-            "clocks": clocks.summary(),
+            "gpu_launches": main["_launches"] or launches_per_step * args.steps,
+            "clocks": main["clocks"],
+            "device_error": device_error,
         }
-        if world == 1 and args.workload == "c2" and not args.skip_cpu_baseline:
-            line["cpu_baseline"] = {
-                k: v for k, v in cpu_baseline(steps=1).items() if k in ("value", "unit", "cores", "kind", "sample")
+        if extras:
+            line["workloads"] = {
+                name: {k: v for k, v in result.items() if not k.startswith("_")} for name, result in extras.items()
             }
+        if tp_parity is not None:
+            line["tp_parity"] = tp_parity
+        if world == 1 and args.workload == "c2" and not args.skip_cpu_baseline:
+            # The reference's CPU forward on row 0 of the same C2 batch, timed
+            # on this host's cores (>= 3 samples); its output is also the
+            # parity check of this run's GPU output row.
+            from workloads import WorkloadConfig, seeded_input
+
+            x0 = seeded_input(WorkloadConfig(**WORKLOAD), INPUT_SEED)[:1].contiguous()
+            base = reference_cpu_forward(WORKLOAD, x0, steps=3, warmup=1)
+            line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            if main["_first_row"] is not None:
+                line["reference_parity"] = {
+                    "rows": "batch row 0 of the C2 input",
+                    "against": base["kind"],
+                    **_errors(main["_first_row"].numpy(), base["output"]),
+                }
         print(json.dumps(line), flush=True)
-    if hasattr(runner, "close"):
-        runner.close()
-    del runner
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -810,6 +1074,11 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("native", "reference"), default="native")
     parser.add_argument("--skip-cpu-baseline", action="store_true")
+    parser.add_argument("--extras", default="c3,c4,c5",
+                        help="with the c2 headline: the other BASELINE configs measured after it and reported "
+                             "under 'workloads' on the same line ('none' to skip)")
+    parser.add_argument("--skip-tp-parity", action="store_true",
+                        help="N >= 2: skip the head-sharded parity check against the reference's CPU forward")
     parser.add_argument("--workload", choices=[*sorted(WORKLOADS), "official"], default="c2",
                         help="BASELINE config to run (c2 is the bench line the driver records), "
                              "or 'official' for the reference's official-shapes table")

@@ -69,6 +69,15 @@ const char* b200tx_last_error(void);
  * Synchronises the device; diagnostic use only. */
 int b200tx_device_error(int clear, unsigned int* code_out);
 
+/* Stream-ordered read of the current device's error word: copies it into
+ * *word (pinned host or device memory) on `stream`, after the work queued
+ * before it.  Does not clear it and does not synchronise; the caller waits on
+ * the stream (or an event) before reading *word.  The word is sticky: once a
+ * wait has run out, later kernels on the device stop early until
+ * b200tx_device_error(clear = 1) resets it.  No reference counterpart (the
+ * reference's Triton kernels have no device-side waits). */
+int b200tx_device_error_async(unsigned int* word, cudaStream_t stream);
+
 /* Multiprocessor count and compute capability of the current device; returns
  * B200TX_ERR_UNSUPPORTED unless it is a compute capability 10.0 device. */
 int b200tx_device_check(int* sm_count_out, int* cc_major_out, int* cc_minor_out);

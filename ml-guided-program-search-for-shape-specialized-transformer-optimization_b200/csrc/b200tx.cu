@@ -230,6 +230,14 @@ int b200tx_device_error(int clear, unsigned int* code_out) {
   return B200TX_OK;
 }
 
+int b200tx_device_error_async(unsigned int* word, cudaStream_t stream) {
+  if (word == nullptr) return fail(B200TX_ERR_INVALID_ARGUMENT, "device_error_async: null destination");
+  cudaError_t err = cudaMemcpyFromSymbolAsync(word, b200tx::g_device_error, sizeof(unsigned int), 0,
+                                              cudaMemcpyDefault, stream);
+  if (err != cudaSuccess) return cuda_fail(err, "device_error_async: cudaMemcpyFromSymbolAsync");
+  return B200TX_OK;
+}
+
 }  // extern "C"
 
 namespace {

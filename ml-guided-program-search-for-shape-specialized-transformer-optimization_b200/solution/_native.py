@@ -48,6 +48,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b200tx_last_error.argtypes = []
     lib.b200tx_device_error.restype = ctypes.c_int
     lib.b200tx_device_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    lib.b200tx_device_error_async.restype = ctypes.c_int
+    lib.b200tx_device_error_async.argtypes = [_c_void_p, _c_void_p]
     lib.b200tx_device_check.restype = ctypes.c_int
     lib.b200tx_device_check.argtypes = [
         ctypes.POINTER(ctypes.c_int),
@@ -293,7 +295,16 @@ def _stream(device: torch.device) -> int:
     it exists: building a ``torch.cuda.Stream`` object per launch is a
     measurable share of the host time of a small eager forward."""
 
-    index = device.index if device.index is not None else torch.cuda.current_device()
+    current = torch.cuda.current_device()
+    index = device.index if device.index is not None else current
+    if index != current:
+        # libb200tx resolves its per-device state (SM count, kernel
+        # attributes, error word) from the current device, so a launch onto
+        # another device's stream would run with the wrong state.
+        raise RuntimeError(
+            f"libb200tx launches on the current device: the operands are on cuda:{index} "
+            f"while cuda:{current} is current (use torch.cuda.device(...))"
+        )
     if _RAW_STREAM is not None:
         return int(_RAW_STREAM(index))
     return torch.cuda.current_stream(device).cuda_stream
@@ -328,6 +339,17 @@ def device_error(clear: bool = True) -> int:
     code = ctypes.c_uint(0)
     _check(lib.b200tx_device_error(int(clear), ctypes.byref(code)), "b200tx_device_error")
     return int(code.value)
+
+
+def device_error_async(word: torch.Tensor) -> None:
+    """Queue a copy of the device error word into ``word`` (one int32 element,
+    pinned host or device memory) on the current stream of the current device.
+    Nothing is synchronised; read ``word`` after the stream got there."""
+
+    if word.numel() != 1 or word.element_size() != 4:
+        raise ValueError("the error word destination is one 32-bit element")
+    device = word.device if word.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    _check(load().b200tx_device_error_async(word.data_ptr(), _stream(device)), "b200tx_device_error_async")
 
 
 def residual_layer_norm(
@@ -695,6 +717,7 @@ __all__ = [
     "attention_generic",
     "device_check",
     "device_error",
+    "device_error_async",
     "dtype_code",
     "library_available",
     "library_path",

@@ -30,6 +30,14 @@ solution/shape14/executor.py:12-49; the reference itself is single-GPU):
     LayerNorm kernel itself waits for the peers' epochs and sums all partials
     over NVLink loads while it normalises -- the reduction is fused into the
     kernel that consumes it, and no all-reduce moves the data twice.
+
+Failures inside a step.  On the NCCL path a departed peer ends the step's
+collective with an error after the process group's timeout.  On the peer
+path no collective runs inside the step: the LayerNorm's wait for a peer's
+epoch is bounded (2 s) and, when it runs out, records its code in the device
+error word and writes nothing; ``forward`` then reads the word after the
+step and raises ``PeerWaitTimeout`` (``check_peer_errors``).  Failures
+between steps are caught on the host by ``StepLiveness``.
 """
 
 from __future__ import annotations
@@ -47,6 +55,28 @@ from ..kernels import (
 from .liveness import StepLiveness
 
 HEAD_DIM = 64
+
+
+class PeerWaitTimeout(RuntimeError):
+    """A device-side wait of the tensor-parallel step ran out: a peer of the
+    group did not publish its partial in time, so the step's output was not
+    written."""
+
+    def __init__(self, code: int) -> None:
+        self.code = code
+        super().__init__(
+            f"a device wait ran out during the tensor-parallel step (device error 0x{code:x}); the output "
+            "was not written.  The error word stays set (later kernels on this device stop early) until "
+            "solution._native.device_error(clear=True)."
+        )
+
+
+def raise_on_error_word(word: int) -> None:
+    """Raise PeerWaitTimeout when the device error word read after a step is set."""
+
+    code = int(word) & 0xFFFFFFFF
+    if code != 0:
+        raise PeerWaitTimeout(code)
 
 
 class _DeviceBuffer:
@@ -268,6 +298,7 @@ class TensorParallelTransformer:
         partial_dtype: torch.dtype = torch.float32,
         reduction: str = "nccl",
         liveness: StepLiveness | None = None,
+        check_peer_errors: bool = True,
     ) -> None:
         import torch.distributed as dist
 
@@ -279,6 +310,8 @@ class TensorParallelTransformer:
             raise ValueError("reduction must be 'nccl' or 'peer'")
         self.reduction = reduction
         self.liveness = liveness
+        self.check_peer_errors = check_peer_errors
+        self._error_word: torch.Tensor | None = None
         self._peer: PeerReduction | None = None
         self.group = group
         self.rank = dist.get_rank(group)
@@ -426,7 +459,29 @@ class TensorParallelTransformer:
                 hidden, shard.w_2, shard.b_2, residual, next_norm,
                 last=last, normalized_out=out.view(rows, d_model) if last else normed,
             )
+        if peer is not None and self.check_peer_errors:
+            self._raise_on_device_error()
         return out
+
+    def _raise_on_device_error(self) -> None:
+        """Wait for this step and read the device error word.
+
+        The peer LayerNorm waits (bounded, 2 s) for every peer's epoch; a wait
+        that runs out writes nothing and records kErrPeerWait (0x301) in the
+        device error word instead.  No collective runs inside a peer-path
+        step, so this check is what turns a departed or stalled peer into an
+        exception rather than an output that was never written.  It costs one
+        host synchronisation per forward; ``check_peer_errors=False`` leaves
+        the check to the caller (``_native.device_error()``).
+        """
+
+        from .. import _native
+
+        if self._error_word is None:
+            self._error_word = torch.zeros(1, dtype=torch.int32).pin_memory()
+        _native.device_error_async(self._error_word)
+        torch.cuda.current_stream(self.device).synchronize()
+        raise_on_error_word(int(self._error_word.item()))
 
     __call__ = forward
 
@@ -434,8 +489,10 @@ class TensorParallelTransformer:
 __all__ = [
     "LayerShard",
     "PeerReduction",
+    "PeerWaitTimeout",
     "TensorParallelTransformer",
     "batch_shard_bounds",
+    "raise_on_error_word",
     "shard_layer",
     "tensor_parallel_groups",
 ]

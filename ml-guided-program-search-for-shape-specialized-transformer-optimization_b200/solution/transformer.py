@@ -295,6 +295,10 @@ class UserOptimizedTransformer(nn.Module):
         self._plan_builder = PlanBuilder()
         self._explicit_config: ConfigSpec | None = None
         self._active_config = portable_config(head_dim=int(config.d_model) // int(config.num_heads))
+        # Where the active config came from: "deployed" (an exact entry of
+        # deployment/deployed_configs.json for this environment and shape),
+        # "default" (no entry matched) or "explicit" (configure_execution).
+        self.active_config_source = "default"
         self._deployment_signature: tuple[object, ...] | None = None
         self.kernel_events: KernelEventRecorder | None = None
         self.register_load_state_dict_post_hook(_after_weight_load)
@@ -405,6 +409,7 @@ class UserOptimizedTransformer(nn.Module):
         if selected != self._active_config:
             self._invalidate_runtime_state()
         self._active_config = selected
+        self.active_config_source = "deployed" if resolved is not None else "default"
         self._deployment_signature = signature
 
     @property
@@ -420,6 +425,7 @@ class UserOptimizedTransformer(nn.Module):
         self._invalidate_runtime_state()
         self._explicit_config = config
         self._active_config = config
+        self.active_config_source = "explicit"
         self._deployment_signature = None
 
     def _execution_context(
@@ -832,6 +838,12 @@ class UserOptimizedTransformer(nn.Module):
     def forward(
         self, x: torch.Tensor, valid_token_mask: torch.Tensor | None = None
     ) -> torch.Tensor:
+        if x.is_cuda and x.device.index != torch.cuda.current_device():
+            # The kernel library works on the current device: make it the
+            # input's for this call (a model on cuda:1 called while cuda:0 is
+            # current).
+            with torch.cuda.device(x.device):
+                return self.forward(x, valid_token_mask)
         self._resolve_default_config(x)
         valid_token_mask = self._effective_valid_token_mask(x, valid_token_mask)
         plan = self._cached_execution_plan(x, valid_token_mask)

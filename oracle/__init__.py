@@ -17,10 +17,12 @@ checks this restatement against them.
 from .reference_forward import (
     attention_core,
     attention_reference,
+    attention_rows,
     ffn_reference,
     gelu_erf,
     layer_norm,
     transformer_forward,
+    transformer_forward_tail,
 )
 from .weights import OfficialConfig, official_input, official_state_dict
 
@@ -28,10 +30,12 @@ __all__ = [
     "OfficialConfig",
     "attention_core",
     "attention_reference",
+    "attention_rows",
     "ffn_reference",
     "gelu_erf",
     "layer_norm",
     "official_input",
     "official_state_dict",
     "transformer_forward",
+    "transformer_forward_tail",
 ]

@@ -113,6 +113,113 @@ def attention_core(
     return out
 
 
+def attention_rows(
+    q: np.ndarray, k: np.ndarray, v: np.ndarray, query_rows: np.ndarray, causal: bool = True
+) -> np.ndarray:
+    """The score/softmax/PV core of official :97-112 for selected query rows of one head.
+
+    ``k``, ``v`` are [S, Dh] float32 arrays of one (batch, head); ``q`` holds
+    the queries of the rows whose absolute positions are ``query_rows``
+    ([len(query_rows), Dh]).  Each row attends to the keys at positions <= its
+    own (causal) or to all keys.  The cost is
+    len(query_rows) x S x Dh, so a few rows of an S = 100 000 sequence are
+    checked in well under a second.
+    """
+
+    rows = np.asarray(query_rows, dtype=np.int64)
+    scale = np.float32(q.shape[-1] ** -0.5)
+    scores = (q @ k.T) * scale
+    if causal:
+        above = np.arange(k.shape[0])[None, :] > rows[:, None]
+        scores = np.where(above, np.float32(-np.inf), scores)
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    probs = np.exp(scores, dtype=np.float32)
+    probs /= probs.sum(axis=-1, keepdims=True)
+    return (probs @ v).astype(np.float32, copy=False)
+
+
+def _threaded_causal_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, query_block: int = 512) -> np.ndarray:
+    """attention_core for [H, S, Dh] arrays, causal, one head per worker thread.
+
+    Query block [a, b) only multiplies against keys [0, b): the keys above the
+    block's last row are masked to -inf by the reference and contribute exact
+    zeros, so leaving them out changes no value.  numpy releases the GIL in
+    its BLAS calls and ufuncs, so the heads run in parallel on the host cores.
+    """
+
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    heads, seq, head_dim = q.shape
+    scale = np.float32(head_dim**-0.5)
+    out = np.empty_like(q, dtype=np.float32)
+
+    def one_head(h: int) -> None:
+        for start in range(0, seq, query_block):
+            stop = min(start + query_block, seq)
+            scores = (q[h, start:stop] @ k[h, :stop].T) * scale
+            above = np.arange(stop)[None, :] > np.arange(start, stop)[:, None]
+            scores = np.where(above, np.float32(-np.inf), scores)
+            scores -= scores.max(axis=-1, keepdims=True)
+            probs = np.exp(scores, dtype=np.float32)
+            probs /= probs.sum(axis=-1, keepdims=True)
+            out[h, start:stop] = probs @ v[h, :stop]
+
+    with threadpool_limits(1), ThreadPoolExecutor(max_workers=min(heads, os.cpu_count() or 1)) as pool:
+        list(pool.map(one_head, range(heads)))
+    return out
+
+
+def transformer_forward_tail(
+    x: np.ndarray,
+    state: dict[str, np.ndarray],
+    *,
+    num_heads: int,
+    num_layers: int,
+    tail: int,
+) -> np.ndarray:
+    """The last ``tail`` positions of BaselineTransformer.forward (official
+    :148-172, causal, no mask) for ONE batch row x of shape [1, S, D].
+
+    Every layer but the last runs on all S positions (the next layer's keys
+    and values depend on all of them).  In the last layer only the keys and
+    values are computed for all positions; the queries, attention rows,
+    out-projection, FFN and final LayerNorm run on the last ``tail`` rows,
+    whose values do not depend on the other rows' outputs of that layer.
+    Same operations in the same order as transformer_forward, so the result
+    equals transformer_forward(x)[:, -tail:] up to BLAS summation order.
+    """
+
+    x = np.asarray(x, dtype=np.float32)[0]
+    seq, d_model = x.shape
+    head_dim = d_model // num_heads
+
+    def split(t: np.ndarray) -> np.ndarray:
+        return np.ascontiguousarray(t.reshape(t.shape[0], num_heads, head_dim).transpose(1, 0, 2))
+
+    for i in range(num_layers):
+        p = f"layers.{i}"
+        a = f"{p}.attention"
+        normed = layer_norm(x, state[f"{p}.norm1.weight"], state[f"{p}.norm1.bias"])
+        k = split(_linear(normed, state[f"{a}.k_proj.weight"], state[f"{a}.k_proj.bias"]))
+        v = split(_linear(normed, state[f"{a}.v_proj.weight"], state[f"{a}.v_proj.bias"]))
+        if i < num_layers - 1:
+            q = split(_linear(normed, state[f"{a}.q_proj.weight"], state[f"{a}.q_proj.bias"]))
+            context = _threaded_causal_attention(q, k, v)
+        else:
+            rows = np.arange(seq - tail, seq)
+            x = x[rows]
+            q = split(_linear(normed[rows], state[f"{a}.q_proj.weight"], state[f"{a}.q_proj.bias"]))
+            context = np.stack([attention_rows(q[h], k[h], v[h], rows) for h in range(num_heads)])
+        merged = context.transpose(1, 0, 2).reshape(-1, d_model)
+        x = x + _linear(merged, state[f"{a}.out_proj.weight"], state[f"{a}.out_proj.bias"])
+        normed = layer_norm(x, state[f"{p}.norm2.weight"], state[f"{p}.norm2.bias"])
+        x = x + ffn_reference(normed, state, p)
+    return layer_norm(x, state["final_norm.weight"], state["final_norm.bias"]).astype(np.float32, copy=False)
+
+
 def ffn_reference(x: np.ndarray, state: dict[str, np.ndarray], prefix: str) -> np.ndarray:
     """ffn_out(GELU(ffn_in(x))) (official :141)."""
 
@@ -157,9 +264,11 @@ def transformer_forward(
 __all__ = [
     "EPS",
     "attention_core",
+    "attention_rows",
     "attention_reference",
     "ffn_reference",
     "gelu_erf",
     "layer_norm",
     "transformer_forward",
+    "transformer_forward_tail",
 ]

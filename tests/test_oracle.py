@@ -16,12 +16,15 @@ from conftest import load_golden, parity_errors
 
 from oracle import (
     OfficialConfig,
+    attention_core,
     attention_reference,
+    attention_rows,
     gelu_erf,
     layer_norm,
     official_input,
     official_state_dict,
     transformer_forward,
+    transformer_forward_tail,
 )
 from oracle.weights import per_row_input, state_checksum, state_to_numpy
 
@@ -127,3 +130,28 @@ def test_per_row_seeds_are_distinct() -> None:
     assert a.shape == (1, 8, 16)
     assert not torch.equal(a, b)
     assert torch.equal(a, official_input(OfficialConfig(1, 8, 16, 1, 32, 1), 4))
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_rows_equal_the_blocked_core(causal: bool) -> None:
+    """The selected-rows attention used by the long-context GPU tests gives the
+    rows of the query-blocked core (same op order; BLAS order only)."""
+
+    rng = np.random.default_rng(3)
+    q, k, v = rng.standard_normal((3, 1, 1, 700, 64)).astype(np.float32)
+    rows = np.array([0, 1, 127, 128, 511, 512, 699])
+    full = attention_core(q, k, v, causal)[0, 0, rows]
+    got = attention_rows(q[0, 0, rows], k[0, 0], v[0, 0], rows, causal=causal)
+    assert np.abs(full - got).max() < 1e-6
+
+
+def test_tail_forward_equals_the_full_forward_tail() -> None:
+    """transformer_forward_tail (every position of the first layers, the tail
+    rows of the last) reproduces the last rows of the whole-row oracle."""
+
+    cfg = OfficialConfig(1, 700, 256, 4, 1024, 2, True)
+    state = state_to_numpy(official_state_dict(cfg, seed=0))
+    x = official_input(cfg, 5).numpy()
+    full = transformer_forward(x, state, num_heads=4, num_layers=2)
+    tail = transformer_forward_tail(x, state, num_heads=4, num_layers=2, tail=130)
+    assert np.abs(full[0, -130:] - tail).max() < 1e-5

@@ -237,3 +237,66 @@ def test_tensor_parallel_groups_split_the_world_into_replicas() -> None:
     assert [g[0] for g in got] == [1.0, 1.0, 5.0, 5.0]
     assert [g[1] for g in got] == [0, 0, 1, 1]
     assert all(g[2] == 2 and g[3] == 1 for g in got)
+
+
+def test_error_word_turns_into_peer_wait_timeout() -> None:
+    """The post-step check of the peer path: a clear word passes, a set one
+    raises with the device's code."""
+
+    from solution.runtimes.sharded import PeerWaitTimeout, raise_on_error_word
+
+    raise_on_error_word(0)
+    with pytest.raises(PeerWaitTimeout) as info:
+        raise_on_error_word(0x301)
+    assert info.value.code == 0x301
+    assert isinstance(info.value, RuntimeError)
+
+
+@pytest.mark.gpu
+def test_peer_layer_norm_wait_runs_out_and_is_reported() -> None:
+    """A peer that never publishes its epoch: the flag array is zero and no
+    kernel ever writes it.  The fused LayerNorm's bounded wait (2 s) runs out,
+    the kernel records kErrPeerWait and writes nothing, and the stream-ordered
+    read of the error word that TensorParallelTransformer.forward makes after
+    a peer-path step sees the code.  One GPU; no peer memory is involved (both
+    'partials' are local buffers), and the context stays usable."""
+
+    import time
+
+    from solution import _native
+    from solution.runtimes.sharded import PeerWaitTimeout, raise_on_error_word
+
+    dev = torch.device("cuda", 0)
+    _native.device_error(clear=True)
+    rows, cols = 64, 256
+    g = torch.Generator().manual_seed(0)
+    resid = torch.randn(rows, cols, generator=g).to(dev)
+    normed = torch.full((rows, cols), 7.0, dtype=torch.bfloat16, device=dev)
+    gamma = torch.ones(cols, device=dev)
+    beta = torch.zeros(cols, device=dev)
+    partials = [torch.zeros(rows, cols, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    flags = torch.zeros(8, dtype=torch.int32, device=dev)
+    word = torch.zeros(1, dtype=torch.int32).pin_memory()
+    start = time.monotonic()
+    _native.residual_layer_norm_peer(
+        resid, [p.data_ptr() for p in partials], 0, flags.data_ptr(), 1, None, normed, gamma, beta, 1e-5
+    )
+    _native.device_error_async(word)
+    torch.cuda.synchronize()
+    elapsed = time.monotonic() - start
+    assert int(word.item()) == 0x301
+    assert 1.0 < elapsed < 30.0
+    assert torch.all(normed == 7.0), "a timed-out wait must not write"
+    with pytest.raises(PeerWaitTimeout):
+        raise_on_error_word(int(word.item()))
+    # Sticky until cleared; afterwards kernels run normally again.
+    assert _native.device_error(clear=True) == 0x301
+    assert _native.device_error(clear=True) == 0
+    flags.fill_(1)
+    _native.residual_layer_norm_peer(
+        resid, [p.data_ptr() for p in partials], 0, flags.data_ptr(), 1, None, normed, gamma, beta, 1e-5
+    )
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+    ref = torch.nn.functional.layer_norm(resid, (cols,), eps=1e-5)
+    assert torch.allclose(normed.float(), ref, atol=3e-2)
