@@ -1,73 +1,73 @@
-"""Batch-tiled execution through one fixed-shape CUDA graph.
+"""Batch-tiled CUDA-graph replay over slices of the caller's own input.
 
-Same contract as the reference's ``BatchTiledGraphReplay``
-(solution/runtimes/batch_tiled_graph.py:10-127): batch rows are independent in
-every operator of the block, so one graph captured for ``tile_size`` rows is
-replayed over consecutive tiles of the logical batch; a short tail tile is
-zero-padded and only its valid rows are copied out.
+Batch rows are independent in every operator of the block, so a batch can
+run as consecutive tiles of ``tile_size`` rows (the reference's
+``BatchTiledGraphReplay``, solution/runtimes/batch_tiled_graph.py:10-127,
+replays one graph over tiles staged through a static buffer, zero-padding the
+last one).  Here each tile of a bound input is its own capture, made on the
+tile's slice of the caller's tensor (rows are contiguous in [B, S, D], so a
+tile is a view, never a copy); a short last tile is captured at its own size,
+so nothing is padded or computed twice.  After each tile's replay its final
+launch (see ``cuda_graph``) writes the tile's rows of the call's output
+directly.
+
+All tile captures of all bindings share one graph memory pool.  A tile's
+replay and its final launch run back to back on one stream, and the buffers
+that final launch reads stay allocated for the binding's lifetime, so the
+shared pool holds one tile's transient activations plus each tile's small
+set of live buffers, and no replay overwrites another tile's live buffers.
 """
 
 from __future__ import annotations
 
+from collections import OrderedDict
 from collections.abc import Callable
 
 import torch
 
-Forward = Callable[[torch.Tensor, None], torch.Tensor]
+from .cuda_graph import Program, capture_program
 
 
 class BatchTiledGraphReplay:
-    """Run independent batch tiles through one captured forward graph."""
+    """Run independent batch tiles of a bound input through per-tile graphs."""
 
-    def __init__(self, tile_size: int) -> None:
+    def __init__(self, tile_size: int, *, max_bindings: int = 2) -> None:
         if isinstance(tile_size, bool) or not isinstance(tile_size, int):
             raise TypeError("tile_size must be an integer")
         if tile_size <= 0:
             raise ValueError("tile_size must be positive")
+        if max_bindings < 1:
+            raise ValueError("max_bindings must be at least 1")
         self._tile_size = tile_size
-        self._signature: tuple[object, ...] | None = None
-        self._graph: torch.cuda.CUDAGraph | None = None
-        self._static_input: torch.Tensor | None = None
-        self._static_output: torch.Tensor | None = None
+        self.max_bindings = max_bindings
+        # key -> (held input, [(rows, graph, finish), ...])
+        self._bindings: OrderedDict[
+            tuple[object, ...],
+            tuple[torch.Tensor, list[tuple[slice, torch.cuda.CUDAGraph, Callable[[torch.Tensor], torch.Tensor]]]],
+        ] = OrderedDict()
+        self._layout: tuple[object, ...] | None = None
+        self._pool: object | None = None
 
     @property
     def tile_size(self) -> int:
         return self._tile_size
 
-    @staticmethod
-    def _sig(value: torch.Tensor) -> tuple[object, ...]:
-        return (value.device, value.dtype, tuple(value.shape), tuple(value.stride()))
+    @property
+    def captured(self) -> bool:
+        return bool(self._bindings)
 
-    def _capture(self, function: Forward, value: torch.Tensor) -> None:
-        static_input = torch.zeros(
-            (self._tile_size, *value.shape[1:]), device=value.device, dtype=value.dtype
-        )
-        first = min(value.shape[0], self._tile_size)
-        static_input[:first].copy_(value[:first])
-        current = torch.cuda.current_stream(value.device)
-        side = torch.cuda.Stream(device=value.device)
-        side.wait_stream(current)
-        with torch.cuda.stream(side), torch.inference_mode():
-            for _ in range(3):
-                function(static_input, None)
-        current.wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.inference_mode(), torch.cuda.graph(graph, stream=side):
-            static_output = function(static_input, None)
-        current.wait_stream(side)
-        if not isinstance(static_output, torch.Tensor):
-            raise TypeError("batch-tiled graph function must return a Tensor")
-        if static_output.shape != static_input.shape:
-            raise RuntimeError("batch-tiled graph output shape must match its input")
-        if static_output.device != value.device or static_output.dtype != value.dtype:
-            raise RuntimeError("batch-tiled graph output must keep the input device and dtype")
-        self._signature = self._sig(value)
-        self._graph = graph
-        self._static_input = static_input
-        self._static_output = static_output
+    def _bind(self, program: Program, value: torch.Tensor) -> list:
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        tiles = []
+        for start in range(0, value.shape[0], self._tile_size):
+            rows = slice(start, min(start + self._tile_size, value.shape[0]))
+            graph, finish = capture_program(program, value[rows], None, self._pool)
+            tiles.append((rows, graph, finish))
+        return tiles
 
-    def run(self, function: Forward, value: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
-        """Replay every tile and assemble one independent full output."""
+    def run(self, program: Program, value: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
+        """Replay every tile of ``value`` (capturing on first use) into one fresh output."""
 
         if value.device.type != "cuda":
             raise ValueError("batch-tiled CUDA graph requires a CUDA input")
@@ -77,31 +77,30 @@ class BatchTiledGraphReplay:
             raise ValueError("batch-tiled CUDA graph requires more than one tile")
         if mask is not None:
             raise ValueError("batch-tiled CUDA graph does not accept a token mask")
-        signature = self._sig(value)
-        if self._graph is not None and signature != self._signature:
+        layout = (value.device, value.dtype, tuple(value.shape))
+        if self._layout is not None and layout != self._layout:
             raise RuntimeError("batch-tiled CUDA graph supports one full input signature")
-        if self._graph is None:
-            self._capture(function, value)
-        assert self._graph is not None and self._static_input is not None
-        assert self._static_output is not None
+        key = (value.data_ptr(), layout)
+        entry = self._bindings.get(key)
+        if entry is None:
+            tiles = self._bind(program, value)
+            if len(self._bindings) >= self.max_bindings:
+                self._bindings.popitem(last=False)
+            entry = (value, tiles)
+            self._bindings[key] = entry
+            self._layout = layout
+        else:
+            self._bindings.move_to_end(key)
         output = torch.empty_like(value)
-        for start in range(0, value.shape[0], self._tile_size):
-            stop = min(start + self._tile_size, value.shape[0])
-            count = stop - start
-            if count == self._tile_size:
-                self._static_input.copy_(value[start:stop])
-            else:
-                self._static_input.zero_()
-                self._static_input[:count].copy_(value[start:stop])
-            self._graph.replay()
-            output[start:stop].copy_(self._static_output[:count])
+        for rows, graph, finish in entry[1]:
+            graph.replay()
+            finish(output[rows])
         return output
 
     def release(self) -> None:
-        self._graph = None
-        self._static_input = None
-        self._static_output = None
-        self._signature = None
+        self._bindings.clear()
+        self._layout = None
+        self._pool = None
 
 
 __all__ = ["BatchTiledGraphReplay"]

@@ -1,19 +1,24 @@
-"""Ordered microbatch execution (reference: solution/shape14/executor.py:12-49).
+"""Streamed execution: a long-sequence batch as microbatches written in place.
 
-The logical batch runs as consecutive microbatches of ``microbatch_size`` rows
-into one preallocated output.  Each chunk is a contiguous slice of the input
-(batch rows are contiguous in [B, S, D]), so no input copy is made; each chunk
-result is copied into its rows of the output and its activations are released
-before the next chunk, which bounds peak memory by one microbatch.
+The reference runs its streamed (Shape-14) batch as ordered microbatches into
+one preallocated output (solution/shape14/executor.py:12-49).  Here every
+microbatch's forward writes its rows of the output itself: the program is
+called as ``forward_chunk(chunk, mask_chunk, out=output_rows)``, where the
+chunk and the output rows are contiguous views (batch rows are contiguous in
+[B, S, D]).  Nothing is copied, and the activations of one microbatch are
+released (back to the caching allocator) before the next one runs, which
+bounds peak memory by one microbatch: about 2.6 GB per 100 000-token row at
+D = 1024, F = 4096.
 """
 
 from __future__ import annotations
 
 from collections.abc import Callable
+from typing import Any
 
 import torch
 
-ChunkForward = Callable[[torch.Tensor, torch.Tensor | None], torch.Tensor]
+ChunkForward = Callable[..., Any]
 
 
 def execute_streamed(
@@ -24,29 +29,33 @@ def execute_streamed(
     forward_chunk: ChunkForward,
     output: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Execute one logical batch as ordered, preallocated microbatches."""
+    """Run ``value`` ([B, S, D]) as B / microbatch_size ordered microbatches.
+
+    ``microbatch_size`` must divide B.  Returns ``output`` (allocated like
+    ``value`` when not given), each microbatch's rows written by its own
+    forward.
+    """
 
     if isinstance(microbatch_size, bool) or not isinstance(microbatch_size, int) or microbatch_size <= 0:
         raise ValueError("microbatch_size must be a positive integer")
-    batch_size = value.shape[0]
-    if batch_size <= 0:
+    batch = value.shape[0]
+    if batch <= 0:
         raise ValueError("streamed execution requires a non-empty batch")
-    if batch_size % microbatch_size:
+    if batch % microbatch_size:
         raise ValueError("microbatch_size must divide the batch size")
-    if valid_token_mask is not None and valid_token_mask.shape[0] != batch_size:
+    if valid_token_mask is not None and valid_token_mask.shape[0] != batch:
         raise ValueError("valid_token_mask batch dimension must match the input")
-
-    for start in range(0, batch_size, microbatch_size):
-        end = start + microbatch_size
-        mask_slice = None if valid_token_mask is None else valid_token_mask[start:end]
-        chunk = forward_chunk(value[start:end], mask_slice)
-        if output is None:
-            output = torch.empty(
-                (batch_size, *chunk.shape[1:]), dtype=chunk.dtype, device=chunk.device
-            )
-        output[start:end].copy_(chunk)
-        del chunk
-    assert output is not None
+    if not value.is_contiguous():
+        raise ValueError("streamed execution reads contiguous batch rows")
+    if output is None:
+        output = torch.empty_like(value)
+    elif output.shape != value.shape or not output.is_contiguous():
+        raise ValueError("output must be a contiguous tensor of the input's shape")
+    for start in range(0, batch, microbatch_size):
+        rows = slice(start, start + microbatch_size)
+        forward_chunk(
+            value[rows], None if valid_token_mask is None else valid_token_mask[rows], out=output[rows]
+        )
     return output
 
 

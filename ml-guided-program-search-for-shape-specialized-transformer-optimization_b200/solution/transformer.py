@@ -556,8 +556,19 @@ class UserOptimizedTransformer(nn.Module):
         plan: ExecutionPlan,
         *,
         observe: bool = True,
-    ) -> torch.Tensor:
-        """One pass of the planned program over ``value`` ([B, S, D], contiguous)."""
+        out: torch.Tensor | None = None,
+        defer_final: bool = False,
+    ) -> Any:
+        """One pass of the planned program over ``value`` ([B, S, D], contiguous).
+
+        Returns the output ([B, S, D] in the input's dtype; ``out`` when given).
+        With ``defer_final`` the output is not written yet: the return value
+        is ``finish(out)``, which launches the pass's last kernel (the final
+        residual LayerNorm, or the fused boundary that ends the last block)
+        into ``out``.  The graph runtimes capture everything before it and
+        call ``finish`` after each replay with a freshly allocated output, so
+        no captured buffer is ever copied out.
+        """
 
         observation = (
             _ExecutionObservation(config_id=plan.config_id)
@@ -601,7 +612,20 @@ class UserOptimizedTransformer(nn.Module):
         ffn_out_variant = gemm_variant(plan.ffn_launch)
 
         flat_in = value.reshape(rows, d_model)
-        output = torch.empty((batch, seq, d_model), dtype=value.dtype, device=device)
+
+        def finish(close: Any) -> Any:
+            """Run (or hand back) the closing launch of the pass."""
+
+            def into(target: torch.Tensor) -> torch.Tensor:
+                close(target.view(rows, d_model))
+                return target
+
+            if defer_final:
+                return into
+            return into(
+                out if out is not None else torch.empty((batch, seq, d_model), dtype=value.dtype, device=device)
+            )
+
         # Padding mask (official/torch_transformer_benchmark.py:105-121,
         # 143-144, 170-171): keys of padding tokens are masked in attention,
         # their attention output is dropped, each block's output rows and the
@@ -613,25 +637,25 @@ class UserOptimizedTransformer(nn.Module):
             key_valid = valid_token_mask.contiguous().view(torch.uint8)
             row_valid = key_valid.view(rows)
         if n_layers == 0:
-            if row_valid is None:
-                sm100_initial_layer_norm(
-                    flat_in,
-                    self.final_norm.kernel_norm(),
-                    out_dtype=value.dtype,
-                    normalized_out=output.view(rows, d_model),
-                )
-            else:
-                sm100_residual_layer_norm(
-                    flat_in,
-                    None,
-                    self.final_norm.kernel_norm(),
-                    final_boundary=True,
-                    out_dtype=value.dtype,
-                    normalized_out=output.view(rows, d_model),
-                    row_valid=row_valid,
-                    mask_mode=MASK_ZERO_NORMED,
-                )
-            return output
+
+            def close_norm_only(normalized_out: torch.Tensor) -> None:
+                if row_valid is None:
+                    sm100_initial_layer_norm(
+                        flat_in, self.final_norm.kernel_norm(), out_dtype=value.dtype, normalized_out=normalized_out
+                    )
+                else:
+                    sm100_residual_layer_norm(
+                        flat_in,
+                        None,
+                        self.final_norm.kernel_norm(),
+                        final_boundary=True,
+                        out_dtype=value.dtype,
+                        normalized_out=normalized_out,
+                        row_valid=row_valid,
+                        mask_mode=MASK_ZERO_NORMED,
+                    )
+
+            return finish(close_norm_only)
 
         residual = torch.empty((rows, d_model), dtype=torch.float32, device=device)
         normalized = torch.empty((rows, d_model), dtype=torch.bfloat16, device=device)
@@ -652,6 +676,92 @@ class UserOptimizedTransformer(nn.Module):
         )
 
         rec = self.kernel_events or _NO_RECORDER
+
+        def ffn_half(index: int, layer: _TransformerBlock, last: bool) -> Any:
+            """The FFN of block ``index`` up to its closing launch, which is
+            returned as ``close(normalized_out)``: the residual LayerNorm (or
+            the fused boundary) that adds the FFN update to the residual and
+            normalises with the next block's norm1, or the final norm after
+            the last block."""
+
+            w_1, b_1 = layer.ffn_in.shadow_parameters()
+            w_2, b_2 = layer.ffn_out.shadow_parameters()
+            next_norm = self.final_norm if last else self.layers[index + 1].norm1
+            boundary = dict(
+                final_boundary=last,
+                update_dtype=ffn_update,
+                out_dtype=value.dtype if last else torch.bfloat16,
+                residual_out=None if last else residual,
+                keep_residual=not last,
+                row_valid=row_valid,
+                mask_mode=MASK_ZERO_RESIDUAL | (MASK_ZERO_NORMED if last else 0),
+            )
+            if fused_mlp:
+
+                def close(normalized_out: torch.Tensor) -> None:
+                    # Each CTA stages its rows of `normalized` before it writes
+                    # them back normalised, so the in-place output is safe.
+                    token = rec.start("residual_norm")
+                    _, _, marker = sm100_mlp_residual_norm(
+                        normalized, w_1, b_1, w_2, b_2, residual, next_norm.kernel_norm(),
+                        normalized_out=normalized_out, **boundary,
+                    )
+                    rec.stop(token)
+                    _strict_backend_marker(
+                        marker,
+                        expected_marker=SM100_MLP_RESIDUAL_NORM_BACKEND,
+                        planned_backend=plan.ffn_backend.value,
+                    )
+
+                return close
+            token = rec.start("ffn_input_projection")
+            _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden, variant=ffn_in_variant)
+            rec.stop(token)
+            _strict_backend_marker(
+                marker,
+                expected_marker=SM100_LINEAR_GELU_BACKEND,
+                planned_backend=plan.ffn_input_projection_backend.value,
+            )
+            if fused_boundary:
+
+                def close(normalized_out: torch.Tensor) -> None:
+                    token = rec.start("residual_norm")
+                    _, _, marker = sm100_linear_residual_norm(
+                        hidden, w_2, b_2, residual, next_norm.kernel_norm(),
+                        normalized_out=normalized_out, **boundary,
+                    )
+                    rec.stop(token)
+                    _strict_backend_marker(
+                        marker,
+                        expected_marker=SM100_LINEAR_RESIDUAL_NORM_BACKEND,
+                        planned_backend=plan.residual_norm_backend.value,
+                    )
+
+                return close
+            token = rec.start("ffn_output_projection")
+            _, marker = sm100_linear(hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out, variant=ffn_out_variant)
+            rec.stop(token)
+            _strict_backend_marker(
+                marker,
+                expected_marker=SM100_LINEAR_BACKEND,
+                planned_backend=plan.ffn_output_projection_backend.value,
+            )
+            norm_args = {k: v for k, v in boundary.items() if k != "update_dtype"}
+
+            def close(normalized_out: torch.Tensor) -> None:
+                token = rec.start("residual_norm")
+                _, _, marker = sm100_residual_layer_norm(
+                    residual, ffn_out, next_norm.kernel_norm(), normalized_out=normalized_out, **norm_args
+                )
+                rec.stop(token)
+                _strict_backend_marker(
+                    marker,
+                    expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
+                    planned_backend=plan.residual_norm_backend.value,
+                )
+
+            return close
+
         token = rec.start("initial_norm")
         _, marker = sm100_initial_layer_norm(
             flat_in, self.layers[0].norm1.kernel_norm(), normalized_out=normalized
@@ -745,74 +855,10 @@ class UserOptimizedTransformer(nn.Module):
                     planned_backend=plan.residual_norm_backend.value,
                 )
             residual_source = residual
-            w_1, b_1 = layer.ffn_in.shadow_parameters()
-            w_2, b_2 = layer.ffn_out.shadow_parameters()
             last = index == n_layers - 1
-            next_norm = self.final_norm if last else self.layers[index + 1].norm1
-            boundary = dict(
-                final_boundary=last,
-                update_dtype=ffn_update,
-                out_dtype=value.dtype if last else torch.bfloat16,
-                residual_out=None if last else residual,
-                keep_residual=not last,
-                normalized_out=output.view(rows, d_model) if last else normalized,
-                row_valid=row_valid,
-                mask_mode=MASK_ZERO_RESIDUAL | (MASK_ZERO_NORMED if last else 0),
-            )
-            if fused_mlp:
-                # Each CTA stages its rows of `normalized` before it writes
-                # them back normalised, so the in-place output is safe.
-                token = rec.start("residual_norm")
-                _, _, marker = sm100_mlp_residual_norm(
-                    normalized, w_1, b_1, w_2, b_2, residual, next_norm.kernel_norm(), **boundary
-                )
-                rec.stop(token)
-                _strict_backend_marker(
-                    marker,
-                    expected_marker=SM100_MLP_RESIDUAL_NORM_BACKEND,
-                    planned_backend=plan.ffn_backend.value,
-                )
-            else:
-                token = rec.start("ffn_input_projection")
-                _, marker = sm100_linear(normalized, w_1, b_1, gelu=True, out=hidden, variant=ffn_in_variant)
-                rec.stop(token)
-                _strict_backend_marker(
-                    marker,
-                    expected_marker=SM100_LINEAR_GELU_BACKEND,
-                    planned_backend=plan.ffn_input_projection_backend.value,
-                )
-                if fused_boundary:
-                    token = rec.start("residual_norm")
-                    _, _, marker = sm100_linear_residual_norm(
-                        hidden, w_2, b_2, residual, next_norm.kernel_norm(), **boundary
-                    )
-                    rec.stop(token)
-                    _strict_backend_marker(
-                        marker,
-                        expected_marker=SM100_LINEAR_RESIDUAL_NORM_BACKEND,
-                        planned_backend=plan.residual_norm_backend.value,
-                    )
-                else:
-                    token = rec.start("ffn_output_projection")
-                    _, marker = sm100_linear(
-                        hidden, w_2, b_2, out_dtype=ffn_update, out=ffn_out, variant=ffn_out_variant
-                    )
-                    rec.stop(token)
-                    _strict_backend_marker(
-                        marker,
-                        expected_marker=SM100_LINEAR_BACKEND,
-                        planned_backend=plan.ffn_output_projection_backend.value,
-                    )
-                    token = rec.start("residual_norm")
-                    _, _, marker = sm100_residual_layer_norm(residual, ffn_out, next_norm.kernel_norm(), **{
-                        k: v for k, v in boundary.items() if k != "update_dtype"
-                    })
-                    rec.stop(token)
-                    _strict_backend_marker(
-                        marker,
-                        expected_marker=SM100_RESIDUAL_LAYER_NORM_BACKEND,
-                        planned_backend=plan.residual_norm_backend.value,
-                    )
+            close_block = ffn_half(index, layer, last)
+            if not last:
+                close_block(normalized)
             if observation is not None:
                 observation.record("qkv_projection", plan.qkv_projection_backend.value, qkv.dtype)
                 observation.record("attention", plan.attention_backend.value, qkv.dtype)
@@ -833,7 +879,7 @@ class UserOptimizedTransformer(nn.Module):
                 observation.record("residual_norm", plan.residual_norm_backend.value)
         if observation is not None:
             self._last_execution_observation = observation.to_signature(plan)
-        return output
+        return finish(close_block)
 
     def forward(
         self, x: torch.Tensor, valid_token_mask: torch.Tensor | None = None
@@ -849,8 +895,14 @@ class UserOptimizedTransformer(nn.Module):
         plan = self._cached_execution_plan(x, valid_token_mask)
         self._materialize_shadow_weights()
 
-        def eager(value: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
-            return self._forward_eager(value, mask, plan)
+        def program(
+            value: torch.Tensor,
+            mask: torch.Tensor | None,
+            *,
+            out: torch.Tensor | None = None,
+            defer_final: bool = False,
+        ) -> Any:
+            return self._forward_eager(value, mask, plan, out=out, defer_final=defer_final)
 
         with torch.inference_mode():
             if plan.use_streamed_execution:
@@ -860,7 +912,7 @@ class UserOptimizedTransformer(nn.Module):
                 if microbatch is None or microbatch <= 0:
                     raise RuntimeError("streamed plan is missing its microbatch size")
                 output = execute_streamed(
-                    x, valid_token_mask, microbatch_size=microbatch, forward_chunk=eager
+                    x, valid_token_mask, microbatch_size=microbatch, forward_chunk=program
                 )
                 self._mark_runtime(RuntimeBackend.STREAMED)
                 return output
@@ -869,7 +921,7 @@ class UserOptimizedTransformer(nn.Module):
                     raise RuntimeError("batch-tiled plan is missing its tile size")
                 if self._batch_tiled_graph_replay is None:
                     self._batch_tiled_graph_replay = BatchTiledGraphReplay(plan.batch_tile_size)
-                output = self._batch_tiled_graph_replay.run(eager, x, valid_token_mask)
+                output = self._batch_tiled_graph_replay.run(program, x, valid_token_mask)
                 self._mark_runtime(RuntimeBackend.BATCH_TILED_CUDA_GRAPH)
                 return output
             if plan.use_cuda_graph:
@@ -877,10 +929,10 @@ class UserOptimizedTransformer(nn.Module):
                     self._cuda_graph_replay = CudaGraphReplay(
                         reuse_unchanged_input=plan.reuse_unchanged_input
                     )
-                output = self._cuda_graph_replay.run(eager, x, valid_token_mask)
+                output = self._cuda_graph_replay.run(program, x, valid_token_mask)
                 self._mark_runtime(RuntimeBackend.CUDA_GRAPH)
                 return output
-            return eager(x, valid_token_mask)
+            return program(x, valid_token_mask)
 
     def _mark_runtime(self, runtime: RuntimeBackend) -> None:
         if self._execution_observation_enabled and self._last_execution_observation is not None:

@@ -91,15 +91,25 @@ def test_configure_execution_is_strict() -> None:
 def test_streamed_executor_order_and_slices() -> None:
     calls: list[tuple[int, int, bool]] = []
 
-    def forward(chunk: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
+    outputs: list[int] = []
+
+    def forward(chunk: torch.Tensor, mask: torch.Tensor | None, *, out: torch.Tensor) -> torch.Tensor:
+        # Each microbatch writes its own rows of the one output, in place.
         calls.append((int(chunk[0, 0, 0].item()), chunk.shape[0], mask is not None))
-        return chunk * 2
+        outputs.append(out.data_ptr())
+        torch.mul(chunk, 2, out=out)
+        return out
 
     x = torch.arange(6, dtype=torch.float32).view(6, 1, 1).expand(6, 2, 3).contiguous()
     mask = torch.ones(6, 2, dtype=torch.bool)
     out = execute_streamed(x, mask, microbatch_size=2, forward_chunk=forward)
     assert calls == [(0, 2, True), (2, 2, True), (4, 2, True)]
     assert torch.equal(out, x * 2)
+    row = out[0].numel() * out.element_size()
+    assert outputs == [out.data_ptr(), out.data_ptr() + 2 * row, out.data_ptr() + 4 * row]
+    given = torch.empty_like(x)
+    assert execute_streamed(x, None, microbatch_size=3, forward_chunk=forward) is not given
+    assert execute_streamed(x, None, microbatch_size=3, forward_chunk=forward, output=given) is given
     with pytest.raises(ValueError):
         execute_streamed(x, None, microbatch_size=4, forward_chunk=forward)
     with pytest.raises(ValueError):
@@ -145,6 +155,37 @@ def test_registry_round_trip(tmp_path: Path) -> None:
     publish_deployed_config(hardware=_hardware(), shape=shape, config=portable_config(), path=path)
     assert resolve_deployed_config(hardware=_hardware(), shape=shape, path=path) == portable_config()
     assert len(iter_deployed_configs(hardware=_hardware(), path=path)) == 1
+
+
+def test_registry_keeps_entry_order_and_sees_rewritten_files(tmp_path: Path) -> None:
+    """A replaced entry keeps its place, new shapes go last, a table of another
+    schema is started afresh, and the cached index follows the file when it
+    is rewritten behind the registry's back."""
+
+    import json
+
+    path = tmp_path / "deployed.json"
+    shapes = [ShapeFingerprint(b, 1024, 16, 2048, 2, True, 4096, "float32", 0.0, 1.0) for b in (1, 2, 4)]
+    graph = ConfigSpec(program=default_program(), schedule=default_schedule(RuntimeBackend.CUDA_GRAPH))
+    for shape in shapes:
+        publish_deployed_config(hardware=_hardware(), shape=shape, config=portable_config(), path=path)
+    publish_deployed_config(hardware=_hardware(), shape=shapes[1], config=graph, path=path)
+    pairs = iter_deployed_configs(hardware=_hardware(), path=path)
+    assert [shape for shape, _ in pairs] == shapes
+    assert [cfg for _, cfg in pairs] == [portable_config(), graph, portable_config()]
+    assert not list(tmp_path.glob("*.tmp"))  # the atomic write left no temporary behind
+
+    document = json.loads(path.read_text())
+    document["bundles"][0]["entries"] = document["bundles"][0]["entries"][:1]
+    path.write_text(json.dumps(document, indent=1))
+    assert resolve_deployed_config(hardware=_hardware(), shape=shapes[1], path=path) is None
+    assert resolve_deployed_config(hardware=_hardware(), shape=shapes[0], path=path) == portable_config()
+
+    path.write_text(json.dumps({"schema_version": 3, "bundles": document["bundles"]}))
+    assert iter_deployed_configs(hardware=_hardware(), path=path) == ()
+    publish_deployed_config(hardware=_hardware(), shape=shapes[2], config=graph, path=path)
+    assert json.loads(path.read_text())["schema_version"] == 4
+    assert iter_deployed_configs(hardware=_hardware(), path=path) == ((shapes[2], graph),)
 
 
 def test_fingerprint_round_trip() -> None:

@@ -184,6 +184,58 @@ def test_runtimes_agree_bitwise_and_observation_matches_plan() -> None:
         assert torch.equal(second, eager), schedule.runtime
 
 
+def test_graph_runtime_binds_the_callers_buffers() -> None:
+    """The graph runtime reads the caller's input in place and writes a fresh
+    output per call: in-place changes of a bound input are seen by the next
+    call, earlier outputs are never overwritten, and buffers beyond
+    max_bindings evict the least recently used capture."""
+
+    golden = load_golden("c1_official")
+    cfg = _golden_config(golden)
+    seed = int(golden["input_seed"])
+    x, x2 = official_input(cfg, seed), official_input(cfg, seed + 1)
+    eager, eager2 = _run(_model(cfg), x), _run(_model(cfg), x2)
+    model = _model(cfg, ConfigSpec(program=default_program(), schedule=default_schedule(RuntimeBackend.CUDA_GRAPH)))
+    bound = x.to(DEV)
+    with torch.inference_mode():
+        a = model(bound)
+        b = model(bound)
+        torch.cuda.synchronize()
+        replay = model._cuda_graph_replay
+        assert replay.bindings == 1
+        assert a.data_ptr() != b.data_ptr()
+        assert torch.equal(a, eager) and torch.equal(b, eager)
+        bound.copy_(x2.to(DEV))
+        c = model(bound)
+        torch.cuda.synchronize()
+        assert replay.bindings == 1
+        assert torch.equal(c, eager2) and torch.equal(a, eager)
+        buffers = [x.to(DEV) for _ in range(replay.max_bindings + 1)]
+        for buffer in buffers:
+            assert torch.equal(model(buffer), eager)
+        assert replay.bindings == replay.max_bindings
+        assert torch.equal(model(buffers[0]), eager)
+
+
+def test_batch_tiled_graph_with_a_short_last_tile() -> None:
+    """Tiles of 2 rows over a batch of 5: the last tile (one row) is its own
+    capture; the tiles write their rows of one output, equal to the eager
+    forward bit for bit."""
+
+    cfg = OfficialConfig(5, 96, 256, 4, 512, 2)
+    x = official_input(cfg, 3)
+    eager = _run(_model(cfg), x)
+    schedule = default_schedule(RuntimeBackend.BATCH_TILED_CUDA_GRAPH, batch_tile_size=2)
+    model = _model(cfg, ConfigSpec(program=default_program(), schedule=schedule))
+    bound = x.to(DEV)
+    with torch.inference_mode():
+        first = model(bound)
+        second = model(bound)
+    torch.cuda.synchronize()
+    assert torch.equal(first, eager) and torch.equal(second, eager)
+    assert first.data_ptr() != second.data_ptr()
+
+
 def test_cuda_graph_rejects_a_second_signature() -> None:
     cfg = OfficialConfig(2, 64, 128, 2, 256, 1)
     model = _model(cfg, ConfigSpec(program=default_program(), schedule=default_schedule(RuntimeBackend.CUDA_GRAPH)))
