@@ -386,7 +386,7 @@ def _workload_input(name: str, args: argparse.Namespace, spec: dict, seed: int, 
 
 
 GEMM_VARIANT_NAMES = {0: "1SM", 1: "PAIR", 2: "WARP"}
-ATTENTION_VARIANT_NAMES = {0: "PAIRED", 1: "SINGLE", 2: "QUAD", 3: "PERSISTENT", 4: "DUO"}
+ATTENTION_VARIANT_NAMES = {0: "PAIRED", 1: "SINGLE", 2: "QUAD", 3: "PERSISTENT", 4: "DUO", 5: "PINGPONG"}
 
 
 def _program(model, runner) -> dict:  # noqa: ANN001
@@ -855,6 +855,7 @@ def run_kernel(args: argparse.Namespace) -> None:
             "attention_single": _native.ATTN_SINGLE,
             "attention_persistent": _native.ATTN_PERSISTENT,
             "attention_duo": _native.ATTN_DUO,
+            "attention_pingpong": _native.ATTN_PINGPONG,
         }[args.kernel]
         launch = lambda: _native.attention(qkv, out, b, s, h, 64, 0.125, True, variant)  # noqa: E731
         work, unit, bound = 2.0 * b * s * s * d, "TFLOP/s", "tensor"
@@ -1106,6 +1107,7 @@ def main() -> None:
             "attention_single",
             "attention_persistent",
             "attention_duo",
+            "attention_pingpong",
             "qkv",
             "out_proj",
             "ffn_in",

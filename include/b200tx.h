@@ -50,6 +50,8 @@ extern "C" {
 #define B200TX_ATTN_QUAD 2   /* four 128-row query tiles per CTA, 64-row KV tiles, P in TMEM */
 #define B200TX_ATTN_PERSISTENT 3 /* persistent grid, two query tiles per item, double-buffered S */
 #define B200TX_ATTN_DUO 4    /* two 128-row query tiles per CTA, 64-row KV tiles, two CTAs per SM */
+#define B200TX_ATTN_PINGPONG 5 /* persistent; two 128-row query tiles x 128-row KV tiles, S, P and O
+                                  in separate TMEM columns so S(j+1) overlaps the softmax of S(j) */
 
 /* Status codes. */
 #define B200TX_OK 0
@@ -171,7 +173,7 @@ int b200tx_attention(const void* qkv, void* out, int64_t batch, int64_t seq, int
 /*
  * b200tx_attention with an explicit kernel variant (B200TX_ATTN_QUAD, the
  * default of b200tx_attention, B200TX_ATTN_DUO, B200TX_ATTN_PERSISTENT,
- * B200TX_ATTN_PAIRED or B200TX_ATTN_SINGLE).  All compute the same function; the execution plan's
+ * B200TX_ATTN_PINGPONG, B200TX_ATTN_PAIRED or B200TX_ATTN_SINGLE).  All compute the same function; the execution plan's
  * attention launch record picks one.
  * Replaces the same reference operators as b200tx_attention; the variant is the
  * sm100 counterpart of the reference's attention launch parameters
@@ -186,8 +188,8 @@ int b200tx_attention_ex(const void* qkv, void* out, int64_t batch, int64_t seq, 
  * (non-null), 0 = padding key, whose scores are -inf for every query (the
  * reference's invalid_keys masked_fill, official/torch_transformer_benchmark.py:
  * 105-108).  A query that sees no valid key gets a zero context row.  Built
- * into B200TX_ATTN_QUAD, B200TX_ATTN_DUO and B200TX_ATTN_PERSISTENT; other variants return
- * B200TX_ERR_UNSUPPORTED.
+ * into B200TX_ATTN_QUAD, B200TX_ATTN_DUO, B200TX_ATTN_PERSISTENT and
+ * B200TX_ATTN_PINGPONG; other variants return B200TX_ERR_UNSUPPORTED.
  */
 int b200tx_attention_masked(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
                             int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,

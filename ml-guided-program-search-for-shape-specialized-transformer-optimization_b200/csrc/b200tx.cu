@@ -20,6 +20,7 @@
 #include "attention_kernels.cuh"
 #include "attention_mma_kernels.cuh"
 #include "attention_persistent.cuh"
+#include "attention_pingpong.cuh"
 #include "attention_simt_kernels.cuh"
 #include "boundary_kernels.cuh"
 #include "gemm_kernels.cuh"
@@ -49,7 +50,13 @@ int cuda_fail(cudaError_t err, const char* what) {
 }
 
 // Attention variant codes run 0 .. kAttnVariants-1 (B200TX_ATTN_*).
-constexpr int kAttnVariants = 5;
+constexpr int kAttnVariants = 6;
+
+// Score pairs (of every 16) whose exponentials the PINGPONG attention
+// computes on the FMA pipe instead of the MUFU.
+#ifndef B200TX_PP_POLY_PAIRS
+#define B200TX_PP_POLY_PAIRS 0
+#endif
 
 struct DeviceState {
   bool probed = false;
@@ -515,10 +522,10 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   if (!aligned16(qkv) || !aligned16(out))
     return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: operands must be 16-byte aligned");
   if (key_valid != nullptr && variant != B200TX_ATTN_QUAD && variant != B200TX_ATTN_PERSISTENT &&
-      variant != B200TX_ATTN_DUO)
+      variant != B200TX_ATTN_DUO && variant != B200TX_ATTN_PINGPONG)
     return fail(B200TX_ERR_UNSUPPORTED,
-                "attention: padding masks are built into the QUAD, DUO and PERSISTENT variants only "
-                "(variant %d)",
+                "attention: padding masks are built into the QUAD, DUO, PERSISTENT and PINGPONG variants "
+                "only (variant %d)",
                 variant);
   if (!(scale > 0.0f)) return fail(B200TX_ERR_INVALID_ARGUMENT, "attention: scale must be > 0");
   const int64_t q_tiles = (seq + b200tx::kAttnBM - 1) / b200tx::kAttnBM;
@@ -526,6 +533,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
                         : variant == B200TX_ATTN_QUAD       ? (q_tiles + 3) / 4
                         : variant == B200TX_ATTN_PERSISTENT ? (q_tiles + 1) / 2
                         : variant == B200TX_ATTN_DUO        ? (q_tiles + 1) / 2
+                        : variant == B200TX_ATTN_PINGPONG   ? (q_tiles + 1) / 2
                                                             : q_tiles;
   const int64_t blocks = units * heads * batch;
   if (blocks > 0x7fffffffLL || seq > 0x7fffffffLL || batch > 0x7fffffffLL)
@@ -554,6 +562,29 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
   args.num_q_tiles = static_cast<int>(q_tiles);
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
+  if (variant == B200TX_ATTN_PINGPONG) {
+    // Persistent: at most one CTA per SM walks the items (pairs of query
+    // tiles); Q, K and V tiles are all 128 x 64 boxes of the one map.
+    using PpFn = void (*)(CUtensorMap, b200tx::AttnArgs);
+    const PpFn kernel = key_valid != nullptr
+                            ? b200tx::attention_fwd_dh64_pingpong_kernel<true, B200TX_PP_POLY_PAIRS>
+                            : b200tx::attention_fwd_dh64_pingpong_kernel<false, B200TX_PP_POLY_PAIRS>;
+    const int attr_slot = key_valid != nullptr ? kAttnVariants + variant : variant;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (!dev->attn_attr[attr_slot]) {
+        cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(b200tx::kPpSmemBytes));
+        if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
+        dev->attn_attr[attr_slot] = true;
+      }
+    }
+    const int64_t grid = blocks < dev->sm_count ? blocks : dev->sm_count;
+    cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(b200tx::kPpThreads),
+                             b200tx::kPpSmemBytes, stream, map_qkv, args);
+    if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+    return B200TX_OK;
+  }
   if (variant == B200TX_ATTN_PERSISTENT) {
     CUtensorMap map_kv;
     const uint64_t dims[3] = {static_cast<uint64_t>(3 * d_model), static_cast<uint64_t>(seq),

@@ -29,6 +29,7 @@ ATTN_SINGLE = 1
 ATTN_QUAD = 2
 ATTN_PERSISTENT = 3
 ATTN_DUO = 4
+ATTN_PINGPONG = 5
 MASK_DROP_UPDATE = 1
 MASK_ZERO_RESIDUAL = 2
 MASK_ZERO_NORMED = 4
@@ -700,6 +701,7 @@ __all__ = [
     "residual_layer_norm_peer",
     "ABI_VERSION",
     "ATTN_DUO",
+    "ATTN_PINGPONG",
     "ATTN_PAIRED",
     "ATTN_PERSISTENT",
     "ATTN_QUAD",

@@ -177,12 +177,16 @@ SM100_GEMM_VARIANTS = frozenset(SM100_GEMM_VARIANT_CODES)
 #                  scores, 8-slot KV rings (B200TX_ATTN_PERSISTENT)
 #   (256, 64, 4):  two query tiles per CTA, 64-row KV tiles, 4-slot KV rings, two CTAs
 #                  per SM (B200TX_ATTN_DUO)
+#   (256, 128, 4): persistent, two query tiles per work item against 128-row KV
+#                  tiles with S, P and O in separate TMEM columns, 4-slot KV rings
+#                  (B200TX_ATTN_PINGPONG)
 SM100_ATTENTION_VARIANTS = {
     (256, 128, 3): 0,
     (128, 128, 3): 1,
     (512, 64, 6): 2,
     (256, 64, 8): 3,
     (256, 64, 4): 4,
+    (256, 128, 4): 5,
 }
 SM100_NORM_ROWS_PER_CTA = frozenset({8})
 

@@ -80,8 +80,8 @@ def sm100_flash_attention(
             "key_valid must be a contiguous uint8 [B, S] tensor on the qkv device",
         )
         require(
-            variant in (_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO),
-            "padding masks are built into the QUAD, PERSISTENT and DUO variants only",
+            variant in (_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO, _native.ATTN_PINGPONG),
+            "padding masks are built into the QUAD, PERSISTENT, DUO and PINGPONG variants only",
         )
     launch(
         _native.attention,

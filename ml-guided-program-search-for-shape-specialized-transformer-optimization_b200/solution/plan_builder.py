@@ -39,9 +39,9 @@ SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
 MMA_HEAD_DIMS = frozenset({8, 16, 32, 64, 128})
 BOUNDARY_WIDTHS = frozenset({32, 64, 128})
 # The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
-# B200TX_ATTN_PERSISTENT and B200TX_ATTN_DUO).
+# B200TX_ATTN_PERSISTENT, B200TX_ATTN_DUO and B200TX_ATTN_PINGPONG).
 SM100_QUAD_ATTENTION_VARIANT = 2
-SM100_MASKED_ATTENTION_VARIANTS = frozenset({2, 3, 4})
+SM100_MASKED_ATTENTION_VARIANTS = frozenset({2, 3, 4, 5})
 SUPPORTED_IO_DTYPES = frozenset({torch.float32, torch.bfloat16})
 _INT32_MAX = 2**31 - 1
 
@@ -288,7 +288,8 @@ class PlanBuilder:
                 "mask_not_supported",
                 "schedule.attention_launch",
                 "padding masks are built into the quad (block_m 512, block_n 64, kv_stages 6), "
-                "persistent (256, 64, 8) and duo (256, 64, 4) attention variants only",
+                "persistent (256, 64, 8), duo (256, 64, 4) and pingpong (256, 128, 4) attention "
+                "variants only",
             )
         if config.program.attention is AttentionBackend.SM100_FLASH:
             if head_dim is not None and head_dim not in SUPPORTED_HEAD_DIMS:

@@ -184,8 +184,15 @@ def test_linear_three_dimensional_input() -> None:
     assert parity_errors(out.cpu().numpy(), ref)[1] < 1e-5
 
 
-VARIANTS = [_native.ATTN_PAIRED, _native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO]
-MASKED_VARIANTS = [_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO]
+VARIANTS = [
+    _native.ATTN_PAIRED,
+    _native.ATTN_SINGLE,
+    _native.ATTN_QUAD,
+    _native.ATTN_PERSISTENT,
+    _native.ATTN_DUO,
+    _native.ATTN_PINGPONG,
+]
+MASKED_VARIANTS = [_native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO, _native.ATTN_PINGPONG]
 
 
 def _attention_case(batch: int, seq: int, heads: int, causal: bool, seed: int, variant: int) -> None:
@@ -253,6 +260,18 @@ def test_attention_persistent_many_items_per_cta(batch: int, seq: int, heads: in
 
 
 @pytest.mark.parametrize(
+    ("batch", "seq", "heads", "causal"),
+    [(8, 1024, 16, True), (4, 640, 40, False), (8, 2048, 8, True), (3, 1000, 20, True), (1, 4096, 148, True)],
+)
+def test_attention_pingpong_many_items_per_cta(batch: int, seq: int, heads: int, causal: bool) -> None:
+    """More work items than CTAs: each persistent PINGPONG CTA walks several
+    items, its Q buffers, K/V ring positions and barrier phases carried across
+    them, items of different lengths interleaved by the snake order."""
+
+    _attention_case(batch, seq, heads, causal, seed=seq + 7 * heads, variant=_native.ATTN_PINGPONG)
+
+
+@pytest.mark.parametrize(
     ("batch", "seq", "heads", "causal"), [(8, 2048, 16, True), (4, 640, 40, False), (16, 512, 12, True)]
 )
 def test_attention_duo_two_ctas_per_sm(batch: int, seq: int, heads: int, causal: bool) -> None:
@@ -268,7 +287,8 @@ def test_attention_variants_agree(causal: bool) -> None:
     qkv = torch.randn(3, 1000, 3 * 2 * 64, generator=g).to(torch.bfloat16).to(DEV)
     with torch.inference_mode():
         a, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=_native.ATTN_PAIRED)
-        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO):
+        for other in (_native.ATTN_SINGLE, _native.ATTN_QUAD, _native.ATTN_PERSISTENT, _native.ATTN_DUO,
+                      _native.ATTN_PINGPONG):
             b, _ = sm100_flash_attention(qkv, 2, causal=causal, variant=other)
             max_abs, rel = parity_errors(_bf16_np(a), _bf16_np(b))
             # Two bf16 results of different summation orders: a few bf16 ulps apart.

@@ -40,7 +40,14 @@ from solution.transformer import UserOptimizedTransformer, copy_model_weights
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0)
-VARIANTS = [_native.ATTN_QUAD, _native.ATTN_DUO, _native.ATTN_PERSISTENT, _native.ATTN_PAIRED, _native.ATTN_SINGLE]
+VARIANTS = [
+    _native.ATTN_PINGPONG,
+    _native.ATTN_QUAD,
+    _native.ATTN_DUO,
+    _native.ATTN_PERSISTENT,
+    _native.ATTN_PAIRED,
+    _native.ATTN_SINGLE,
+]
 
 
 @pytest.fixture(autouse=True)

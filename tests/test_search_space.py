@@ -19,7 +19,7 @@ import pytest
 import torch
 
 from autotune.search_space import ProgramSearchSpace, SearchContext, StructureSpec
-from solution.config import ConfigSpec, RuntimeBackend, portable_config
+from solution.config import SM100_ATTENTION_VARIANTS, ConfigSpec, RuntimeBackend, portable_config
 from solution.plan import ExecutionContext
 from solution.plan_builder import HardwareCapabilities, PlanBuilder
 
@@ -66,8 +66,8 @@ def test_resident_space_has_every_structure_and_the_portable_branch() -> None:
     portable = space.branch_for(portable_config())
     assert portable is not None and portable.structure.portable
     assert portable.branch_id in space.mandatory_branch_ids
-    # 5 attention variants x 3^4 GEMM variants
-    assert portable.cardinality == 5 * 81
+    # every attention variant x 3^4 GEMM variants
+    assert portable.cardinality == len(SM100_ATTENTION_VARIANTS) * 81
     assert space.cardinality == sum(b.cardinality for b in space.branches)
 
 
@@ -113,7 +113,7 @@ def test_masked_context_keeps_only_the_mask_reading_attention() -> None:
     tiles = {branch.parameters_for(c).get("attention_tile") for branch in space.branches for c in branch.configs()
              if space.accepted(c)}
     # the quad, persistent and duo kernels, or the CUDA-core kernel (no tile)
-    assert tiles == {"512x64x6", "256x64x8", "256x64x4", None}
+    assert tiles == {"512x64x6", "256x64x8", "256x64x4", "256x128x4", None}
 
 
 def test_other_head_dims_search_the_warp_mma_and_cuda_core_attention() -> None:
