@@ -52,16 +52,25 @@
 
 namespace b200tx {
 
-constexpr int kPpThreads = 576;
 constexpr int kPpSoftmaxWarp0 = 2;
-constexpr int kPpRing = 4;
-constexpr uint32_t kPpTmemCols = 512;
 constexpr uint32_t kPpTileCols = 256;  // TMEM columns per query tile
 constexpr uint32_t kPpColP = 128;      // P_w offset inside the tile's columns
 constexpr uint32_t kPpColO = 192;      // O_w offset inside the tile's columns
-constexpr uint32_t kPpQBufBytes = 2 * kAttnTileBytes;  // both Q tiles of an item
-constexpr size_t kPpSmemBytes = 1024 + 2 * kPpQBufBytes + 2 * kPpRing * kAttnTileBytes;  // 193 KB
 constexpr float kPpMaxSlack = 8.0f;
+
+// Launch shape of the kernel with kTiles query tiles per CTA: two tiles and
+// one CTA per SM (512 TMEM columns), or one tile and two CTAs per SM (256
+// each, smaller K/V rings so that two CTAs' shared memory fits).
+template <int kTiles>
+struct PpShape {
+  static_assert(kTiles == 1 || kTiles == 2, "one or two query tiles per CTA");
+  static constexpr int kThreads = 64 + 256 * kTiles;
+  static constexpr int kCtasPerSm = 2 / kTiles;
+  static constexpr int kRing = kTiles == 2 ? 4 : 2;
+  static constexpr uint32_t kTmemCols = kPpTileCols * kTiles;
+  static constexpr uint32_t kQBufBytes = kTiles * kAttnTileBytes;
+  static constexpr size_t kSmemBytes = 1024 + 2 * kQBufBytes + 2 * kRing * kAttnTileBytes;  // 193 / 97 KB
+};
 
 struct PpItem {
   int batch;
@@ -71,32 +80,39 @@ struct PpItem {
   int n_max;
 };
 
-// The r-th item of this CTA in snake order, or false when it has no more.
+// The r-th item (kTiles consecutive query tiles of one batch row and head) of
+// this CTA in snake order, or false when it has no more.
+template <int kTiles>
 __device__ __forceinline__ bool pp_item(const AttnArgs& args, int r, PpItem& it) {
   const int grid = static_cast<int>(gridDim.x);
   const int c = static_cast<int>(blockIdx.x);
   const int64_t t64 = static_cast<int64_t>(r) * grid + ((r & 1) ? (grid - 1 - c) : c);
   const int hb_count = args.heads * args.batch;
-  const int num_pairs = (args.num_q_tiles + 1) / 2;
-  if (t64 >= static_cast<int64_t>(num_pairs) * hb_count) return false;
+  const int num_groups = (args.num_q_tiles + kTiles - 1) / kTiles;
+  if (t64 >= static_cast<int64_t>(num_groups) * hb_count) return false;
   const int t = static_cast<int>(t64);
-  const int pair = num_pairs - 1 - t / hb_count;  // longest first
+  const int group = num_groups - 1 - t / hb_count;  // longest first
   const int hb = t % hb_count;
   it.head = hb % args.heads;
   it.batch = hb / args.heads;
-  it.q_tile0 = 2 * pair;
+  it.q_tile0 = kTiles * group;
   const int kv_total = (args.seq + kAttnBN - 1) / kAttnBN;
   const int q1 = it.q_tile0 + 1;
   it.n[0] = args.causal ? (it.q_tile0 + 1 < kv_total ? it.q_tile0 + 1 : kv_total) : kv_total;
-  it.n[1] = q1 >= args.num_q_tiles ? 0 : (args.causal ? (q1 + 1 < kv_total ? q1 + 1 : kv_total) : kv_total);
+  it.n[1] = (kTiles == 1 || q1 >= args.num_q_tiles)
+                ? 0
+                : (args.causal ? (q1 + 1 < kv_total ? q1 + 1 : kv_total) : kv_total);
   it.n_max = it.n[0] > it.n[1] ? it.n[0] : it.n[1];
   return true;
 }
 
-template <bool kMasked, int kPolyPairs>
-__global__ void __launch_bounds__(kPpThreads, 1)
+template <bool kMasked, int kPolyPairs, int kTiles>
+__global__ void __launch_bounds__(PpShape<kTiles>::kThreads, PpShape<kTiles>::kCtasPerSm)
     attention_fwd_dh64_pingpong_kernel(const __grid_constant__ CUtensorMap tmap_qkv, AttnArgs args) {
   static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per 16");
+  constexpr int kPpRing = PpShape<kTiles>::kRing;
+  constexpr uint32_t kPpTmemCols = PpShape<kTiles>::kTmemCols;
+  constexpr uint32_t kPpQBufBytes = PpShape<kTiles>::kQBufBytes;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full_bar[2];
   __shared__ uint64_t q_empty_bar[2];
@@ -113,9 +129,9 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   __shared__ uint64_t drain_bar;
   // Exchange between the two warps that share rows: each thread writes its
   // value (a partial row max, or at the end of an item its partial row sum)
-  // into slot [exchange parity][tile][half][row] and arrives on the pair's
-  // barrier (64 arrivals); the partner's value is read after the phase
-  // completes.  Two slots suffice: a warp can only write a slot again after
+  // into slot [exchange parity][tile][half][row]; after __syncwarp one lane
+  // per warp arrives on the pair's barrier (2 arrivals), and the partner's
+  // value is read after the phase completes.  Two slots suffice: a warp can only write a slot again after
   // the exchange in between, which its partner joins after reading it.
   __shared__ uint64_t pair_bar[2][4];  // [tile][lane quarter]
   __shared__ float xchg[2][2][2][kAttnBM];
@@ -150,7 +166,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       mbar_init(&pv_done_bar[w], 1);
       mbar_init(&o_final_bar[w], 1);
       mbar_init(&o_empty_bar[w], 8);
-      for (int k = 0; k < 4; ++k) mbar_init(&pair_bar[w][k], 64);
+      for (int k = 0; k < 4; ++k) mbar_init(&pair_bar[w][k], 2);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -174,7 +190,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       int q_loaded = 0;  // items whose Q load was issued
       bool ok = true;
       PpItem it;
-      for (int r = 0; ok && pp_item(args, r, it); ++r) {
+      for (int r = 0; ok && pp_item<kTiles>(args, r, it); ++r) {
         const int buf = r & 1;
         if (r >= 2 && !mbar_wait(&q_empty_bar[buf], ((r >> 1) - 1) & 1, kErrAttnProducerWait, &abort_flag)) {
           ok = false;
@@ -231,7 +247,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       bool issued_any = false;
       bool ok = true;
       PpItem it;
-      for (int r = 0; ok && pp_item(args, r, it); ++r) {
+      for (int r = 0; ok && pp_item<kTiles>(args, r, it); ++r) {
         const int buf = r & 1;
         if (!mbar_wait(&q_full_bar[buf], (r >> 1) & 1, kErrAttnMmaWait, &abort_flag)) {
           ok = false;
@@ -338,7 +354,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     int exchanges = 0;  // completed phases of this warp pair's barrier
     bool ok = true;
     PpItem it;
-    for (int r = 0; ok && pp_item(args, r, it); ++r) {
+    for (int r = 0; ok && pp_item<kTiles>(args, r, it); ++r) {
       const int n = it.n[w];
       if (n == 0) continue;
       const int q_tile = it.q_tile0 + w;
@@ -403,7 +419,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         const float mine2 = max3(mine, __uint_as_float(s[62]), __uint_as_float(s[63]));
         const int slot = exchanges & 1;
         xchg[slot][w][h][row] = mine2;
-        mbar_arrive(pair);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pair);
         ok = mbar_wait(pair, exchanges & 1, kErrAttnSoftmaxWait, &abort_flag);
         if (__any_sync(0xffffffffu, !ok)) {
           ok = false;
@@ -486,7 +503,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       ++items;
       const int slot = exchanges & 1;
       xchg[slot][w][h][row] = l_run;
-      mbar_arrive(pair);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pair);
       ok = mbar_wait(pair, exchanges & 1, kErrAttnSoftmaxWait, &abort_flag);
       if (__any_sync(0xffffffffu, !ok)) {
         ok = false;

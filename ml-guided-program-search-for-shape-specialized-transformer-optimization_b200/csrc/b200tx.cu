@@ -52,11 +52,11 @@ int cuda_fail(cudaError_t err, const char* what) {
 // Attention variant codes run 0 .. kAttnVariants-1 (B200TX_ATTN_*).
 constexpr int kAttnVariants = 6;
 
-// Score pairs (of every 16) whose exponentials the PINGPONG attention
-// computes on the FMA pipe instead of the MUFU.
-#ifndef B200TX_PP_POLY_PAIRS
-#define B200TX_PP_POLY_PAIRS 0
-#endif
+// PINGPONG attention build: two query tiles per CTA (one CTA per SM; one
+// tile with two CTAs per SM measured slower at every shape), and 2 of every
+// 16 score pairs exponentiated on the FMA pipe (the measured best of 0..8).
+constexpr int kPpTiles = 2;
+constexpr int kPpPolyPairs = 2;
 
 struct DeviceState {
   bool probed = false;
@@ -566,22 +566,26 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     // Persistent: at most one CTA per SM walks the items (pairs of query
     // tiles); Q, K and V tiles are all 128 x 64 boxes of the one map.
     using PpFn = void (*)(CUtensorMap, b200tx::AttnArgs);
-    const PpFn kernel = key_valid != nullptr
-                            ? b200tx::attention_fwd_dh64_pingpong_kernel<true, B200TX_PP_POLY_PAIRS>
-                            : b200tx::attention_fwd_dh64_pingpong_kernel<false, B200TX_PP_POLY_PAIRS>;
+    using Shape = b200tx::PpShape<kPpTiles>;
+    const PpFn kernel =
+        key_valid != nullptr
+            ? b200tx::attention_fwd_dh64_pingpong_kernel<true, kPpPolyPairs, kPpTiles>
+            : b200tx::attention_fwd_dh64_pingpong_kernel<false, kPpPolyPairs, kPpTiles>;
     const int attr_slot = key_valid != nullptr ? kAttnVariants + variant : variant;
     {
       std::lock_guard<std::mutex> lock(g_mutex);
       if (!dev->attn_attr[attr_slot]) {
         cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(b200tx::kPpSmemBytes));
+                                               static_cast<int>(Shape::kSmemBytes));
         if (err != cudaSuccess) return cuda_fail(err, "attention: cudaFuncSetAttribute");
         dev->attn_attr[attr_slot] = true;
       }
     }
-    const int64_t grid = blocks < dev->sm_count ? blocks : dev->sm_count;
-    cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(b200tx::kPpThreads),
-                             b200tx::kPpSmemBytes, stream, map_qkv, args);
+    const int64_t items = ((q_tiles + kPpTiles - 1) / kPpTiles) * heads * batch;
+    const int64_t slots = static_cast<int64_t>(dev->sm_count) * Shape::kCtasPerSm;
+    const int64_t grid = items < slots ? items : slots;
+    cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(Shape::kThreads),
+                             Shape::kSmemBytes, stream, map_qkv, args);
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
   }
