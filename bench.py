@@ -869,6 +869,13 @@ def run_kernel(args: argparse.Namespace) -> None:
         epi = _native.EPI_BIAS_GELU if gelu else _native.EPI_BIAS
         launch = lambda: _native.linear(a, w, bias, out, epi, variant)  # noqa: E731
         work, unit, bound = 2.0 * m * n * k, "TFLOP/s", "tensor"
+    elif args.kernel == "initial_norm":
+        x = randn(m, d, dtype=torch.float32)
+        normed = torch.empty(m, d, device=device, dtype=torch.bfloat16)
+        gamma = torch.ones(d, device=device)
+        beta = torch.zeros(d, device=device)
+        launch = lambda: _native.residual_layer_norm(x, None, None, normed, gamma, beta, 1e-5)  # noqa: E731
+        work, unit, bound = 6.0 * m * d, "GB/s", "hbm"
     elif args.kernel == "residual_norm":
         resid = randn(m, d, dtype=torch.float32)
         upd = randn(m, d)
@@ -1117,6 +1124,7 @@ def main() -> None:
             "ffn_in_pair",
             "ffn_out_pair",
             "residual_norm",
+            "initial_norm",
         ),
         default=None,
     )
