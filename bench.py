@@ -568,12 +568,37 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
             barrier()
             e2e_ms = e2e_start.elapsed_time(e2e_end) / steps
             out_host = outs_host[0]
+            # The host link alone, all ranks at once: the step's input copied
+            # H2D, then its output D2H, then both directions together (on two
+            # streams), each timed by CUDA events -- the rates that bound e2e.
+            link = torch.empty_like(x_dev)
+            down = torch.cuda.Stream(device)
+            link_ms = {}
+            for name in ("h2d", "d2h", "both"):
+                barrier()
+                t0 = torch.cuda.Event(enable_timing=True)
+                t1 = torch.cuda.Event(enable_timing=True)
+                t0.record()
+                reps = 5
+                for _ in range(reps):
+                    if name in ("h2d", "both"):
+                        link.copy_(x_host, non_blocking=True)
+                    if name in ("d2h", "both"):
+                        down.wait_stream(torch.cuda.current_stream(device))
+                        with torch.cuda.stream(down):
+                            out_host.copy_(x_dev, non_blocking=True)
+                        torch.cuda.current_stream(device).wait_stream(down)
+                t1.record()
+                torch.cuda.synchronize(device)
+                link_ms[name] = t0.elapsed_time(t1) / reps
+            del link
 
     total_ms = sum(step_ms)
-    stats = torch.tensor([total_ms, e2e_ms, peak_gb], dtype=torch.float64, device=device)
+    link_vals = [link_ms.get(k, 0.0) for k in ("h2d", "d2h", "both")] if full else [0.0, 0.0, 0.0]
+    stats = torch.tensor([total_ms, e2e_ms, peak_gb, *link_vals], dtype=torch.float64, device=device)
     if dist is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    total_ms_max, e2e_ms_max, peak_gb_max = stats.tolist()
+    total_ms_max, e2e_ms_max, peak_gb_max, h2d_ms, d2h_ms, both_ms = stats.tolist()
     ms_per_step = total_ms_max / steps
 
     b_loc = x_dev.shape[0]
@@ -670,6 +695,19 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         "_e2e_ms": e2e_ms_max,
         "_total_tokens": total_tokens,
         "_first_row": first_row,
+        "_host_link": (
+            {
+                "bytes_per_rank_each_way": int(x_host.numel() * x_host.element_size()),
+                "ranks_copying_at_once": world,
+                "h2d_gbs_per_rank": x_host.numel() * x_host.element_size() / (h2d_ms / 1000.0) / 1e9,
+                "d2h_gbs_per_rank": x_host.numel() * x_host.element_size() / (d2h_ms / 1000.0) / 1e9,
+                "both_directions_ms": both_ms,
+                "h2d_then_d2h_ms": h2d_ms + d2h_ms,
+                "timing": "CUDA events, slowest rank, 5 copies each, pinned host memory",
+            }
+            if full and h2d_ms > 0
+            else None
+        ),
         "_h2d": int(x_host.numel() * x_host.element_size()) if x_host is not None else 0,
         "_d2h": int(out_host.numel() * out_host.element_size()) if out_host is not None else 0,
     }
@@ -789,6 +827,7 @@ def run_gpu(args: argparse.Namespace) -> None:
                 "h2d_bytes_per_step": main["_h2d"],
                 "d2h_bytes_per_step": main["_d2h"],
                 "ms_per_step": main["_e2e_ms"],
+                "host_link": main["_host_link"],
             },
             "gpu_launches": main["_launches"] or launches_per_step * args.steps,
             "clocks": main["clocks"],
