@@ -24,6 +24,7 @@
 #include "attention_simt_kernels.cuh"
 #include "boundary_kernels.cuh"
 #include "gemm_kernels.cuh"
+#include "gemm_rownorm_kernels.cuh"
 #include "gemm_warp_kernels.cuh"
 #include "norm_kernels.cuh"
 #include "sm100_common.cuh"
@@ -65,6 +66,7 @@ struct DeviceState {
   int cc_minor = 0;
   bool gemm_attr[8] = {false, false, false, false, false, false, false, false};
   bool attn_attr[2 * kAttnVariants] = {};  // unmasked builds by variant, then the masked builds
+  bool rownorm_attr[4] = {};               // GEMM + residual LayerNorm builds by (in, out) dtype
 };
 
 std::mutex g_mutex;
@@ -917,6 +919,76 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
 
 namespace {
 
+// The Linear boundary at d_model 512 / 768 / 1024: a tcgen05 GEMM whose CTA
+// pair holds whole rows in TMEM and applies the residual LayerNorm in its
+// epilogue (gemm_rownorm_kernels.cuh).
+int launch_gemm_rownorm(const b200tx::BoundaryArgs& a, DeviceState* dev, int in_dtype, int out_dtype,
+                        int64_t rows, int64_t cols, int64_t inner, cudaStream_t stream) {
+  const size_t in_align = in_dtype == B200TX_F32 ? 16 : 8;
+  if ((reinterpret_cast<uintptr_t>(a.residual_in) % in_align) != 0 ||
+      (a.residual_out != nullptr && !aligned16(a.residual_out)) ||
+      (reinterpret_cast<uintptr_t>(a.normed) % (out_dtype == B200TX_F32 ? 16 : 8)) != 0 ||
+      (reinterpret_cast<uintptr_t>(a.bias) & 3u) != 0)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear_residual_layer_norm: misaligned operand at d_model %lld",
+                (long long)cols);
+  CUtensorMap map_x, map_w;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(inner) * 2};
+    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), static_cast<uint32_t>(b200tx::kRnBM)};
+    int rc = encode_bf16_map(&map_x, a.x, 2, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(cols)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(inner) * 2};
+    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), static_cast<uint32_t>(b200tx::kRnPieceRows)};
+    int rc = encode_bf16_map(&map_w, a.w, 2, dims, strides, box);
+    if (rc != B200TX_OK) return rc;
+  }
+  b200tx::RowNormArgs r;
+  r.bias = a.bias;
+  r.residual_in = a.residual_in;
+  r.residual_out = a.residual_out;
+  r.normed = a.normed;
+  r.gamma = a.gamma;
+  r.beta = a.beta;
+  r.row_valid = a.row_valid;
+  r.mask_mode = a.mask_mode;
+  r.rows = static_cast<int>(rows);
+  r.cols = static_cast<int>(cols);
+  r.inner = static_cast<int>(inner);
+  r.num_tiles = static_cast<int>((rows + b200tx::kRnBM - 1) / b200tx::kRnBM);
+  r.round_update_bf16 = a.update_bf16;
+  r.eps = a.eps;
+  // Persistent: one CTA pair per two SMs, walking the 128-row tiles.
+  const int64_t pairs_avail = dev->sm_count / 2;
+  const int64_t pairs = r.num_tiles < pairs_avail ? r.num_tiles : pairs_avail;
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::RowNormArgs);
+  KernelFn kernel;
+  const int instance = (in_dtype == B200TX_F32 ? 2 : 0) + (out_dtype == B200TX_F32 ? 1 : 0);
+  switch (instance) {
+    case 0: kernel = b200tx::gemm_residual_layernorm_kernel<__nv_bfloat16, __nv_bfloat16>; break;
+    case 1: kernel = b200tx::gemm_residual_layernorm_kernel<__nv_bfloat16, float>; break;
+    case 2: kernel = b200tx::gemm_residual_layernorm_kernel<float, __nv_bfloat16>; break;
+    default: kernel = b200tx::gemm_residual_layernorm_kernel<float, float>; break;
+  }
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->rownorm_attr[instance]) {
+      cudaError_t err = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(b200tx::kRnSmemBytes));
+      if (err != cudaSuccess) return cuda_fail(err, "linear_residual_layer_norm: cudaFuncSetAttribute");
+      dev->rownorm_attr[instance] = true;
+    }
+  }
+  cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(b200tx::kRnThreads),
+                           b200tx::kRnSmemBytes, stream, map_x, map_w, r);
+  if (err != cudaSuccess) return cuda_fail(err, "linear_residual_layer_norm (row-complete GEMM) launch");
+  return B200TX_OK;
+}
+
 template <bool MLP, int D, typename InT, typename OutT>
 cudaError_t launch_boundary_typed(const b200tx::BoundaryArgs& a, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>((a.M + b200tx::kBoundaryRows - 1) / b200tx::kBoundaryRows));
@@ -947,8 +1019,10 @@ int boundary_impl(const char* name, b200tx::BoundaryArgs& a, int in_dtype, int o
   if (rows <= 0 || rows > 0x7fffffffLL || inner <= 0 || inner > 0x7fffffffLL)
     return fail(B200TX_ERR_INVALID_ARGUMENT, "%s: bad shape rows=%lld inner=%lld", name, (long long)rows,
                 (long long)inner);
-  if (cols != 32 && cols != 64 && cols != 128)
-    return fail(B200TX_ERR_UNSUPPORTED, "%s: cols (d_model) %lld (built: 32, 64, 128)", name, (long long)cols);
+  const bool wide = !MLP && (cols == 512 || cols == 768 || cols == 1024);
+  if (cols != 32 && cols != 64 && cols != 128 && !wide)
+    return fail(B200TX_ERR_UNSUPPORTED, "%s: cols (d_model) %lld (built: 32, 64, 128%s)", name, (long long)cols,
+                MLP ? "" : ", 512, 768, 1024");
   if (MLP ? inner % 16 != 0 : inner % 8 != 0)
     return fail(B200TX_ERR_UNSUPPORTED, "%s: inner dimension %lld must be a multiple of %d", name,
                 (long long)inner, MLP ? 16 : 8);
@@ -967,6 +1041,7 @@ int boundary_impl(const char* name, b200tx::BoundaryArgs& a, int in_dtype, int o
   a.K = static_cast<int>(inner);
   a.update_bf16 = update_dtype == B200TX_BF16 ? 1 : 0;
   if (a.row_valid == nullptr) a.mask_mode = 0;
+  if (wide) return launch_gemm_rownorm(a, dev, in_dtype, out_dtype, rows, cols, inner, stream);
   cudaError_t err;
   switch (cols) {
     case 32: err = launch_boundary_d<MLP, 32>(a, in_dtype, out_dtype, stream); break;

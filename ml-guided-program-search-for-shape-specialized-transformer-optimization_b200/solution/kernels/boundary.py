@@ -7,7 +7,10 @@ Replaces the reference's fused Linear residual-norm boundary
 the projection that closes a branch, its bias, the rounding of the update to
 the dtype the unfused program stores, the fp32 residual add and the LayerNorm
 run as one kernel; the MLP form also keeps the GELU hidden row in registers.
-Built for d_model 32, 64 and 128.  Conventions as the other wrappers:
+Both are built for d_model 32, 64 and 128 (a row in one warp's registers);
+the Linear form also for d_model 512, 768 and 1024, as a tcgen05 GEMM whose
+CTA pair holds whole rows in tensor memory and normalises them in its
+epilogue (csrc/gemm_rownorm_kernels.cuh).  Conventions as the other wrappers:
 ``can_use_*`` never raises, the ops return ``(residual, normalized, marker)``,
 ``ValueError`` for caller errors, ``RuntimeError`` for ineligible inputs.
 """
@@ -23,6 +26,7 @@ from ._common import is_sm100_cuda, launch, library_ready, require
 SM100_LINEAR_RESIDUAL_NORM_BACKEND = "sm100_linear_residual_norm"
 SM100_MLP_RESIDUAL_NORM_BACKEND = "sm100_mlp_residual_norm"
 BOUNDARY_WIDTHS = (32, 64, 128)
+LINEAR_BOUNDARY_WIDTHS = (32, 64, 128, 512, 768, 1024)
 MLP_HIDDEN_MULTIPLE = 16
 
 _IO = (torch.float32, torch.bfloat16)
@@ -52,11 +56,11 @@ def _f32_vector(t: torch.Tensor, n: int, device: torch.device) -> bool:
     return t.dtype == torch.float32 and tuple(t.shape) == (n,) and t.is_contiguous() and t.device == device
 
 
-def _common_ok(x: torch.Tensor, value: torch.Tensor, layer_norm: nn.LayerNorm) -> bool:
+def _common_ok(x: torch.Tensor, value: torch.Tensor, layer_norm: nn.LayerNorm, widths: tuple[int, ...]) -> bool:
     if not library_ready() or torch.is_grad_enabled() or not is_sm100_cuda(value):
         return False
     width = value.shape[-1]
-    if width not in BOUNDARY_WIDTHS or value.dtype not in _IO or not value.is_contiguous():
+    if width not in widths or value.dtype not in _IO or not value.is_contiguous():
         return False
     if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.device != value.device or x.data_ptr() % 16:
         return False
@@ -71,7 +75,7 @@ def can_use_sm100_linear_residual_norm(
     """Whether the fused Linear boundary can run on these operands (never raises)."""
 
     try:
-        if not _common_ok(x, value, layer_norm):
+        if not _common_ok(x, value, layer_norm, LINEAR_BOUNDARY_WIDTHS):
             return False
         width, inner = value.shape[-1], x.shape[-1]
         return inner % 8 == 0 and _bf16_matrix(weight, (width, inner), value.device) and _f32_vector(
@@ -93,7 +97,7 @@ def can_use_sm100_mlp_residual_norm(
     """Whether the fused MLP boundary can run on these operands (never raises)."""
 
     try:
-        if not _common_ok(x, value, layer_norm):
+        if not _common_ok(x, value, layer_norm, BOUNDARY_WIDTHS):
             return False
         width = value.shape[-1]
         if x.shape[-1] != width:
@@ -222,6 +226,7 @@ def sm100_mlp_residual_norm(
 
 __all__ = [
     "BOUNDARY_WIDTHS",
+    "LINEAR_BOUNDARY_WIDTHS",
     "MLP_HIDDEN_MULTIPLE",
     "SM100_LINEAR_RESIDUAL_NORM_BACKEND",
     "SM100_MLP_RESIDUAL_NORM_BACKEND",

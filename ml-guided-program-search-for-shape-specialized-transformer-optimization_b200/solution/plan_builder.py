@@ -37,7 +37,10 @@ SUPPORTED_HEAD_DIMS = frozenset({64})
 # Head dims built into the CUDA-core attention (b200tx_attention_generic).
 SIMT_HEAD_DIMS = frozenset({8, 16, 32, 64, 128, 256})
 MMA_HEAD_DIMS = frozenset({8, 16, 32, 64, 128})
+# d_model of the fused boundaries: the MLP form holds a row in one warp's
+# registers; the Linear form also runs as a row-complete tcgen05 GEMM.
 BOUNDARY_WIDTHS = frozenset({32, 64, 128})
+LINEAR_BOUNDARY_WIDTHS = BOUNDARY_WIDTHS | {512, 768, 1024}
 # The attention variants that read a key padding mask (B200TX_ATTN_QUAD,
 # B200TX_ATTN_PERSISTENT, B200TX_ATTN_DUO and B200TX_ATTN_PINGPONG).
 SM100_QUAD_ATTENTION_VARIANT = 2
@@ -331,11 +334,11 @@ class PlanBuilder:
         # 783-805): a whole row of d_model in a warp's registers.
         program = config.program
         if program.residual_norm is ResidualNormBackend.SM100_LINEAR_MIXED:
-            if context.d_model not in BOUNDARY_WIDTHS:
+            if context.d_model not in LINEAR_BOUNDARY_WIDTHS:
                 reject(
                     "unsupported_shape",
                     "program.residual_norm",
-                    f"the fused Linear residual-norm boundary is built for d_model {sorted(BOUNDARY_WIDTHS)}, "
+                    f"the fused Linear residual-norm boundary is built for d_model {sorted(LINEAR_BOUNDARY_WIDTHS)}, "
                     f"not {context.d_model}",
                 )
         if program.ffn is FFNBackend.SM100_FUSED_MLP_BOUNDARY:
@@ -344,6 +347,12 @@ class PlanBuilder:
                     "backend_incompatible",
                     "program.residual_norm",
                     "the fused MLP boundary requires the fused Linear residual-norm boundary",
+                )
+            if context.d_model not in BOUNDARY_WIDTHS:
+                reject(
+                    "unsupported_shape",
+                    "program.ffn",
+                    f"the fused MLP boundary is built for d_model {sorted(BOUNDARY_WIDTHS)}, not {context.d_model}",
                 )
             if ffn_dim is not None and ffn_dim > 0 and ffn_dim % 16:
                 reject(

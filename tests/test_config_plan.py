@@ -273,14 +273,22 @@ def test_fused_boundaries_drop_the_fused_projections_launch_records(fusion: str)
 
 
 @pytest.mark.parametrize("fusion", ["linear", "mlp"])
-def test_fused_boundaries_accepted_for_small_d_model_only(fusion: str) -> None:
-    for width in (32, 64, 128):
-        context = _context(d_model=width, num_heads=width // 32 if width > 32 else 1, ffn_dim=4 * width)
-        assert PlanBuilder().evaluate(_fused(fusion), context, B200).accepted, width
+def test_fused_boundaries_accepted_for_their_built_widths(fusion: str) -> None:
+    """Both boundaries are built for d_model 32, 64 and 128; the Linear one
+    also for 512, 768 and 1024 (the row-complete tcgen05 GEMM)."""
+
+    for width in (32, 64, 128, 512, 768, 1024):
+        heads = max(1, width // 64)
+        context = _context(d_model=width, num_heads=heads, ffn_dim=4 * width)
+        accepted = PlanBuilder().evaluate(_fused(fusion), context, B200).accepted
+        assert accepted == (fusion == "linear" or width <= 128), width
     result = PlanBuilder().evaluate(_fused(fusion), _context(), B200)  # d_model 256
     assert not result.accepted and "unsupported_shape" in _codes(result)
     fields = {v.field for v in result.violations}
     assert "program.residual_norm" in fields
+    if fusion == "mlp":
+        wide = PlanBuilder().evaluate(_fused(fusion), _context(d_model=1024, num_heads=16, ffn_dim=4096), B200)
+        assert {v.field for v in wide.violations} == {"program.ffn"}
 
 
 def test_fused_mlp_needs_the_fused_linear_boundary_and_ffn_dim_multiple_of_16() -> None:

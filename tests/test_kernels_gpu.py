@@ -565,6 +565,13 @@ def _boundary_reference(
         (129, 128, 512, torch.bfloat16, torch.bfloat16, True, 0),  # FFN-out shape, bf16 residual input
         (200, 128, 128, torch.float32, torch.bfloat16, True, 1),  # drop the update of padding rows
         (200, 32, 32, torch.float32, torch.float32, True, 2 | 4),  # zero residual and output
+        # d_model 512 / 768 / 1024: the row-complete tcgen05 GEMM (CTA pair per 128-row tile)
+        (1, 512, 512, torch.float32, torch.bfloat16, True, 0),  # one row of one tile
+        (300, 768, 768, torch.float32, torch.bfloat16, True, 0),  # ragged last tile, 3 pieces per CTA
+        (257, 512, 200, torch.float32, torch.float32, False, 0),  # last K slab partly outside x and w
+        (19205, 1024, 4096, torch.bfloat16, torch.bfloat16, True, 0),  # FFN-out; pairs walk 151 tiles
+        (1000, 1024, 1024, torch.float32, torch.bfloat16, True, 1),  # drop the update of padding rows
+        (1000, 768, 3072, torch.float32, torch.float32, True, 2 | 4),  # zero residual and output
     ],
 )
 def test_linear_residual_norm(rows, width, inner, in_dtype, out_dtype, update_bf16, mask_mode) -> None:  # noqa: ANN001

@@ -331,6 +331,49 @@ def test_fused_boundaries_match_the_oracle_and_the_unfused_program(case: str, fu
         assert torch.equal(_run(model, x), y)  # replays give the same bits
 
 
+@pytest.mark.parametrize(
+    "cfg",
+    [OfficialConfig(4, 256, 768, 12, 3072, 2), OfficialConfig(2, 384, 1024, 16, 4096, 2)],
+    ids=["d768", "d1024"],
+)
+def test_wide_linear_boundary_matches_the_oracle_and_the_unfused_program(cfg: OfficialConfig) -> None:
+    """d_model 768 / 1024 (the C3 and C2/C5 widths): the out-projection and
+    FFN-out GEMMs fused with their residual LayerNorm by the row-complete
+    tcgen05 kernel, eager and graph-replayed, with and without a padding mask."""
+
+    x = official_input(cfg, 9)
+    rows = [0, cfg.batch_size - 1]
+    ref = _rows_reference(cfg, x, rows)
+    unfused = _run(_model(cfg, ConfigSpec(program=default_program(), schedule=default_schedule())), x)
+    for runtime in (RuntimeBackend.EAGER, RuntimeBackend.CUDA_GRAPH):
+        config = ConfigSpec(
+            program=default_program(fused_boundary="linear"),
+            schedule=default_schedule(runtime, fused_boundary="linear"),
+        )
+        model = _model(cfg, config)
+        if runtime is RuntimeBackend.EAGER:
+            model.set_execution_observation(True)
+        y = _run(model, x)
+        _gate(y[rows], ref)
+        max_abs, rel = parity_errors(y.float().cpu().numpy(), unfused.float().cpu().numpy())
+        assert max_abs < 2e-2 and rel < 5e-3, (runtime, max_abs, rel)
+        if runtime is RuntimeBackend.EAGER:
+            description = model.describe_execution_path()
+            assert dict(description["observed_execution_signature"]) == dict(
+                description["expected_execution_signature"]
+            )
+        assert torch.equal(_run(model, x), y)
+    mask = torch.ones(cfg.batch_size, cfg.seq_len, dtype=torch.bool)
+    mask[0, :37] = False
+    mask[-1, cfg.seq_len - 100:] = False
+    eager = ConfigSpec(program=default_program(fused_boundary="linear"), schedule=default_schedule(fused_boundary="linear"))
+    y = _run(_model(cfg, eager), x, mask)
+    y_unfused = _run(_model(cfg, ConfigSpec(program=default_program(), schedule=default_schedule())), x, mask)
+    assert not y.cpu()[~mask].any(), "padding rows must be exactly zero"
+    max_abs, rel = parity_errors(y.float().cpu().numpy(), y_unfused.float().cpu().numpy())
+    assert max_abs < 2e-2 and rel < 5e-3, ("masked", max_abs, rel)
+
+
 @pytest.mark.parametrize("fusion", ["linear", "mlp"])
 def test_fused_boundaries_with_a_padding_mask(fusion: str) -> None:
     from solution.config import AttentionBackend
