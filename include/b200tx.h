@@ -225,7 +225,9 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
 /*
  * The projection that closes a block branch fused with the residual add and
  * LayerNorm after it, for d_model (cols) 32, 64 or 128 (CTAs of 16 rows whose
- * four warps split the columns; warp-level tensor-core MMAs):
+ * four warps split the columns; warp-level tensor-core MMAs) and 512, 768 or
+ * 1024 (tcgen05 CTA pairs in clusters of 2 * cols / 256 CTAs holding 256 whole
+ * rows; residual_in, residual_out and normed 16-byte aligned there):
  *     u = x[rows, inner] . w[cols, inner]^T + bias[cols]   (rounded to update_dtype)
  *     r = residual_in + u;  normed = LayerNorm(r) * gamma + beta
  * x, w BF16 row-major; bias, gamma, beta F32; residual_in in_dtype (F32 or

@@ -67,6 +67,7 @@ struct DeviceState {
   bool gemm_attr[8] = {false, false, false, false, false, false, false, false};
   bool attn_attr[2 * kAttnVariants] = {};  // unmasked builds by variant, then the masked builds
   bool rownorm_attr[4] = {};               // GEMM + residual LayerNorm builds by (in, out) dtype
+  int rownorm_clusters[4][5] = {};         // their co-resident clusters by CTA pairs per cluster
 };
 
 std::mutex g_mutex;
@@ -117,9 +118,9 @@ int encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
 // Tiled bf16 tensor map (128-byte swizzle unless given); out-of-range elements
 // of a box read as zero and are not written by stores.  dims/strides innermost
 // first; strides in bytes for dims 1..
-int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box,
-                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                     CUtensorMapSwizzle swizzle) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   int rc = encoder(&encode);
   if (rc != B200TX_OK) return rc;
@@ -133,7 +134,7 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
     es[i] = 1;
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
-  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+  CUresult res = encode(map, dtype, static_cast<cuuint32_t>(rank),
                         const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -141,6 +142,22 @@ int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t
     return fail(B200TX_ERR_DRIVER, "cuTensorMapEncodeTiled failed with CUresult %d", int(res));
   }
   return B200TX_OK;
+}
+
+int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  return encode_tiled_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swizzle);
+}
+
+// A [rows, cols] row-major matrix of fp32 or bf16 in 32 x 32 boxes (128- or
+// 64-byte rows, swizzled to match).
+int encode_box32_map(CUtensorMap* map, const void* base, bool fp32, int64_t rows, int64_t cols) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(cols) * (fp32 ? 4 : 2)};
+  const uint32_t box[2] = {32u, 32u};
+  return encode_tiled_map(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, 2,
+                          dims, strides, box, fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -162,6 +179,27 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// As launch, for kernels whose cluster size is chosen at run time.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cluster_x,
+                             cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -919,60 +957,62 @@ int b200tx_attention_mma(const void* qkv, const uint8_t* key_valid, void* out, i
 
 namespace {
 
-// The Linear boundary at d_model 512 / 768 / 1024: a tcgen05 GEMM whose CTA
-// pair holds whole rows in TMEM and applies the residual LayerNorm in its
-// epilogue (gemm_rownorm_kernels.cuh).
+// The Linear boundary at d_model 512 / 768 / 1024: a tcgen05 GEMM whose
+// clusters of CTA pairs hold whole rows and apply the residual LayerNorm in
+// their epilogue (gemm_rownorm_kernels.cuh).
 int launch_gemm_rownorm(const b200tx::BoundaryArgs& a, DeviceState* dev, int in_dtype, int out_dtype,
                         int64_t rows, int64_t cols, int64_t inner, cudaStream_t stream) {
-  const size_t in_align = in_dtype == B200TX_F32 ? 16 : 8;
-  if ((reinterpret_cast<uintptr_t>(a.residual_in) % in_align) != 0 ||
-      (a.residual_out != nullptr && !aligned16(a.residual_out)) ||
-      (reinterpret_cast<uintptr_t>(a.normed) % (out_dtype == B200TX_F32 ? 16 : 8)) != 0 ||
-      (reinterpret_cast<uintptr_t>(a.bias) & 3u) != 0)
-    return fail(B200TX_ERR_INVALID_ARGUMENT, "linear_residual_layer_norm: misaligned operand at d_model %lld",
+  if (!aligned16(a.residual_in) || (a.residual_out != nullptr && !aligned16(a.residual_out)) ||
+      !aligned16(a.normed) || (reinterpret_cast<uintptr_t>(a.bias) & 3u) != 0)
+    return fail(B200TX_ERR_INVALID_ARGUMENT,
+                "linear_residual_layer_norm: at d_model %lld residual_in, residual_out and normed must be "
+                "16-byte aligned",
                 (long long)cols);
-  CUtensorMap map_x, map_w;
+  const bool in_f32 = in_dtype == B200TX_F32;
+  const bool out_f32 = out_dtype == B200TX_F32;
+  CUtensorMap map_x, map_w, map_rin;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(inner) * 2};
-    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), static_cast<uint32_t>(b200tx::kRnBM)};
+    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), 128u};
     int rc = encode_bf16_map(&map_x, a.x, 2, dims, strides, box);
     if (rc != B200TX_OK) return rc;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(cols)};
     const uint64_t strides[1] = {static_cast<uint64_t>(inner) * 2};
-    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), static_cast<uint32_t>(b200tx::kRnPieceRows)};
+    const uint32_t box[2] = {static_cast<uint32_t>(b200tx::kRnBK), 128u};
     int rc = encode_bf16_map(&map_w, a.w, 2, dims, strides, box);
     if (rc != B200TX_OK) return rc;
   }
+  int rc = encode_box32_map(&map_rin, a.residual_in, in_f32, rows, cols);
+  if (rc != B200TX_OK) return rc;
   b200tx::RowNormArgs r;
   r.bias = a.bias;
-  r.residual_in = a.residual_in;
-  r.residual_out = a.residual_out;
-  r.normed = a.normed;
   r.gamma = a.gamma;
   r.beta = a.beta;
   r.row_valid = a.row_valid;
+  r.residual_out = a.residual_out;
+  r.normed = a.normed;
   r.mask_mode = a.mask_mode;
   r.rows = static_cast<int>(rows);
   r.cols = static_cast<int>(cols);
   r.inner = static_cast<int>(inner);
+  r.pairs = static_cast<int>(cols / b200tx::kRnBN);
   r.num_tiles = static_cast<int>((rows + b200tx::kRnBM - 1) / b200tx::kRnBM);
   r.round_update_bf16 = a.update_bf16;
   r.eps = a.eps;
-  // Persistent: one CTA pair per two SMs, walking the 128-row tiles.
-  const int64_t pairs_avail = dev->sm_count / 2;
-  const int64_t pairs = r.num_tiles < pairs_avail ? r.num_tiles : pairs_avail;
-  using KernelFn = void (*)(CUtensorMap, CUtensorMap, b200tx::RowNormArgs);
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, b200tx::RowNormArgs);
   KernelFn kernel;
-  const int instance = (in_dtype == B200TX_F32 ? 2 : 0) + (out_dtype == B200TX_F32 ? 1 : 0);
+  const int instance = (in_f32 ? 2 : 0) + (out_f32 ? 1 : 0);
   switch (instance) {
     case 0: kernel = b200tx::gemm_residual_layernorm_kernel<__nv_bfloat16, __nv_bfloat16>; break;
     case 1: kernel = b200tx::gemm_residual_layernorm_kernel<__nv_bfloat16, float>; break;
     case 2: kernel = b200tx::gemm_residual_layernorm_kernel<float, __nv_bfloat16>; break;
     default: kernel = b200tx::gemm_residual_layernorm_kernel<float, float>; break;
   }
+  const unsigned cluster = static_cast<unsigned>(2 * r.pairs);
+  int max_clusters = 0;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!dev->rownorm_attr[instance]) {
@@ -982,9 +1022,33 @@ int launch_gemm_rownorm(const b200tx::BoundaryArgs& a, DeviceState* dev, int in_
       if (err != cudaSuccess) return cuda_fail(err, "linear_residual_layer_norm: cudaFuncSetAttribute");
       dev->rownorm_attr[instance] = true;
     }
+    int& cached = dev->rownorm_clusters[instance][r.pairs];
+    if (cached == 0) {
+      // How many clusters of this size the device holds at once (one CTA per SM).
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cluster * 64);
+      cfg.blockDim = dim3(b200tx::kRnThreads);
+      cfg.dynamicSmemBytes = b200tx::kRnSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = cluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaError_t err = cudaOccupancyMaxActiveClusters(&cached, reinterpret_cast<const void*>(kernel), &cfg);
+      if (err != cudaSuccess) return cuda_fail(err, "linear_residual_layer_norm: cudaOccupancyMaxActiveClusters");
+      if (cached <= 0)
+        return fail(B200TX_ERR_UNSUPPORTED, "linear_residual_layer_norm: no cluster of %u CTAs fits the device",
+                    cluster);
+    }
+    max_clusters = cached;
   }
-  cudaError_t err = launch(kernel, dim3(static_cast<unsigned>(2 * pairs)), dim3(b200tx::kRnThreads),
-                           b200tx::kRnSmemBytes, stream, map_x, map_w, r);
+  // Persistent: as many clusters as are co-resident, walking the 256-row tiles.
+  const int clusters = r.num_tiles < max_clusters ? r.num_tiles : max_clusters;
+  cudaError_t err = launch_clustered(kernel, dim3(static_cast<unsigned>(clusters) * cluster),
+                                     dim3(b200tx::kRnThreads), b200tx::kRnSmemBytes, cluster, stream, map_x, map_w,
+                                     map_rin, r);
   if (err != cudaSuccess) return cuda_fail(err, "linear_residual_layer_norm (row-complete GEMM) launch");
   return B200TX_OK;
 }
