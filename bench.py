@@ -782,7 +782,11 @@ def run_gpu(args: argparse.Namespace) -> None:
     main = measure_workload(ctx, args.workload, args.steps, warmup, full=True)
     extras: dict[str, dict] = {}
     if args.workload == "c2" and args.extras != "none":
-        for name in args.extras.split(","):
+        for name in (n.strip() for n in args.extras.split(",")):
+            if not name:
+                continue
+            if name not in WORKLOADS:
+                raise SystemExit(f"--extras: unknown workload {name!r} (choose from {sorted(WORKLOADS)} or 'none')")
             steps = {"c3": args.steps, "c4": min(args.steps, 10), "c5": min(args.steps, 3)}.get(name, args.steps)
             extras[name] = measure_workload(ctx, name, steps, 3, full=False)
     tp_parity = tensor_parallel_parity(ctx) if world >= 2 and not args.skip_tp_parity else None
