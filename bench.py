@@ -455,10 +455,15 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         group, _, _ = tensor_parallel_groups(tp)
         partials = torch.bfloat16 if args.tp_partials == "bf16" else torch.float32
         reduction = args.tp_reduction if args.tp_reduction != "auto" else ("peer" if tp == 2 else "nccl")
+        # peer: the whole partials of every peer for groups of two, the
+        # reduce-scatter + gather form for larger groups; peer-full and
+        # peer-scatter force one of them.
+        scatter = {"peer-full": False, "peer-scatter": True}.get(reduction)
         # The error word is read once after all steps (device_error below),
         # not after every step, so the host keeps running ahead of the GPU.
         runner = TensorParallelTransformer(
-            model, group=group, partial_dtype=partials, reduction=reduction, check_peer_errors=False
+            model, group=group, partial_dtype=partials, reduction="nccl" if reduction == "nccl" else "peer",
+            check_peer_errors=False, peer_scatter=scatter,
         )
     else:
         reduction = None
@@ -662,8 +667,14 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         + (
             f"tp{tp} (head-sharded, NCCL all-reduce of {args.tp_partials} partials after out-proj and FFN-down)"
             if reduction == "nccl"
-            else f"tp{tp} (head-sharded, bf16 partials summed over NVLink peer memory inside the residual "
-            "LayerNorm after out-proj and FFN-down)"
+            else (
+                f"tp{tp} (head-sharded, each rank sums the group's bf16 partials for its slice of the rows over "
+                "NVLink peer memory inside the residual LayerNorm and writes the normalised slice into every "
+                "rank's buffer, after out-proj and FFN-down)"
+                if getattr(getattr(runner, "_peer", None), "scatter", False)
+                else f"tp{tp} (head-sharded, bf16 partials summed over NVLink peer memory inside the residual "
+                "LayerNorm after out-proj and FFN-down)"
+            )
         )
         if parallel == "heads"
         else f"dp{world} (batch-sharded, no collective)"
@@ -1143,9 +1154,11 @@ def main() -> None:
                              "(one launch per kernel, for ncu launch lists)")
     parser.add_argument("--tp", type=int, default=0,
                         help="c4 under torchrun: tensor-parallel group size (default: max(2, N / B))")
-    parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer"), default="auto",
+    parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer", "peer-full", "peer-scatter"), default="auto",
                         help="c4: NCCL all-reduce, or the peer-memory reduction fused into the "
-                             "LayerNorm (auto: peer for groups of 2, NCCL otherwise)")
+                             "LayerNorm: peer (whole partials for groups of 2, reduce-scatter + gather for "
+                             "larger groups), peer-full / peer-scatter (forced); auto: peer for groups of 2, "
+                             "NCCL otherwise")
     parser.add_argument("--tp-partials", choices=("fp32", "bf16"), default="bf16",
                         help="dtype of the partial sums all-reduced by the head-sharded runtime")
     parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")

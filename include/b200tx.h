@@ -301,6 +301,32 @@ int b200tx_residual_layer_norm_peer(const float* residual_in, const void* const*
                                     int mask_mode, int64_t rows, int64_t cols, float eps,
                                     cudaStream_t stream);
 
+/*
+ * Reduce-scatter + all-gather form of b200tx_residual_layer_norm_peer for
+ * groups of three or more ranks (count 2..8): after the same epoch wait, this
+ * rank sums the partials only for its rows [row_begin, row_begin + row_count)
+ * of the [rows, cols] tensors, writes residual_out for those rows (may be NULL)
+ * and the normalised rows into outs[r] for every rank r (outs[self] local, the
+ * others peers' buffers, out_dtype F32 or BF16).  When every CTA is done (a
+ * count on *counter, which starts at counter_base and ends at *counter_after,
+ * returned), epoch is published into done_slots[r], this rank's slot in each
+ * peer's done flags (done_slots[self] unused).  No padding-row mask.  No
+ * reference counterpart (the reference runs on one GPU); it serves the
+ * head-sharded runtime as b200tx_residual_layer_norm_peer does.
+ */
+int b200tx_residual_layer_norm_peer_rs(const float* residual_in, const void* const* partials, int count,
+                                       int self, const uint32_t* flags, uint32_t epoch, int64_t row_begin,
+                                       int64_t row_count, float* residual_out, void* const* outs,
+                                       int out_dtype, const float* gamma, const float* beta,
+                                       uint32_t* const* done_slots, uint32_t* counter, uint32_t counter_base,
+                                       uint32_t* counter_after, int64_t rows, int64_t cols, float eps,
+                                       cudaStream_t stream);
+
+/* Holds the stream (one thread, bounded system-scope acquire spin) until
+ * flags[r] >= epoch for every r != self; a wait that runs out records its code
+ * in b200tx_device_error. */
+int b200tx_peer_wait(const uint32_t* flags, int count, int self, uint32_t epoch, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

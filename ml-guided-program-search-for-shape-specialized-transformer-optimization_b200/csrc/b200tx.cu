@@ -860,6 +860,100 @@ int b200tx_residual_layer_norm_peer(const float* residual_in, const void* const*
   return B200TX_OK;
 }
 
+int b200tx_residual_layer_norm_peer_rs(const float* residual_in, const void* const* partials, int count,
+                                       int self, const uint32_t* flags, uint32_t epoch, int64_t row_begin,
+                                       int64_t row_count, float* residual_out, void* const* outs,
+                                       int out_dtype, const float* gamma, const float* beta,
+                                       uint32_t* const* done_slots, uint32_t* counter, uint32_t counter_base,
+                                       uint32_t* counter_after, int64_t rows, int64_t cols, float eps,
+                                       cudaStream_t stream) {
+  if (residual_in == nullptr || partials == nullptr || flags == nullptr || outs == nullptr ||
+      done_slots == nullptr || counter == nullptr || gamma == nullptr || beta == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer_rs: null pointer");
+  if (count < 2 || count > b200tx::kMaxPeers || self < 0 || self >= count)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer_rs: count %d self %d", count, self);
+  if (rows <= 0 || cols <= 0 || cols % 128 != 0 || row_begin < 0 || row_count <= 0 ||
+      row_begin + row_count > rows || (row_count + 7) / 8 > 0x7fffffffLL)
+    return fail(B200TX_ERR_UNSUPPORTED,
+                "residual_layer_norm_peer_rs: rows [%lld, %lld) of [%lld, %lld] (cols %% 128 == 0)",
+                (long long)row_begin, (long long)(row_begin + row_count), (long long)rows, (long long)cols);
+  if (out_dtype != B200TX_F32 && out_dtype != B200TX_BF16)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer_rs: out_dtype %d", out_dtype);
+  bool ok = aligned16(residual_in) && aligned16(gamma) && aligned16(beta) &&
+            (residual_out == nullptr || aligned16(residual_out)) &&
+            (reinterpret_cast<uintptr_t>(counter) & 3u) == 0;
+  b200tx::PeerSumArgs p = {};
+  b200tx::PeerGatherArgs g = {};
+  for (int i = 0; i < count; ++i) {
+    if (partials[i] == nullptr || (reinterpret_cast<uintptr_t>(partials[i]) & 7u) != 0) ok = false;
+    if (outs[i] == nullptr || !aligned16(outs[i])) ok = false;
+    if (i != self && done_slots[i] == nullptr) ok = false;
+    p.partials[i] = static_cast<const __nv_bfloat16*>(partials[i]);
+    g.outs[i] = outs[i];
+    g.done_slots[i] = i == self ? nullptr : done_slots[i];
+  }
+  if (!ok) return fail(B200TX_ERR_INVALID_ARGUMENT, "residual_layer_norm_peer_rs: misaligned or null operand");
+  p.count = count;
+  p.self = self;
+  p.flags = flags;
+  p.epoch = epoch;
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  b200tx::NormArgs a;
+  a.residual_in = residual_in;
+  a.update = nullptr;
+  a.residual_out = residual_out;
+  a.normed = outs[self];
+  a.gamma = gamma;
+  a.beta = beta;
+  a.row_valid = nullptr;
+  a.mask_mode = 0;
+  a.rows = row_count;
+  a.cols = static_cast<int>(cols);
+  a.eps = eps;
+  const unsigned ctas = static_cast<unsigned>((row_count + b200tx::kNormWarpsPerBlock - 1) / b200tx::kNormWarpsPerBlock);
+  g.counter = counter;
+  g.counter_target = counter_base + ctas;
+  g.row_begin = row_begin;
+  const dim3 block(b200tx::kNormWarpsPerBlock * 32);
+  const bool bf16 = out_dtype == B200TX_BF16;
+  cudaError_t err;
+#define B200TX_PEER_RS_NV(NV)                                                                            \
+  case NV:                                                                                              \
+    err = bf16 ? launch(b200tx::residual_layernorm_peer_rs_kernel<NV, __nv_bfloat16>, dim3(ctas), block, 0, \
+                        stream, a, p, g)                                                                \
+               : launch(b200tx::residual_layernorm_peer_rs_kernel<NV, float>, dim3(ctas), block, 0, stream, a, \
+                        p, g);                                                                          \
+    break;
+  switch (cols / 128) {
+    B200TX_PEER_RS_NV(1)
+    B200TX_PEER_RS_NV(2)
+    B200TX_PEER_RS_NV(4)
+    B200TX_PEER_RS_NV(6)
+    B200TX_PEER_RS_NV(8)
+    B200TX_PEER_RS_NV(12)
+    B200TX_PEER_RS_NV(16)
+    default:
+      return fail(B200TX_ERR_UNSUPPORTED, "residual_layer_norm_peer_rs: cols %lld not built", (long long)cols);
+  }
+#undef B200TX_PEER_RS_NV
+  if (err != cudaSuccess) return cuda_fail(err, "residual_layer_norm_peer_rs launch");
+  if (counter_after != nullptr) *counter_after = g.counter_target;
+  return B200TX_OK;
+}
+
+int b200tx_peer_wait(const uint32_t* flags, int count, int self, uint32_t epoch, cudaStream_t stream) {
+  if (flags == nullptr || count < 1 || count > b200tx::kMaxPeers || self < 0 || self >= count)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "peer_wait: count %d self %d", count, self);
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  cudaError_t err = launch(b200tx::peer_wait_kernel, dim3(1), dim3(32), 0, stream, flags, count, self, epoch);
+  if (err != cudaSuccess) return cuda_fail(err, "peer_wait launch");
+  return B200TX_OK;
+}
+
 int b200tx_attention_generic(const void* qkv, const uint8_t* key_valid, void* out, int64_t batch,
                              int64_t seq, int64_t heads, int64_t head_dim, float scale, int causal,
                              cudaStream_t stream) {

@@ -395,6 +395,123 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
   }
 }
 
+// Reduce-scatter + all-gather form for groups of three or more ranks: each
+// rank sums the group's partials only for its own slice of rows [row_begin,
+// row_begin + rows), adds the residual, normalises, keeps residual_out for
+// those rows and writes the normalised rows into every rank's output buffer
+// (`outs`, its own local, the others peer memory).  NVLink traffic per rank:
+// (P - 1)/P of the rows' partials in and as many normalised rows out, instead
+// of every peer's whole partial.  Each thread fences its stores at system scope
+// before its CTA counts itself done on a local counter; the CTA that completes
+// the launch's count publishes `epoch` into this rank's slot of every peer's
+// done flags (release, system scope).  peer_wait_kernel then holds the stream
+// until every peer's slice has landed here.  Rows are independent, so each
+// row is computed by one rank only and the ranks agree by construction.
+struct PeerGatherArgs {
+  void* outs[kMaxPeers];            // [rows_total, cols] OutT of every rank, index = group rank
+  uint32_t* done_slots[kMaxPeers];  // this rank's slot in each peer's done flags (null: none)
+  uint32_t* counter;                // this rank's CTA counter (monotonic)
+  uint32_t counter_target;          // its value once every CTA of this launch is done
+  int64_t row_begin;
+};
+
+template <int NV, typename OutT>
+__global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
+    residual_layernorm_peer_rs_kernel(NormArgs args, PeerSumArgs peers, PeerGatherArgs g) {
+  griddep_wait();
+  griddep_launch_dependents();
+  // A CTA that gives up here never counts itself done: the peers' waits for
+  // this rank's slice run out and record the error too.
+  if (!wait_peer_epoch(peers)) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t local_row = static_cast<int64_t>(blockIdx.x) * kNormWarpsPerBlock + (threadIdx.x >> 5);
+  if (local_row < args.rows) {
+    const int cols = 128 * NV;
+    const int64_t base = (g.row_begin + local_row) * cols;
+    const float* rin = static_cast<const float*>(args.residual_in);
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = load4<float>(rin, base + (i * 32 + lane) * 4);
+    for (int r = 0; r < peers.count; ++r) {
+      const __nv_bfloat16* part = peers.partials[r];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t idx = base + (i * 32 + lane) * 4;
+        const uint2 raw = r == peers.self ? __ldg(reinterpret_cast<const uint2*>(part + idx))
+                                          : __ldcg(reinterpret_cast<const uint2*>(part + idx));
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        v[i].x += a.x;
+        v[i].y += a.y;
+        v[i].z += b.x;
+        v[i].w += b.y;
+      }
+    }
+    if (args.residual_out != nullptr) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) store4<float>(args.residual_out, base + (i * 32 + lane) * 4, v[i]);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) * (1.0f / cols);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / cols) + args.eps);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      const float4 gm = __ldg(reinterpret_cast<const float4*>(args.gamma + c));
+      const float4 bt = __ldg(reinterpret_cast<const float4*>(args.beta + c));
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * gm.x + bt.x;
+      o.y = (v[i].y - mean) * rstd * gm.y + bt.y;
+      o.z = (v[i].z - mean) * rstd * gm.z + bt.z;
+      o.w = (v[i].w - mean) * rstd * gm.w + bt.w;
+      // The peers' copies first (NVLink), then this rank's.
+      for (int k = 1; k <= peers.count; ++k) {
+        const int r = (peers.self + k) % peers.count;
+        store4<OutT>(static_cast<OutT*>(g.outs[r]), base + c, o);
+      }
+    }
+  }
+  // Every thread's stores are visible system-wide before its CTA counts itself.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t done = atomicAdd(g.counter, 1u) + 1u;
+    if (done == g.counter_target) {
+      __threadfence_system();
+      for (int r = 0; r < peers.count; ++r)
+        if (g.done_slots[r] != nullptr) st_release_sys(g.done_slots[r], peers.epoch);
+    }
+  }
+}
+
+// Holds the stream until every peer has published `epoch` into this rank's
+// done flags (bounded acquire spin at system scope, one thread; a wait that
+// runs out records kErrPeerWait).
+__global__ void peer_wait_kernel(const uint32_t* flags, int count, int self, uint32_t epoch) {
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x != 0) return;
+  const unsigned long long start = global_timer_ns();
+  for (int r = 0; r < count; ++r) {
+    if (r == self) continue;
+    uint32_t spins = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(flags + r) - epoch) < 0) {
+      if ((++spins & 63u) == 0u && (device_error_raised() || global_timer_ns() - start > kWaitTimeoutNs)) {
+        record_device_error(kErrPeerWait);
+        return;
+      }
+    }
+  }
+}
+
 // Publishes `epoch` to the peers after this rank's partial is complete: the
 // kernel runs after the GEMM on the stream, fences at system scope and stores
 // the epoch with release semantics into this rank's slot of every peer's flag

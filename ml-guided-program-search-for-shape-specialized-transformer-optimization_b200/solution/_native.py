@@ -207,6 +207,32 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_float,  # eps
         _c_void_p,  # stream
     ]
+    lib.b200tx_residual_layer_norm_peer_rs.restype = ctypes.c_int
+    lib.b200tx_residual_layer_norm_peer_rs.argtypes = [
+        _c_void_p,  # residual_in (fp32)
+        ctypes.POINTER(ctypes.c_void_p),  # partials
+        ctypes.c_int,  # count
+        ctypes.c_int,  # self
+        _c_void_p,  # flags
+        ctypes.c_uint32,  # epoch
+        _c_int64,  # row_begin
+        _c_int64,  # row_count
+        _c_void_p,  # residual_out
+        ctypes.POINTER(ctypes.c_void_p),  # outs
+        ctypes.c_int,  # out_dtype
+        _c_void_p,  # gamma
+        _c_void_p,  # beta
+        ctypes.POINTER(ctypes.c_void_p),  # done_slots
+        _c_void_p,  # counter
+        ctypes.c_uint32,  # counter_base
+        ctypes.POINTER(ctypes.c_uint32),  # counter_after
+        _c_int64,  # rows
+        _c_int64,  # cols
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
+    lib.b200tx_peer_wait.restype = ctypes.c_int
+    lib.b200tx_peer_wait.argtypes = [_c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _c_void_p]
     lib.b200tx_attention_generic.restype = ctypes.c_int
     lib.b200tx_attention_generic.argtypes = [
         _c_void_p,  # qkv
@@ -691,6 +717,72 @@ def residual_layer_norm_peer(
     )
 
 
+def residual_layer_norm_peer_rs(
+    residual_in: torch.Tensor,
+    partials: list[int],
+    self_index: int,
+    flags: int,
+    epoch: int,
+    row_begin: int,
+    row_count: int,
+    residual_out: torch.Tensor | None,
+    outs: list[int],
+    out_dtype: torch.dtype,
+    gamma: torch.Tensor,
+    beta: torch.Tensor,
+    eps: float,
+    done_slots: list[int],
+    counter: int,
+    counter_base: int,
+) -> int:
+    """Launch b200tx_residual_layer_norm_peer_rs: this rank's rows of
+    residual + the group's partials, normalised into every rank's output
+    buffer (device pointers, index = group rank); returns the CTA counter's
+    value once the launch is done."""
+
+    cols = residual_in.shape[-1]
+    rows = residual_in.numel() // cols
+    count = len(partials)
+    parts = (ctypes.c_void_p * count)(*partials)
+    out_arr = (ctypes.c_void_p * count)(*outs)
+    slots = (ctypes.c_void_p * count)(*[s or None for s in done_slots])
+    after = ctypes.c_uint32(0)
+    _check(
+        load().b200tx_residual_layer_norm_peer_rs(
+            residual_in.data_ptr(),
+            parts,
+            count,
+            int(self_index),
+            flags,
+            epoch & 0xFFFFFFFF,
+            int(row_begin),
+            int(row_count),
+            None if residual_out is None else residual_out.data_ptr(),
+            out_arr,
+            dtype_code(out_dtype),
+            gamma.data_ptr(),
+            beta.data_ptr(),
+            slots,
+            counter,
+            counter_base & 0xFFFFFFFF,
+            ctypes.byref(after),
+            rows,
+            cols,
+            float(eps),
+            _stream(residual_in.device),
+        ),
+        "b200tx_residual_layer_norm_peer_rs",
+    )
+    return int(after.value)
+
+
+def peer_wait(flags: int, count: int, self_index: int, epoch: int, device: torch.device) -> None:
+    """Launch b200tx_peer_wait: hold the stream until every peer's flag reaches `epoch`."""
+
+    _check(load().b200tx_peer_wait(flags, int(count), int(self_index), epoch & 0xFFFFFFFF, _stream(device)),
+           "b200tx_peer_wait")
+
+
 __all__ = [
     "IPC_HANDLE_BYTES",
     "peer_alloc",
@@ -698,7 +790,9 @@ __all__ = [
     "peer_free",
     "peer_open",
     "peer_signal",
+    "peer_wait",
     "residual_layer_norm_peer",
+    "residual_layer_norm_peer_rs",
     "ABI_VERSION",
     "ATTN_DUO",
     "ATTN_PINGPONG",

@@ -29,7 +29,11 @@ solution/shape14/executor.py:12-49; the reference itself is single-GPU):
     kernel publishes an epoch into each peer's flag array, and the residual
     LayerNorm kernel itself waits for the peers' epochs and sums all partials
     over NVLink loads while it normalises -- the reduction is fused into the
-    kernel that consumes it, and no all-reduce moves the data twice.
+    kernel that consumes it, and no all-reduce moves the data twice.  Groups
+    of three or more (``peer_scatter``) reduce and normalise only their own
+    slice of the rows and write it into every rank's gather buffer, so a
+    rank moves (P - 1)/P of the rows each way instead of P - 1 whole
+    partials; the residual stream then stays sharded by rows.
 
 Failures inside a step.  On the NCCL path a departed peer ends the step's
 collective with an error after the process group's timeout.  On the peer
@@ -92,6 +96,25 @@ class _DeviceBuffer:
         return self.ptr
 
 
+class _CudaArray:
+    """A device allocation of this library presented to torch through the
+    CUDA array interface (no ownership: the owner frees it)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str) -> None:
+        self.__cuda_array_interface__ = {
+            "shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3, "strides": None,
+        }
+
+
+def _tensor_view(ptr: int, shape: tuple[int, int], dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A torch tensor over `ptr` (bf16 through its 16-bit bit pattern)."""
+
+    typestr = {torch.float32: "<f4", torch.bfloat16: "<u2"}[dtype]
+    with torch.cuda.device(device):
+        t = torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+
+
 class PeerReduction:
     """Partial-sum exchange of one tensor-parallel group over NVLink peer memory.
 
@@ -106,9 +129,21 @@ class PeerReduction:
     reductions later, after its own LayerNorm waited for the peers' epoch of
     the reduction in between, which each peer publishes only after its
     LayerNorm finished reading buffer k.
+
+    ``scatter`` (the default for groups of three or more) reduces each rank's
+    slice of the rows only and gathers the normalised rows: every rank also
+    owns a bf16 and an fp32 [rows, cols] gather buffer that all ranks write
+    their slices into, a second flag array ("slice landed", published by the
+    last CTA of the slice's LayerNorm) and a CTA counter.  A rank's gather
+    buffer is written by a peer only after that peer waited for this rank's
+    partial epoch of the same reduction, published after every earlier read
+    of the buffer here; so it too needs no acknowledgement.  The residual
+    stream then stays sharded by rows: each rank keeps its slice only.
     """
 
-    def __init__(self, group: object, rows: int, cols: int, device: torch.device) -> None:
+    def __init__(
+        self, group: object, rows: int, cols: int, device: torch.device, *, scatter: bool | None = None
+    ) -> None:
         import torch.distributed as dist
 
         from .. import _native
@@ -120,16 +155,21 @@ class PeerReduction:
         if self.world > 8:
             raise ValueError("the peer reduction is built for groups of up to 8 ranks")
         self.rows, self.cols, self.device = rows, cols, device
+        self.scatter = self.world >= 3 if scatter is None else bool(scatter)
+        if self.scatter and self.world < 2:
+            raise ValueError("the scattered reduction needs a group of two or more ranks")
+        # Flag block: [0, 32) partial epochs by peer, [32, 64) "slice landed"
+        # epochs by peer, [64, 68) this rank's CTA counter.
+        sizes = [rows * cols * 2, rows * cols * 2, 128]
+        if self.scatter:
+            sizes += [rows * cols * 2, rows * cols * 4]  # gather buffers: bf16 normed, fp32 final
         with torch.cuda.device(device):
-            own = [_native.peer_alloc(rows * cols * 2) for _ in range(2)]
-            flags = _native.peer_alloc(4 * 8)
-        self._own = [ptr for ptr, _ in own] + [flags[0]]
-        handles = [[h for _, h in own] + [flags[1]]]
+            own = [_native.peer_alloc(n) for n in sizes]
+        self._own = [ptr for ptr, _ in own]
         gathered: list[object] = [None] * self.world
-        dist.all_gather_object(gathered, handles[0], group=group)
+        dist.all_gather_object(gathered, [h for _, h in own], group=group)
         self._opened: list[int] = []
-        self.partials: list[list[int]] = [[0] * self.world for _ in range(2)]
-        peer_flags: list[int] = [0] * self.world
+        mapped: list[list[int]] = []
         with torch.cuda.device(device):
             for r, hs in enumerate(gathered):
                 if r == self.rank:
@@ -137,10 +177,18 @@ class PeerReduction:
                 else:
                     ptrs = [_native.peer_open(h) for h in hs]
                     self._opened += ptrs
-                self.partials[0][r], self.partials[1][r], peer_flags[r] = ptrs
-        self.flags = flags[0]
-        # This rank's slot in each peer's flag array (its own slot unused).
+                mapped.append(ptrs)
+        self.partials = [[m[0] for m in mapped], [m[1] for m in mapped]]
+        peer_flags = [m[2] for m in mapped]
+        self.flags = self._own[2]
+        self.done_flags = self.flags + 32
+        self.counter = self.flags + 64
+        self.counter_value = 0
+        # This rank's slot in each peer's flag arrays (its own slot unused).
         self.slots = [peer_flags[r] + 4 * self.rank for r in range(self.world) if r != self.rank]
+        self.done_slots = [0 if r == self.rank else peer_flags[r] + 32 + 4 * self.rank for r in range(self.world)]
+        self.gather_bf16 = [m[3] for m in mapped] if self.scatter else []
+        self.gather_f32 = [m[4] for m in mapped] if self.scatter else []
         self.epoch = 0
         self._buffer = 0
 
@@ -161,6 +209,44 @@ class PeerReduction:
         self._native.residual_layer_norm_peer(
             residual_in, self.partials[self._buffer], self.rank, self.flags, self.epoch, **kwargs
         )
+        self._buffer ^= 1
+
+    def slice_bounds(self, rows: int) -> tuple[int, int]:
+        """This rank's rows [start, stop) of a scattered reduction."""
+
+        return batch_shard_bounds(rows, self.rank, self.world)
+
+    def gather_tensor(self, rows: int, dtype: torch.dtype) -> torch.Tensor:
+        """This rank's gather buffer as a [rows, cols] tensor (bf16: the
+        normalised input of the next projections; fp32: the final output)."""
+
+        if not self.scatter:
+            raise RuntimeError("gather buffers exist in the scattered mode only")
+        if rows > self.rows:
+            raise ValueError(f"{rows} rows exceed the {self.rows} the peer buffers were sized for")
+        ptr = self._own[3] if dtype == torch.bfloat16 else self._own[4]
+        return _tensor_view(ptr, (rows, self.cols), dtype, self.device)
+
+    def reduce_layer_norm_scattered(
+        self, residual_in: torch.Tensor, residual_out: torch.Tensor | None, out_dtype: torch.dtype,
+        gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+    ) -> None:
+        """This rank's slice of residual_in + the partials, normalised into
+        every rank's gather buffer of `out_dtype`; then the stream waits until
+        every peer's slice has landed in this rank's buffer."""
+
+        rows = residual_in.numel() // residual_in.shape[-1]
+        start, stop = self.slice_bounds(rows)
+        outs = self.gather_bf16 if out_dtype == torch.bfloat16 else self.gather_f32
+        if stop > start:
+            self.counter_value = self._native.residual_layer_norm_peer_rs(
+                residual_in, self.partials[self._buffer], self.rank, self.flags, self.epoch, start, stop - start,
+                residual_out, outs, out_dtype, gamma, beta, eps, self.done_slots, self.counter, self.counter_value,
+            )
+        else:
+            # An empty slice still publishes its epoch, so the peers' waits end.
+            self._native.peer_signal([s for s in self.done_slots if s], self.epoch, self.device)
+        self._native.peer_wait(self.done_flags, self.world, self.rank, self.epoch, self.device)
         self._buffer ^= 1
 
     def close(self) -> None:
@@ -299,6 +385,7 @@ class TensorParallelTransformer:
         reduction: str = "nccl",
         liveness: StepLiveness | None = None,
         check_peer_errors: bool = True,
+        peer_scatter: bool | None = None,
     ) -> None:
         import torch.distributed as dist
 
@@ -309,6 +396,7 @@ class TensorParallelTransformer:
         if reduction not in ("nccl", "peer"):
             raise ValueError("reduction must be 'nccl' or 'peer'")
         self.reduction = reduction
+        self.peer_scatter = peer_scatter
         self.liveness = liveness
         self.check_peer_errors = check_peer_errors
         self._error_word: torch.Tensor | None = None
@@ -367,7 +455,7 @@ class TensorParallelTransformer:
         if self._peer is None or self._peer.rows < rows:
             if self._peer is not None:
                 self._peer.close()
-            self._peer = PeerReduction(self.group, rows, d_model, self.device)
+            self._peer = PeerReduction(self.group, rows, d_model, self.device, scatter=self.peer_scatter)
         return self._peer
 
     def close(self) -> None:
@@ -403,7 +491,14 @@ class TensorParallelTransformer:
                 raise ValueError("the peer reduction reads the fp32 input as the first residual")
             peer = self._peer_reduction(rows, d_model)
         residual = torch.empty((rows, d_model), dtype=torch.float32, device=x.device)
-        normed = torch.empty((rows, d_model), dtype=torch.bfloat16, device=x.device)
+        scattered = peer is not None and peer.scatter
+        # Scattered: the normalised rows are gathered into this rank's peer
+        # buffer, which the next projections read in place.
+        normed = (
+            peer.gather_tensor(rows, torch.bfloat16)
+            if scattered
+            else torch.empty((rows, d_model), dtype=torch.bfloat16, device=x.device)
+        )
         qkv = torch.empty((batch, seq, 3 * d_local), dtype=torch.bfloat16, device=x.device)
         context = torch.empty((batch, seq, d_local), dtype=torch.bfloat16, device=x.device)
         hidden = torch.empty((rows, f_local), dtype=torch.bfloat16, device=x.device)
@@ -437,6 +532,14 @@ class TensorParallelTransformer:
                 raise RuntimeError("sm100 linear is ineligible for the requested operands")
             _native.linear(a, w, b, peer.partial(rows), _native.EPI_BIAS, _native.GEMM_PAIR)
             peer.signal()
+            if scattered:
+                # This rank's slice of the rows; residual stays sharded by rows.
+                peer.reduce_layer_norm_scattered(
+                    residual_in, None if last else residual, out_dtype, norm.weight, norm.bias, norm.eps
+                )
+                if last:
+                    normalized_out.copy_(peer.gather_tensor(rows, out_dtype))
+                return
             peer.reduce_layer_norm(
                 residual_in, residual_out=residual, normed=normalized_out,
                 gamma=norm.weight, beta=norm.bias, eps=norm.eps,

@@ -168,8 +168,9 @@ def _nccl_worker(
         tp = TensorParallelTransformer(
             model,
             partial_dtype=torch.bfloat16 if partials == "bf16" else torch.float32,
-            reduction=reduction,
+            reduction="peer" if reduction.startswith("peer") else reduction,
             liveness=live,
+            peer_scatter=True if reduction == "peer_scatter" else None,
         )
         x = official_input(cfg, 5).to(f"cuda:{rank}")
         y_tp = tp(x)
@@ -191,18 +192,29 @@ def _nccl_worker(
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize(("partials", "reduction"), [("fp32", "nccl"), ("bf16", "nccl"), ("bf16", "peer")])
-def test_tensor_parallel_matches_single_gpu(partials: str, reduction: str) -> None:
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+@pytest.mark.parametrize(
+    ("partials", "reduction", "world"),
+    [
+        ("fp32", "nccl", 2),
+        ("bf16", "nccl", 2),
+        ("bf16", "peer", 2),
+        # the reduce-scatter + gather form: forced on two ranks, the default on four
+        ("bf16", "peer_scatter", 2),
+        ("bf16", "peer", 4),
+        ("bf16", "nccl", 4),
+    ],
+)
+def test_tensor_parallel_matches_single_gpu(partials: str, reduction: str, world: int) -> None:
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as tmp:
         mp.start_processes(
             _nccl_worker, args=(world, _free_port(), tmp, partials, reduction), nprocs=world, start_method="spawn"
         )
         tp = [np.load(os.path.join(tmp, f"tp{r}.npy")) for r in range(world)]
         single = np.load(os.path.join(tmp, "single0.npy"))
-    np.testing.assert_array_equal(tp[0], tp[1])
+    for r in range(1, world):
+        np.testing.assert_array_equal(tp[0], tp[r])
     diff = tp[0].astype(np.float64) - single
     assert np.abs(diff).max() < 2e-2
     assert np.linalg.norm(diff) / np.linalg.norm(single) < 5e-3
