@@ -977,8 +977,9 @@ def official_schedules(cfg, eager: bool = False) -> list[tuple[str, object]]:  #
     ``graph_warp_gemm`` (every projection on the small-problem GEMM) and, for
     d_model 32/64/128, ``graph_fused_{linear,mlp}[_warp_gemm]`` (the fused
     block boundaries, optionally with the remaining projections on the
-    small-problem GEMM).  ``eager`` runs the same programs under the eager
-    runtime (one launch per kernel, for ncu launch lists)."""
+    small-problem GEMM), and, where it is built, ``sequence_resident`` (the
+    whole forward in one kernel).  ``eager`` runs the other programs under the
+    eager runtime (one launch per kernel, for ncu launch lists)."""
 
     import dataclasses
 
@@ -1013,6 +1014,17 @@ def official_schedules(cfg, eager: bool = False) -> list[tuple[str, object]]:  #
             rest = {"qkv_launch": warp, **({"ffn_input_launch": warp} if fusion == "linear" else {})}
             out.append((f"graph_fused_{fusion}_warp_gemm",
                         ConfigSpec(program=program, schedule=dataclasses.replace(fused, **rest))))
+    from solution.runtimes.sequence_resident import sequence_resident_supported
+
+    if not eager and sequence_resident_supported(
+        d_model=cfg.d_model, ffn_dim=cfg.ffn_dim, num_heads=cfg.num_heads, seq_len=cfg.seq_len,
+        num_layers=cfg.num_layers, causal=bool(cfg.causal),
+    ) is None:
+        # The whole forward in one kernel (csrc/seq_forward_kernels.cuh).
+        out.append(("sequence_resident", ConfigSpec(
+            program=default_program(attention=attention),
+            schedule=default_schedule(RuntimeBackend.SEQUENCE_RESIDENT, attention=attention),
+        )))
     return out
 
 
@@ -1148,7 +1160,7 @@ def main() -> None:
                         help="--workload official: comma-separated case ids (default: all 14)")
     parser.add_argument("--schedule", default=None,
                         help="--workload official: time only this schedule (default, graph, graph_warp_gemm, "
-                             "graph_fused_linear, graph_fused_mlp, ..._warp_gemm)")
+                             "graph_fused_linear, graph_fused_mlp, ..._warp_gemm, sequence_resident)")
     parser.add_argument("--eager-runtime", action="store_true",
                         help="--workload official: run the named schedules under the eager runtime "
                              "(one launch per kernel, for ncu launch lists)")

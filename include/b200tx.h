@@ -263,6 +263,40 @@ int b200tx_mlp_residual_layer_norm(const void* x, const void* w1, const float* b
                                    cudaStream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The whole forward of a small model in one launch (d_model = ffn_dim = 128,
+ * 1, 2 or 4 heads, sequences of 32, 64 or 128 tokens, 1-8 layers): one CTA per
+ * 128 rows (whole sequences) runs every layer on chip -- tcgen05 UMMAs with the
+ * residual and the accumulators in TMEM, weights streamed by bulk copies from
+ * pre-swizzled images.  Replaces, for the reference's small official shapes
+ * (official/test_shapes.json), the per-primitive forward of
+ * solution/transformer.py:1346-1513; no padding mask.
+ * ------------------------------------------------------------------------ */
+
+/* One [128, 128] BF16 row-major weight (a Linear's [out, in]) into its 32 KB
+ * operand image (16-byte aligned).  A layer's images are six consecutive
+ * images: Wq, Wk, Wv (the rows of the packed QKV weight), Wo, W1, W2. */
+int b200tx_seq_weight_image(const void* weight, void* image, cudaStream_t stream);
+
+typedef struct b200tx_seq_layer {
+  const void* weight_images;  /* 6 x 32 KB images (b200tx_seq_weight_image) */
+  const float* b_qkv;         /* [384] q, k, v biases */
+  const float* b_o;           /* [128] */
+  const float* b_1;           /* [128] */
+  const float* b_2;           /* [128] */
+  const float* ln2_gamma;     /* norm2 of this layer */
+  const float* ln2_beta;
+  const float* next_gamma;    /* norm1 of the next layer, or the final norm */
+  const float* next_beta;
+} b200tx_seq_layer;
+
+/* out = forward(x), x and out F32 [batch, seq, 128]; ln0 = norm1 of layer 0.
+ * Every pointer 16-byte aligned; causal attention; the unfused program's
+ * rounding points (bf16 projections, probabilities and updates). */
+int b200tx_sequence_forward(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model,
+                            int64_t heads, int64_t ffn_dim, int num_layers, const b200tx_seq_layer* layers,
+                            const float* ln0_gamma, const float* ln0_beta, float eps, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel reduction over NVLink peer memory.  The reference is
  * single-GPU; these entry points implement the head-sharded runtime's
  * reduction after the row-parallel projections (out-proj and FFN-out) without

@@ -44,6 +44,7 @@ from solution.config import (
     RuntimeBackend,
     Sm100AttentionParams,
     Sm100GemmParams,
+    default_attention,
     default_program,
     default_schedule,
     portable_config,
@@ -221,6 +222,8 @@ def _divisors(n: int, *, below: int | None = None) -> tuple[int, ...]:
 
 
 def _domains_for_structure(structure: StructureSpec, context: SearchContext) -> tuple[ParameterDomain, ...]:
+    if structure.runtime is RuntimeBackend.SEQUENCE_RESIDENT:
+        return ()  # one kernel for the whole forward: no per-primitive launch to tune
     domains = []
     if structure.attention is AttentionBackend.SM100_FLASH:
         domains.append(ParameterDomain("attention_tile", _ATTENTION_CHOICES, _DEFAULT_ATTENTION))
@@ -252,7 +255,26 @@ def _structure_specs(context: SearchContext) -> tuple[StructureSpec, ...]:
                     if runtime is RuntimeBackend.BATCH_TILED_CUDA_GRAPH and context.batch_size < 2:
                         continue
                     specs.append(StructureSpec(plan, runtime, attention, boundary))
+    ctx = context.execution_context
+    if context.scope == "resident" and _sequence_resident_eligible(ctx):
+        # The whole forward in one kernel: one structure, the program's
+        # primitives being the kernel's own.
+        head_dim = ctx.d_model // ctx.num_heads
+        specs.append(StructureSpec(PrecisionPlan.BF16_CORE, RuntimeBackend.SEQUENCE_RESIDENT,
+                                   default_attention(head_dim), None))
     return tuple(specs)
+
+
+def _sequence_resident_eligible(ctx: Any) -> bool:
+    from solution.runtimes.sequence_resident import sequence_resident_supported
+
+    try:
+        return sequence_resident_supported(
+            d_model=ctx.d_model, ffn_dim=ctx.ffn_dim, num_heads=ctx.num_heads, seq_len=ctx.seq_len,
+            num_layers=ctx.num_layers, causal=bool(ctx.causal),
+        ) is None and not ctx.has_valid_token_mask
+    except (AttributeError, TypeError, ZeroDivisionError):
+        return False
 
 
 @dataclass(frozen=True, slots=True)

@@ -27,6 +27,7 @@
 #include "gemm_rownorm_kernels.cuh"
 #include "gemm_warp_kernels.cuh"
 #include "norm_kernels.cuh"
+#include "seq_forward_kernels.cuh"
 #include "sm100_common.cuh"
 
 namespace {
@@ -68,6 +69,7 @@ struct DeviceState {
   bool attn_attr[2 * kAttnVariants] = {};  // unmasked builds by variant, then the masked builds
   bool rownorm_attr[4] = {};               // GEMM + residual LayerNorm builds by (in, out) dtype
   int rownorm_clusters[4][5] = {};         // their co-resident clusters by CTA pairs per cluster
+  bool seq_forward_attr = false;           // whole-forward kernel's shared-memory size set
 };
 
 std::mutex g_mutex;
@@ -951,6 +953,83 @@ int b200tx_peer_wait(const uint32_t* flags, int count, int self, uint32_t epoch,
   if (rc != B200TX_OK) return rc;
   cudaError_t err = launch(b200tx::peer_wait_kernel, dim3(1), dim3(32), 0, stream, flags, count, self, epoch);
   if (err != cudaSuccess) return cuda_fail(err, "peer_wait launch");
+  return B200TX_OK;
+}
+
+int b200tx_seq_weight_image(const void* weight, void* image, cudaStream_t stream) {
+  if (weight == nullptr || image == nullptr || !aligned16(weight) || !aligned16(image))
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "seq_weight_image: null or misaligned pointer");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  cudaError_t err = launch(b200tx::seq_weight_image_kernel, dim3(b200tx::kSfRows * (b200tx::kSfD / 8) / 256),
+                           dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(weight),
+                           static_cast<uint8_t*>(image));
+  if (err != cudaSuccess) return cuda_fail(err, "seq_weight_image launch");
+  return B200TX_OK;
+}
+
+int b200tx_sequence_forward(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model,
+                            int64_t heads, int64_t ffn_dim, int num_layers, const b200tx_seq_layer* layers,
+                            const float* ln0_gamma, const float* ln0_beta, float eps, cudaStream_t stream) {
+  if (x == nullptr || out == nullptr || layers == nullptr || ln0_gamma == nullptr || ln0_beta == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward: null pointer");
+  if (d_model != b200tx::kSfD || ffn_dim != b200tx::kSfD)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward: d_model %lld ffn_dim %lld (built: 128, 128)",
+                (long long)d_model, (long long)ffn_dim);
+  if (heads != 1 && heads != 2 && heads != 4)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward: %lld heads (built: 1, 2, 4)", (long long)heads);
+  if (seq != 32 && seq != 64 && seq != 128)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward: seq_len %lld (built: 32, 64, 128)", (long long)seq);
+  if (num_layers < 1 || num_layers > b200tx::kSfMaxLayers)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward: %d layers (1..%d)", num_layers, b200tx::kSfMaxLayers);
+  if (batch <= 0 || batch * seq > 0x7fffffffLL)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward: batch %lld", (long long)batch);
+  bool ok = aligned16(x) && aligned16(out) && aligned16(ln0_gamma) && aligned16(ln0_beta);
+  b200tx::SeqForwardArgs a = {};
+  for (int l = 0; l < num_layers; ++l) {
+    const b200tx_seq_layer& s = layers[l];
+    const void* ptrs[] = {s.weight_images, s.b_qkv, s.b_o, s.b_1, s.b_2, s.ln2_gamma, s.ln2_beta, s.next_gamma,
+                          s.next_beta};
+    for (const void* q : ptrs) ok = ok && q != nullptr && aligned16(q);
+    a.layers[l].w_img = static_cast<const uint8_t*>(s.weight_images);
+    a.layers[l].b_qkv = s.b_qkv;
+    a.layers[l].b_o = s.b_o;
+    a.layers[l].b_1 = s.b_1;
+    a.layers[l].b_2 = s.b_2;
+    a.layers[l].ln2_g = s.ln2_gamma;
+    a.layers[l].ln2_b = s.ln2_beta;
+    a.layers[l].next_g = s.next_gamma;
+    a.layers[l].next_b = s.next_beta;
+  }
+  if (!ok) return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward: null or misaligned operand");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  a.x = x;
+  a.out = out;
+  a.ln0_g = ln0_gamma;
+  a.ln0_b = ln0_beta;
+  a.num_layers = num_layers;
+  a.rows = static_cast<int>(batch * seq);
+  a.seq = static_cast<int>(seq);
+  a.heads = static_cast<int>(heads);
+  a.num_tiles = (a.rows + b200tx::kSfRows - 1) / b200tx::kSfRows;
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(b200tx::kSfD / heads));
+  a.eps = eps;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!dev->seq_forward_attr) {
+      cudaError_t err = cudaFuncSetAttribute(b200tx::seq_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(b200tx::kSfSmemBytes));
+      if (err != cudaSuccess) return cuda_fail(err, "sequence_forward: cudaFuncSetAttribute");
+      dev->seq_forward_attr = true;
+    }
+  }
+  const int ctas = a.num_tiles < dev->sm_count ? a.num_tiles : dev->sm_count;
+  cudaError_t err = launch(b200tx::seq_forward_kernel, dim3(static_cast<unsigned>(ctas)), dim3(b200tx::kSfThreads),
+                           b200tx::kSfSmemBytes, stream, a);
+  if (err != cudaSuccess) return cuda_fail(err, "sequence_forward launch");
   return B200TX_OK;
 }
 

@@ -30,6 +30,7 @@ enum DeviceErrorCode : unsigned int {
   kErrAttnMmaWait = 0x202,
   kErrAttnSoftmaxWait = 0x203,
   kErrPeerWait = 0x301,  // a tensor-parallel peer did not publish its partial in time
+  kErrSeqWait = 0x401,   // the whole-forward kernel's copy or UMMA did not complete in time
 };
 
 // A single wait gives up after this many nanoseconds.  Every event waited on

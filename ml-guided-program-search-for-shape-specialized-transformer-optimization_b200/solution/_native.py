@@ -231,6 +231,24 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_float,  # eps
         _c_void_p,  # stream
     ]
+    lib.b200tx_seq_weight_image.restype = ctypes.c_int
+    lib.b200tx_seq_weight_image.argtypes = [_c_void_p, _c_void_p, _c_void_p]
+    lib.b200tx_sequence_forward.restype = ctypes.c_int
+    lib.b200tx_sequence_forward.argtypes = [
+        _c_void_p,  # x
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # d_model
+        _c_int64,  # heads
+        _c_int64,  # ffn_dim
+        ctypes.c_int,  # num_layers
+        ctypes.POINTER(SeqLayer),  # layers
+        _c_void_p,  # ln0 gamma
+        _c_void_p,  # ln0 beta
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
     lib.b200tx_peer_wait.restype = ctypes.c_int
     lib.b200tx_peer_wait.argtypes = [_c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _c_void_p]
     lib.b200tx_attention_generic.restype = ctypes.c_int
@@ -776,6 +794,54 @@ def residual_layer_norm_peer_rs(
     return int(after.value)
 
 
+class SeqLayer(ctypes.Structure):
+    """b200tx_seq_layer: device pointers of one layer of the whole-forward kernel."""
+
+    _fields_ = [
+        ("weight_images", ctypes.c_void_p),
+        ("b_qkv", ctypes.c_void_p),
+        ("b_o", ctypes.c_void_p),
+        ("b_1", ctypes.c_void_p),
+        ("b_2", ctypes.c_void_p),
+        ("ln2_gamma", ctypes.c_void_p),
+        ("ln2_beta", ctypes.c_void_p),
+        ("next_gamma", ctypes.c_void_p),
+        ("next_beta", ctypes.c_void_p),
+    ]
+
+
+SEQ_IMAGE_BYTES = 128 * 128 * 2
+
+
+def seq_weight_image(weight: torch.Tensor, image: torch.Tensor) -> None:
+    """Launch b200tx_seq_weight_image: a [128, 128] bf16 weight into its 32 KB operand image."""
+
+    _check(load().b200tx_seq_weight_image(weight.data_ptr(), image.data_ptr(), _stream(weight.device)),
+           "b200tx_seq_weight_image")
+
+
+def sequence_forward(
+    x: torch.Tensor,
+    out: torch.Tensor,
+    heads: int,
+    layers: list[SeqLayer],
+    ln0_gamma: torch.Tensor,
+    ln0_beta: torch.Tensor,
+    eps: float,
+) -> None:
+    """Launch b200tx_sequence_forward: the whole forward of x [B, S, 128] into out."""
+
+    batch, seq, d_model = x.shape
+    arr = (SeqLayer * len(layers))(*layers)
+    _check(
+        load().b200tx_sequence_forward(
+            x.data_ptr(), out.data_ptr(), batch, seq, d_model, int(heads), d_model, len(layers), arr,
+            ln0_gamma.data_ptr(), ln0_beta.data_ptr(), float(eps), _stream(x.device),
+        ),
+        "b200tx_sequence_forward",
+    )
+
+
 def peer_wait(flags: int, count: int, self_index: int, epoch: int, device: torch.device) -> None:
     """Launch b200tx_peer_wait: hold the stream until every peer's flag reaches `epoch`."""
 
@@ -792,6 +858,10 @@ __all__ = [
     "peer_signal",
     "peer_wait",
     "residual_layer_norm_peer",
+    "SEQ_IMAGE_BYTES",
+    "SeqLayer",
+    "seq_weight_image",
+    "sequence_forward",
     "residual_layer_norm_peer_rs",
     "ABI_VERSION",
     "ATTN_DUO",

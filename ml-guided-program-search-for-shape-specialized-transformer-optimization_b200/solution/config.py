@@ -108,6 +108,9 @@ class RuntimeBackend(StrEnum):
     CUDA_GRAPH = "cuda_graph"
     BATCH_TILED_CUDA_GRAPH = "batch_tiled_cuda_graph"
     STREAMED = "streamed"
+    # The whole forward in one kernel (solution/runtimes/sequence_resident.py):
+    # d_model = ffn_dim = 128, 1-4 heads, sequences of 32-128 tokens, no mask.
+    SEQUENCE_RESIDENT = "sm100_sequence_resident"
 
 
 class AttentionOutputLayout(StrEnum):

@@ -219,6 +219,10 @@ class ExecutionPlan:
     def use_streamed_execution(self) -> bool:
         return self.runtime_backend is RuntimeBackend.STREAMED
 
+    @property
+    def use_sequence_resident(self) -> bool:
+        return self.runtime_backend is RuntimeBackend.SEQUENCE_RESIDENT
+
     def describe(self) -> dict[str, Any]:
         """Serialise the plan and its derived evidence (reference plan.py:266-341)."""
 

@@ -275,6 +275,24 @@ class PlanBuilder:
             from .shape14.planning import validate_streamed_runtime
 
             return validate_streamed_runtime(config, context, reject)
+        if runtime is RuntimeBackend.SEQUENCE_RESIDENT:
+            from .runtimes.sequence_resident import sequence_resident_supported
+
+            why = sequence_resident_supported(
+                d_model=context.d_model,
+                ffn_dim=context.ffn_dim if context.ffn_dim is not None else -1,
+                num_heads=context.num_heads,
+                seq_len=context.seq_len,
+                num_layers=context.num_layers if context.num_layers is not None else 0,
+                causal=bool(context.causal),
+            )
+            if why is not None:
+                reject("unsupported_shape", "schedule.runtime", f"the whole-forward kernel is {why}")
+            if context.has_valid_token_mask:
+                reject("mask_not_supported", "schedule.runtime", "the whole-forward kernel takes no padding mask")
+            if context.dtype != torch.float32:
+                reject("unsupported_dtype", "schedule.runtime", "the whole-forward kernel takes float32 input")
+            return context
         raise AssertionError(f"unhandled runtime backend: {runtime}")
 
     @staticmethod

@@ -285,6 +285,7 @@ class UserOptimizedTransformer(nn.Module):
 
         self._cuda_graph_replay: CudaGraphReplay | None = None
         self._batch_tiled_graph_replay: BatchTiledGraphReplay | None = None
+        self._sequence_resident: Any = None  # SequenceResidentForward, built on first use
         self._runtime_plan_signature: tuple[object, ...] | None = None
         self._runtime_plan: ExecutionPlan | None = None
         self._execution_observation_enabled = False
@@ -307,6 +308,7 @@ class UserOptimizedTransformer(nn.Module):
     def _invalidate_runtime_state(self) -> None:
         self._cuda_graph_replay = None
         self._batch_tiled_graph_replay = None
+        self._sequence_resident = None
         self._runtime_plan_signature = None
         self._runtime_plan = None
         self._last_execution_observation = None
@@ -334,9 +336,11 @@ class UserOptimizedTransformer(nn.Module):
                 module.clear_bf16_shadow()
             elif isinstance(module, _Fp32LayerNorm):
                 module.clear_shadow()
-        # Captured graphs hold pointers to the old shadows.
+        # Captured graphs hold pointers to the old shadows; the whole-forward
+        # runtime holds copies of the old weights.
         self._cuda_graph_replay = None
         self._batch_tiled_graph_replay = None
+        self._sequence_resident = None
 
     # ------------------------------------------------------------ config
     def _resolve_default_config(self, value: torch.Tensor | None = None) -> None:
@@ -905,6 +909,21 @@ class UserOptimizedTransformer(nn.Module):
             return self._forward_eager(value, mask, plan, out=out, defer_final=defer_final)
 
         with torch.inference_mode():
+            if plan.use_sequence_resident:
+                # The whole forward in one kernel; its weight images are built
+                # on first use (and again after any weight load or device move).
+                from .runtimes.sequence_resident import SequenceResidentForward
+
+                if self._sequence_resident is None or self._sequence_resident.device != x.device:
+                    self._sequence_resident = SequenceResidentForward(self)
+                output = self._sequence_resident(x)
+                if self._execution_observation_enabled:
+                    self._last_execution_observation = {
+                        "runtime_backend": RuntimeBackend.SEQUENCE_RESIDENT.value,
+                        "kernel": "sm100_sequence_forward",
+                        "runtime_calls": 1,
+                    }
+                return output
             if plan.use_streamed_execution:
                 from .shape14.executor import execute_streamed
 

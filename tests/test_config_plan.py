@@ -335,3 +335,40 @@ def test_official_bench_schedules_are_accepted_for_every_official_shape() -> Non
             for name, config in bench.official_schedules(cfg, eager):
                 result = PlanBuilder().evaluate(config, context, B200)
                 assert result.accepted, (case, name, [v.message for v in result.violations])
+
+
+# ---------------------------------------------------------------- whole-forward runtime
+def _sequence_resident() -> ConfigSpec:
+    from solution.config import AttentionBackend, RuntimeBackend
+
+    mma = AttentionBackend.SM100_MMA
+    return ConfigSpec(
+        program=default_program(attention=mma), schedule=default_schedule(RuntimeBackend.SEQUENCE_RESIDENT, attention=mma)
+    )
+
+
+def test_sequence_resident_runtime_accepts_the_small_official_shapes() -> None:
+    config = _sequence_resident()
+    assert ConfigSpec.from_dict(json.loads(config.canonical_json())) == config
+    for heads, seq in ((4, 128), (1, 128), (2, 128), (4, 32), (4, 64)):
+        context = _context(d_model=128, num_heads=heads, ffn_dim=128, seq_len=seq, batch_size=64, num_layers=4)
+        result = PlanBuilder().evaluate(config, context, B200)
+        assert result.accepted, (heads, seq, _codes(result))
+        assert result.plan.use_sequence_resident
+
+
+def test_sequence_resident_runtime_rejects_what_the_kernel_does_not_build() -> None:
+    config = _sequence_resident()
+    base = dict(d_model=128, num_heads=4, ffn_dim=128, seq_len=128, batch_size=64, num_layers=4)
+    cases = [
+        (dict(d_model=256, num_heads=4, ffn_dim=1024), "unsupported_shape"),
+        (dict(num_heads=16), "unsupported_shape"),
+        (dict(seq_len=1024), "unsupported_shape"),
+        (dict(num_layers=9), "unsupported_shape"),
+        (dict(has_valid_token_mask=True), "mask_not_supported"),
+        (dict(dtype=torch.bfloat16), "unsupported_dtype"),
+    ]
+    for overrides, code in cases:
+        result = PlanBuilder().evaluate(config, _context(**{**base, **overrides}), B200)
+        assert not result.accepted and code in _codes(result), (overrides, _codes(result))
+        assert "schedule.runtime" in {v.field for v in result.violations}

@@ -210,3 +210,16 @@ def test_small_d_model_searches_the_fused_boundaries() -> None:
         assert ("ffn_input_tile" in branch.parameter_names) == (branch.structure.boundary == "linear")
     # d_model 256 builds no fused boundary
     assert {b.structure.boundary for b in _space(max_branches=64).branches} == {None}
+
+
+def test_small_official_shapes_search_the_whole_forward_kernel() -> None:
+    space = _space(d_model=128, num_heads=4, ffn_dim=128, seq_len=128, batch_size=64, num_layers=4, max_branches=256)
+    whole = [b for b in space.branches if b.structure.runtime is RuntimeBackend.SEQUENCE_RESIDENT]
+    assert len(whole) == 1
+    branch = whole[0]
+    assert branch.parameter_names == ()  # one kernel: nothing per launch to tune
+    config = branch.default_config()
+    assert space.accepted(config)
+    assert space.branch_for(config) is branch
+    # d_model 256 (the default context here) builds no whole-forward branch
+    assert RuntimeBackend.SEQUENCE_RESIDENT not in {b.structure.runtime for b in _space(max_branches=256).branches}
