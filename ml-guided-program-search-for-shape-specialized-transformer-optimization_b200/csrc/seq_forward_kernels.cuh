@@ -502,12 +502,12 @@ __global__ void __launch_bounds__(kSfThreads, 1) seq_forward_kernel(const __grid
       if (!wait_on(&tbar[0], tph[0])) { failed = true; break; }
       load_w(0, L.w_img + 2 * kSfMatBytes);  // Wv
       sf_epilogue_proj(tT1, L.b_qkv, img_q, rw);
+      // --- V projection (A still holds n), running under K's epilogue
+      if (!wait_w(0)) { failed = true; break; }
+      issue(dT3, img_a, img_w[0], 0, 128, 0, kSfD, &tbar[2]);
       if (!wait_on(&tbar[1], tph[1])) { failed = true; break; }
       load_w(1, L.w_img + 3 * kSfMatBytes);  // Wo
       sf_epilogue_proj(tT2, L.b_qkv + kSfD, img_k, rw);
-      // --- V projection (A still holds n)
-      if (!wait_w(0)) { failed = true; break; }
-      issue(dT3, img_a, img_w[0], 0, 128, 0, kSfD, &tbar[2]);
       if (!wait_on(&tbar[2], tph[2])) { failed = true; break; }
       sf_epilogue_vt(tT3, L.b_qkv + 2 * kSfD, img_vt, rw);
       operands_ready();

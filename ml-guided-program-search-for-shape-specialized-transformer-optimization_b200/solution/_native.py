@@ -824,18 +824,18 @@ def sequence_forward(
     x: torch.Tensor,
     out: torch.Tensor,
     heads: int,
-    layers: list[SeqLayer],
+    layers: ctypes.Array,
     ln0_gamma: torch.Tensor,
     ln0_beta: torch.Tensor,
     eps: float,
 ) -> None:
-    """Launch b200tx_sequence_forward: the whole forward of x [B, S, 128] into out."""
+    """Launch b200tx_sequence_forward: the whole forward of x [B, S, 128] into
+    out; `layers` a ctypes array of SeqLayer (built once by the caller)."""
 
     batch, seq, d_model = x.shape
-    arr = (SeqLayer * len(layers))(*layers)
     _check(
         load().b200tx_sequence_forward(
-            x.data_ptr(), out.data_ptr(), batch, seq, d_model, int(heads), d_model, len(layers), arr,
+            x.data_ptr(), out.data_ptr(), batch, seq, d_model, int(heads), d_model, len(layers), layers,
             ln0_gamma.data_ptr(), ln0_beta.data_ptr(), float(eps), _stream(x.device),
         ),
         "b200tx_sequence_forward",

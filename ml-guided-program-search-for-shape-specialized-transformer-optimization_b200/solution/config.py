@@ -14,9 +14,10 @@ documents are rejected rather than reinterpreted.
 
 from __future__ import annotations
 
+import functools
 import hashlib
 import json
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from enum import StrEnum
 from typing import Any, ClassVar
 
@@ -487,6 +488,11 @@ class ScheduleConfig:
         )
 
 
+@functools.lru_cache(maxsize=256)
+def _sha256_of(text: str) -> str:
+    return hashlib.sha256(text.encode("utf-8")).hexdigest()
+
+
 @dataclass(frozen=True, slots=True)
 class ConfigSpec:
     """Canonical program plus schedule (reference: solution/config.py:672-785)."""
@@ -494,6 +500,9 @@ class ConfigSpec:
     program: ProgramConfig
     schedule: ScheduleConfig
     schema_version: int = CONFIG_SCHEMA_VERSION
+    # The canonical JSON, computed once: the config is immutable, and the
+    # forward reads config_id on every call.
+    _canonical: str = field(default="", init=False, repr=False, compare=False)
 
     _FIELDS: ClassVar[frozenset[str]] = frozenset({"schema_version", "program", "schedule"})
 
@@ -540,13 +549,17 @@ class ConfigSpec:
         }
 
     def canonical_json(self) -> str:
-        return json.dumps(
-            self.to_dict(), ensure_ascii=True, allow_nan=False, sort_keys=True, separators=(",", ":")
-        )
+        if not self._canonical:
+            object.__setattr__(
+                self,
+                "_canonical",
+                json.dumps(self.to_dict(), ensure_ascii=True, allow_nan=False, sort_keys=True, separators=(",", ":")),
+            )
+        return self._canonical
 
     @property
     def sha256(self) -> str:
-        return hashlib.sha256(self.canonical_json().encode("utf-8")).hexdigest()
+        return _sha256_of(self.canonical_json())
 
     @property
     def config_id(self) -> str:

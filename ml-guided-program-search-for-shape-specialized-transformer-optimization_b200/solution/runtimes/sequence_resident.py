@@ -92,6 +92,7 @@ class SequenceResidentForward:
                     _native.SeqLayer(self.images[i].data_ptr(), *[p.data_ptr() for p in ptrs])
                 )
             self.eps = float(final.eps)
+            self._layer_array = (_native.SeqLayer * len(self.layers))(*self.layers)
             torch.cuda.current_stream(self.device).synchronize()
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -99,8 +100,8 @@ class SequenceResidentForward:
             raise ValueError("x must be a contiguous float32 [B, S, 128] tensor on the model's device")
         if out is None:
             out = torch.empty_like(x)
-        with torch.cuda.device(self.device):
-            _native.sequence_forward(x, out, self.heads, self.layers, self.ln0[0], self.ln0[1], self.eps)
+        # Launched on the current device's stream; _native checks that it is x's device.
+        _native.sequence_forward(x, out, self.heads, self._layer_array, self.ln0[0], self.ln0[1], self.eps)
         return out
 
 

@@ -286,6 +286,7 @@ class UserOptimizedTransformer(nn.Module):
         self._cuda_graph_replay: CudaGraphReplay | None = None
         self._batch_tiled_graph_replay: BatchTiledGraphReplay | None = None
         self._sequence_resident: Any = None  # SequenceResidentForward, built on first use
+        self._shadows_ready = False
         self._runtime_plan_signature: tuple[object, ...] | None = None
         self._runtime_plan: ExecutionPlan | None = None
         self._execution_observation_enabled = False
@@ -326,11 +327,16 @@ class UserOptimizedTransformer(nn.Module):
         return result
 
     def _materialize_shadow_weights(self) -> None:
+        # A no-op once done; a weight load, a device move or a clear resets it.
+        if self._shadows_ready:
+            return
         for module in self.modules():
             if isinstance(module, _Bf16ShadowLinear):
                 module.materialize_bf16_shadow()
+        self._shadows_ready = True
 
     def _clear_shadow_weights(self) -> None:
+        self._shadows_ready = False
         for module in self.modules():
             if isinstance(module, _Bf16ShadowLinear):
                 module.clear_bf16_shadow()
