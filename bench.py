@@ -454,7 +454,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         tp = _c4_tp(args, cfg.batch_size, world)
         group, _, _ = tensor_parallel_groups(tp)
         partials = torch.bfloat16 if args.tp_partials == "bf16" else torch.float32
-        reduction = args.tp_reduction if args.tp_reduction != "auto" else ("peer" if tp == 2 else "nccl")
+        reduction = args.tp_reduction if args.tp_reduction != "auto" else ("peer" if tp <= 4 else "nccl")
         # peer: the whole partials of every peer for groups of two, the
         # reduce-scatter + gather form for larger groups; peer-full and
         # peer-scatter force one of them.
@@ -1169,8 +1169,8 @@ def main() -> None:
     parser.add_argument("--tp-reduction", choices=("auto", "nccl", "peer", "peer-full", "peer-scatter"), default="auto",
                         help="c4: NCCL all-reduce, or the peer-memory reduction fused into the "
                              "LayerNorm: peer (whole partials for groups of 2, reduce-scatter + gather for "
-                             "larger groups), peer-full / peer-scatter (forced); auto: peer for groups of 2, "
-                             "NCCL otherwise")
+                             "larger groups), peer-full / peer-scatter (forced); auto: peer for groups of up "
+                             "to 4 (measured ahead of NCCL there), NCCL for 8")
     parser.add_argument("--tp-partials", choices=("fp32", "bf16"), default="bf16",
                         help="dtype of the partial sums all-reduced by the head-sharded runtime")
     parser.add_argument("--shape", default=None, help="B,S,H override for --kernel (head_dim 64, F=4D)")

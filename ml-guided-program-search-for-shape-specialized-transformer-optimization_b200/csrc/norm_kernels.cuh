@@ -401,12 +401,13 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
 // those rows and writes the normalised rows into every rank's output buffer
 // (`outs`, its own local, the others peer memory).  NVLink traffic per rank:
 // (P - 1)/P of the rows' partials in and as many normalised rows out, instead
-// of every peer's whole partial.  Each thread fences its stores at system scope
-// before its CTA counts itself done on a local counter; the CTA that completes
-// the launch's count publishes `epoch` into this rank's slot of every peer's
-// done flags (release, system scope).  peer_wait_kernel then holds the stream
-// until every peer's slice has landed here.  Rows are independent, so each
-// row is computed by one rank only and the ranks agree by construction.
+// of every peer's whole partial.  After a CTA barrier (which orders every
+// thread's stores before thread 0), thread 0 fences at system scope (a
+// cumulative fence) and counts the CTA done on a local counter; the CTA that
+// completes the launch's count publishes `epoch` into this rank's slot of every
+// peer's done flags (release, system scope).  peer_wait_kernel then holds the
+// stream until every peer's slice has landed here.  Rows are independent, so
+// each row is computed by one rank only and the ranks agree by construction.
 struct PeerGatherArgs {
   void* outs[kMaxPeers];            // [rows_total, cols] OutT of every rank, index = group rank
   uint32_t* done_slots[kMaxPeers];  // this rank's slot in each peer's done flags (null: none)
@@ -432,15 +433,23 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
     float4 v[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) v[i] = load4<float>(rin, base + (i * 32 + lane) * 4);
-    for (int r = 0; r < peers.count; ++r) {
+    // Partials added in rank order (the rank loop unrolled, so that the next
+    // rank's loads can be issued while this one's are added).
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r >= peers.count) break;
       const __nv_bfloat16* part = peers.partials[r];
+      uint2 raw[NV];
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         const int64_t idx = base + (i * 32 + lane) * 4;
-        const uint2 raw = r == peers.self ? __ldg(reinterpret_cast<const uint2*>(part + idx))
-                                          : __ldcg(reinterpret_cast<const uint2*>(part + idx));
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        raw[i] = r == peers.self ? __ldg(reinterpret_cast<const uint2*>(part + idx))
+                                 : __ldcg(reinterpret_cast<const uint2*>(part + idx));
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i].y));
         v[i].x += a.x;
         v[i].y += a.y;
         v[i].z += b.x;
@@ -479,10 +488,11 @@ __global__ void __launch_bounds__(kNormWarpsPerBlock * 32)
       }
     }
   }
-  // Every thread's stores are visible system-wide before its CTA counts itself.
-  __threadfence_system();
+  // The CTA's stores (every thread's, ordered before thread 0 by the barrier)
+  // are visible system-wide before the CTA counts itself.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const uint32_t done = atomicAdd(g.counter, 1u) + 1u;
     if (done == g.counter_target) {
       __threadfence_system();
