@@ -79,6 +79,28 @@ METRIC = "fwd tokens/s"
 UNIT = "tokens/s"
 WORKLOAD_NAME = "C2 resident mid shape: B8 S2048 D1024 H16(Dh64) F4096 L2 causal"
 L2_FLUSH_BYTES = 256 * 1024 * 1024
+L2_FLUSH_NOTE = "flushed before every timed step (256 MB written, then 256 MB of another buffer read)"
+
+
+class L2Flush:
+    """Evict the L2 between timed steps without leaving write-backs behind.
+
+    Writing a buffer larger than the L2 (126 MB) evicts the step's inputs, but
+    leaves the L2 full of dirty lines that the first kernel of the next step
+    would then write back to HBM inside its timed region (~100 MB for C2's
+    initial LayerNorm, which doubled its DRAM traffic).  Reading a second
+    buffer of the same size afterwards forces those write-backs here, untimed,
+    and leaves clean lines of an unrelated buffer.
+    """
+
+    def __init__(self, device: torch.device) -> None:
+        self._write = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+        self._read = torch.zeros(L2_FLUSH_BYTES // 8, dtype=torch.int64, device=device)
+
+    def __call__(self) -> None:
+        self._write.zero_()
+        self._sink = self._read.sum()
+
 
 
 def _env_int(name: str, default: int) -> int:
@@ -472,7 +494,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
     x_dev = (x_host if full else x_cpu).to(device)
     del x_cpu
     big_input = x_dev.numel() * x_dev.element_size() > 2 * L2_FLUSH_BYTES
-    flush = None if big_input else torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = None if big_input else L2Flush(device)
     torch.cuda.synchronize(device)
     torch.cuda.reset_peak_memory_stats(device)
 
@@ -498,7 +520,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         with ClockSampler(ctx.local_rank) as clocks:
             for i in range(steps):
                 if flush is not None:
-                    flush.zero_()
+                    flush()
                 starts[i].record()
                 runner(x_dev)
                 ends[i].record()
@@ -514,6 +536,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         # runtime replays its launches where the events cannot sit, so this
         # pass runs the same program under the eager runtime.
         kernel_ms: dict[str, list[float]] = {}
+        event_floor_us = None
         kernel_steps = steps if full else 1
         if runner is model:
             from dataclasses import replace as _replace
@@ -537,7 +560,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
             model.kernel_events = recorder
             for _ in range(kernel_steps):
                 if flush is not None:
-                    flush.zero_()
+                    flush()
                 runner(x_dev)
             torch.cuda.synchronize()
             model.kernel_events = None
@@ -545,6 +568,23 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
             if graph_config is not None:
                 model.configure_execution(config=graph_config)
                 model.active_config_source = graph_source
+            # The floor of that method: a one-element fill bracketed by the
+            # same two events after the same flush (event processing and the
+            # launch gap it adds to every kernel's figure).
+            tiny = torch.empty(1, device=device)
+            floor_ms = []
+            for _ in range(max(5, kernel_steps)):
+                if flush is not None:
+                    flush()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                tiny.zero_()
+                e1.record()
+                floor_ms.append((e0, e1))
+            torch.cuda.synchronize()
+            floor_ms = sorted(a.elapsed_time(b) for a, b in floor_ms)
+            event_floor_us = 1000.0 * floor_ms[len(floor_ms) // 2]
 
         e2e_ms = 0.0
         out_host = None
@@ -576,23 +616,30 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
             # The host link alone, all ranks at once: the step's input copied
             # H2D, then its output D2H, then both directions together (on two
             # streams), each timed by CUDA events -- the rates that bound e2e.
+            # "both": the two directions on two streams with no dependency
+            # between them, as the pipeline runs them.
             link = torch.empty_like(x_dev)
+            up = torch.cuda.Stream(device)
             down = torch.cuda.Stream(device)
             link_ms = {}
+            reps = 5
             for name in ("h2d", "d2h", "both"):
                 barrier()
                 t0 = torch.cuda.Event(enable_timing=True)
                 t1 = torch.cuda.Event(enable_timing=True)
                 t0.record()
-                reps = 5
+                up.wait_event(t0)
+                down.wait_event(t0)
                 for _ in range(reps):
                     if name in ("h2d", "both"):
-                        link.copy_(x_host, non_blocking=True)
+                        with torch.cuda.stream(up):
+                            link.copy_(x_host, non_blocking=True)
                     if name in ("d2h", "both"):
-                        down.wait_stream(torch.cuda.current_stream(device))
                         with torch.cuda.stream(down):
                             out_host.copy_(x_dev, non_blocking=True)
-                        torch.cuda.current_stream(device).wait_stream(down)
+                cur = torch.cuda.current_stream(device)
+                cur.wait_stream(up)
+                cur.wait_stream(down)
                 t1.record()
                 torch.cuda.synchronize(device)
                 link_ms[name] = t0.elapsed_time(t1) / reps
@@ -691,7 +738,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         "global_batch": cfg.batch_size * (world if scaling == "weak" else 1),
         "seq_len": cfg.seq_len,
         "parallelism": parallelism,
-        "l2": "inputs larger than L2" if big_input else "flushed (256 MB write) before every timed step",
+        "l2": "inputs larger than L2" if big_input else L2_FLUSH_NOTE,
         "program": _program(model, runner),
         "attention_tflops": attention_tflops,
         "attention_frac_of_burst": attention_tflops / float(peaks["bf16_tflops"]) if attention_tflops else None,
@@ -701,6 +748,7 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
         # rank-local extras for the headline line
         "_kernels": {role: {"ms_per_step": per_role[role], "launches_per_step": launches[role]}
                      for role in sorted(per_role)},
+        "_event_floor_us": event_floor_us,
         "_roofline": roofline,
         "_launches": int(sum(len(v) for v in kernel_ms.values())),
         "_e2e_ms": e2e_ms_max,
@@ -713,8 +761,10 @@ def measure_workload(ctx: _Context, name: str, steps: int, warmup: int, full: bo
                 "h2d_gbs_per_rank": x_host.numel() * x_host.element_size() / (h2d_ms / 1000.0) / 1e9,
                 "d2h_gbs_per_rank": x_host.numel() * x_host.element_size() / (d2h_ms / 1000.0) / 1e9,
                 "both_directions_ms": both_ms,
+                "both_directions_gbs_per_rank": 2 * x_host.numel() * x_host.element_size() / (both_ms / 1000.0) / 1e9,
                 "h2d_then_d2h_ms": h2d_ms + d2h_ms,
-                "timing": "CUDA events, slowest rank, 5 copies each, pinned host memory",
+                "timing": "CUDA events, slowest rank, 5 copies each, pinned host memory; 'both' runs "
+                          "the two directions on two independent streams",
             }
             if full and h2d_ms > 0
             else None
@@ -835,6 +885,7 @@ def run_gpu(args: argparse.Namespace) -> None:
             "model_tflops": main["model_tflops"],
             "peak_memory_gb_per_gpu": main["peak_memory_gb_per_gpu"],
             "kernels": main["_kernels"],
+            "kernel_event_floor_us": main["_event_floor_us"],
             "roofline": main["_roofline"],
             "e2e": {
                 "value": main["_total_tokens"] / (main["_e2e_ms"] / 1000.0),
@@ -940,14 +991,14 @@ def run_kernel(args: argparse.Namespace) -> None:
         work, unit, bound = 12.0 * m * d, "GB/s", "hbm"
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
     for _ in range(max(3, args.warmup)):
         launch()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
-        flush.zero_()
+        flush()
         starts[i].record()
         launch()
         ends[i].record()
@@ -1051,7 +1102,7 @@ def run_official(args: argparse.Namespace) -> None:
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     _native.device_check()
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
     cases = args.cases.split(",") if args.cases else sorted(OFFICIAL_SHAPES)
 
     def median_ms(model, x, warmup: int, steps: int) -> float:  # noqa: ANN001
@@ -1061,7 +1112,7 @@ def run_official(args: argparse.Namespace) -> None:
             torch.cuda.synchronize()
             times = []
             for _ in range(steps):
-                flush.zero_()
+                flush()
                 start = torch.cuda.Event(enable_timing=True)
                 end = torch.cuda.Event(enable_timing=True)
                 start.record()

@@ -147,15 +147,6 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32
                : "memory");
 }
 
-// Drain wait before a CTA leaves: for copies this CTA issued, whatever the
-// abort state, bounded by the same timeout.
-__device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
-  const unsigned long long start = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - start > kWaitTimeoutNs) return;
-  }
-}
-
 // Relaxed arrive on an mbarrier given by its cluster address: for a signal
 // whose data dependency the caller has already enforced (the TMEM reads of an
 // accumulator stage, completed by tcgen05.wait::ld), without a release that

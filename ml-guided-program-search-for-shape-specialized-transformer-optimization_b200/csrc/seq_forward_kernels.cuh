@@ -76,15 +76,6 @@ struct SeqForwardArgs {
   float eps;
 };
 
-// 1D bulk copy global -> this CTA's shared memory, counted on `bar`.
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Byte offset of element (row, col) of a [128 x 128] bf16 operand image:
 // panel col / 64, row pitch 128 bytes, 16-byte chunk (col % 64) / 8 swizzled
 // with row % 8.
@@ -127,14 +118,6 @@ __global__ void seq_weight_image_kernel(const __nv_bfloat16* w, uint8_t* image) 
   const int r = i / (kSfD / 8), j = i % (kSfD / 8);
   const uint4 v = *reinterpret_cast<const uint4*>(w + r * kSfD + j * 8);
   *reinterpret_cast<uint4*>(image + sf_offset(r, j * 8)) = v;
-}
-
-// Drain wait before the CTA leaves (bounded, whatever the abort state).
-__device__ __forceinline__ void mbar_drain_wait_sf(uint64_t* bar, uint32_t parity) {
-  const unsigned long long start = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - start > kWaitTimeoutNs) return;
-  }
 }
 
 // The per-row phases.  Thread (warp w, lane l) owns row 32 (w % 4) + l (its
@@ -571,12 +554,12 @@ __global__ void __launch_bounds__(kSfThreads, 1) seq_forward_kernel(const __grid
   if (tid == 0) {
     for (int s = 0; s < 2; ++s)
       for (; w_waited[s] < w_issued[s]; ++w_waited[s]) {
-        mbar_drain_wait_sf(&wbar[s], wph[s]);
+        mbar_drain_wait(&wbar[s], wph[s]);
         wph[s] ^= 1u;
       }
     if (mma_issued) {
       umma_commit(&drain_bar);
-      mbar_drain_wait_sf(&drain_bar, 0);
+      mbar_drain_wait(&drain_bar, 0);
     }
   }
   tc_fence_before();

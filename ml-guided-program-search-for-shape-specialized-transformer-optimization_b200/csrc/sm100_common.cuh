@@ -130,6 +130,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   return true;
 }
 
+// Drain wait before a CTA leaves: for copies this CTA issued, whatever the
+// abort state or the device error word, bounded by the same timeout.
+__device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
+  const unsigned long long start = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - start > kWaitTimeoutNs) return;
+  }
+}
+
 // Round a dynamic shared-memory pointer up to the 1024-byte alignment that
 // 128-byte-swizzled TMA tiles and UMMA descriptors (base offset 0) require.
 __device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
@@ -158,6 +167,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
                : "memory");
+}
+
+// 1D bulk copy global -> this CTA's shared memory, counted on `bar`.  Both
+// addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // Closes the issuing thread's outstanding bulk stores into one group (an
