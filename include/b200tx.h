@@ -297,6 +297,50 @@ int b200tx_sequence_forward(const float* x, float* out, int64_t batch, int64_t s
                             const float* ln0_gamma, const float* ln0_beta, float eps, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The same whole forward for callers that cannot allocate device memory.
+ * No counterpart in the reference.  b200tx_sequence_forward needs 192 KB of
+ * weight images per layer that the caller allocates and fills; some callers
+ * cannot: a process whose device memory is all handed out by its framework's
+ * own pool (a serving engine that reserves the GPU at start-up), or code that
+ * must not call cudaMalloc because it synchronizes the device.  This entry
+ * point takes the plain weights instead and builds the images, on the
+ * stream, in a fixed array that the library holds in device memory for up to
+ * B200TX_SEQ_NOALLOC_MAX_LAYERS layers (768 KB on every GPU that loads the
+ * library, until the process exits); more layers are rejected with
+ * B200TX_ERR_UNSUPPORTED.  It allocates nothing.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture.
+ * - Every call on a device shares the one array and rewrites the images of
+ *   the layers it runs before its forward reads them, so nothing in it needs
+ *   clearing.  Calls whose work overlaps on the GPU (different streams, or
+ *   host threads) race on it: serialize them.
+ * - Same shapes, results and pointer rules as b200tx_sequence_forward, with
+ *   each weight a BF16 row-major [out, in] matrix, 16-byte aligned.
+ * ------------------------------------------------------------------------ */
+#define B200TX_SEQ_NOALLOC_MAX_LAYERS 4
+
+typedef struct b200tx_seq_layer_weights {
+  const void* w_qkv;          /* [384, 128] BF16: the q, k and v weights stacked by rows */
+  const void* w_o;            /* [128, 128] BF16 out-projection */
+  const void* w_1;            /* [128, 128] BF16 FFN in */
+  const void* w_2;            /* [128, 128] BF16 FFN out */
+  const float* b_qkv;         /* [384] q, k, v biases */
+  const float* b_o;           /* [128] */
+  const float* b_1;           /* [128] */
+  const float* b_2;           /* [128] */
+  const float* ln2_gamma;     /* norm2 of this layer */
+  const float* ln2_beta;
+  const float* next_gamma;    /* norm1 of the next layer, or the final norm */
+  const float* next_beta;
+} b200tx_seq_layer_weights;
+
+int b200tx_sequence_forward_noalloc(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model,
+                                    int64_t heads, int64_t ffn_dim, int num_layers,
+                                    const b200tx_seq_layer_weights* layers, const float* ln0_gamma,
+                                    const float* ln0_beta, float eps, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel reduction over NVLink peer memory.  The reference is
  * single-GPU; these entry points implement the head-sharded runtime's
  * reduction after the row-parallel projections (out-proj and FFN-out) without

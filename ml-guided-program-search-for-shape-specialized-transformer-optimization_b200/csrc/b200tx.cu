@@ -30,6 +30,15 @@
 #include "seq_forward_kernels.cuh"
 #include "sm100_common.cuh"
 
+// Weight images of b200tx_sequence_forward_noalloc, the library's only fixed
+// scratch array: B200TX_SEQ_NOALLOC_MAX_LAYERS layers x 6 images x 32 KB =
+// 768 KB of global memory on every device that loads the library, held until
+// the process exits.  In host code this name is not a device address; the
+// entry point looks the address up once per device (cudaGetSymbolAddress).
+static __device__ __align__(256) uint8_t
+    g_seq_noalloc_images[static_cast<size_t>(B200TX_SEQ_NOALLOC_MAX_LAYERS) * b200tx::kSfWeightImages *
+                         b200tx::kSfMatBytes];
+
 namespace {
 
 constexpr int kAbiVersion = 2;
@@ -70,6 +79,7 @@ struct DeviceState {
   bool rownorm_attr[4] = {};               // GEMM + residual LayerNorm builds by (in, out) dtype
   int rownorm_clusters[4][5] = {};         // their co-resident clusters by CTA pairs per cluster
   bool seq_forward_attr = false;           // whole-forward kernel's shared-memory size set
+  uint8_t* seq_noalloc_images = nullptr;   // device address of g_seq_noalloc_images on this device
 };
 
 std::mutex g_mutex;
@@ -1030,6 +1040,102 @@ int b200tx_sequence_forward(const float* x, float* out, int64_t batch, int64_t s
   cudaError_t err = launch(b200tx::seq_forward_kernel, dim3(static_cast<unsigned>(ctas)), dim3(b200tx::kSfThreads),
                            b200tx::kSfSmemBytes, stream, a);
   if (err != cudaSuccess) return cuda_fail(err, "sequence_forward launch");
+  return B200TX_OK;
+}
+
+// The whole forward without any allocation: the weight images go into
+// g_seq_noalloc_images (rewritten by every call, on the stream, before its
+// forward reads them) instead of caller-allocated memory.
+int b200tx_sequence_forward_noalloc(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model,
+                                    int64_t heads, int64_t ffn_dim, int num_layers,
+                                    const b200tx_seq_layer_weights* layers, const float* ln0_gamma,
+                                    const float* ln0_beta, float eps, cudaStream_t stream) {
+  if (x == nullptr || out == nullptr || layers == nullptr || ln0_gamma == nullptr || ln0_beta == nullptr)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward_noalloc: null pointer");
+  if (d_model != b200tx::kSfD || ffn_dim != b200tx::kSfD)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward_noalloc: d_model %lld ffn_dim %lld (built: 128, 128)",
+                (long long)d_model, (long long)ffn_dim);
+  if (heads != 1 && heads != 2 && heads != 4)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward_noalloc: %lld heads (built: 1, 2, 4)", (long long)heads);
+  if (seq != 32 && seq != 64 && seq != 128)
+    return fail(B200TX_ERR_UNSUPPORTED, "sequence_forward_noalloc: seq_len %lld (built: 32, 64, 128)",
+                (long long)seq);
+  if (num_layers < 1 || num_layers > B200TX_SEQ_NOALLOC_MAX_LAYERS)
+    return fail(B200TX_ERR_UNSUPPORTED,
+                "sequence_forward_noalloc: %d layers; its fixed image array holds 1..%d (%zu KB per device); "
+                "use b200tx_sequence_forward with caller-allocated images for more",
+                num_layers, B200TX_SEQ_NOALLOC_MAX_LAYERS, sizeof(g_seq_noalloc_images) / 1024);
+  if (batch <= 0 || batch * seq > 0x7fffffffLL)
+    return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward_noalloc: batch %lld", (long long)batch);
+  bool ok = aligned16(x) && aligned16(out) && aligned16(ln0_gamma) && aligned16(ln0_beta);
+  for (int l = 0; l < num_layers; ++l) {
+    const b200tx_seq_layer_weights& w = layers[l];
+    const void* ptrs[] = {w.w_qkv, w.w_o,       w.w_1,      w.w_2,        w.b_qkv,    w.b_o,
+                          w.b_1,   w.b_2,       w.ln2_gamma, w.ln2_beta, w.next_gamma, w.next_beta};
+    for (const void* q : ptrs) ok = ok && q != nullptr && aligned16(q);
+  }
+  if (!ok) return fail(B200TX_ERR_INVALID_ARGUMENT, "sequence_forward_noalloc: null or misaligned operand");
+  DeviceState* dev = nullptr;
+  int rc = current_device(&dev);
+  if (rc != B200TX_OK) return rc;
+  {
+    // Set-up, once per device, with that device current (current_device).
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (dev->seq_noalloc_images == nullptr) {
+      void* images = nullptr;
+      cudaError_t err = cudaGetSymbolAddress(&images, g_seq_noalloc_images);
+      if (err != cudaSuccess) return cuda_fail(err, "sequence_forward_noalloc: cudaGetSymbolAddress");
+      dev->seq_noalloc_images = static_cast<uint8_t*>(images);
+    }
+    if (!dev->seq_forward_attr) {
+      cudaError_t err = cudaFuncSetAttribute(b200tx::seq_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(b200tx::kSfSmemBytes));
+      if (err != cudaSuccess) return cuda_fail(err, "sequence_forward_noalloc: cudaFuncSetAttribute");
+      dev->seq_forward_attr = true;
+    }
+  }
+  uint8_t* const images = dev->seq_noalloc_images;
+  constexpr size_t kLayerBytes = static_cast<size_t>(b200tx::kSfWeightImages) * b200tx::kSfMatBytes;
+  b200tx::SeqImageSources src = {};
+  b200tx::SeqForwardArgs a = {};
+  for (int l = 0; l < num_layers; ++l) {
+    const b200tx_seq_layer_weights& w = layers[l];
+    const auto* qkv = static_cast<const __nv_bfloat16*>(w.w_qkv);
+    const __nv_bfloat16* mats[b200tx::kSfWeightImages] = {
+        qkv, qkv + b200tx::kSfD * b200tx::kSfD, qkv + 2 * b200tx::kSfD * b200tx::kSfD,
+        static_cast<const __nv_bfloat16*>(w.w_o), static_cast<const __nv_bfloat16*>(w.w_1),
+        static_cast<const __nv_bfloat16*>(w.w_2)};
+    for (int m = 0; m < b200tx::kSfWeightImages; ++m) src.w[l * b200tx::kSfWeightImages + m] = mats[m];
+    a.layers[l].w_img = images + l * kLayerBytes;
+    a.layers[l].b_qkv = w.b_qkv;
+    a.layers[l].b_o = w.b_o;
+    a.layers[l].b_1 = w.b_1;
+    a.layers[l].b_2 = w.b_2;
+    a.layers[l].ln2_g = w.ln2_gamma;
+    a.layers[l].ln2_b = w.ln2_beta;
+    a.layers[l].next_g = w.next_gamma;
+    a.layers[l].next_b = w.next_beta;
+  }
+  cudaError_t err = launch(b200tx::seq_weight_images_kernel,
+                           dim3(b200tx::kSfRows * (b200tx::kSfD / 8) / 256,
+                                static_cast<unsigned>(num_layers * b200tx::kSfWeightImages)),
+                           dim3(256), 0, stream, src, images);
+  if (err != cudaSuccess) return cuda_fail(err, "sequence_forward_noalloc: weight image launch");
+  a.x = x;
+  a.out = out;
+  a.ln0_g = ln0_gamma;
+  a.ln0_b = ln0_beta;
+  a.num_layers = num_layers;
+  a.rows = static_cast<int>(batch * seq);
+  a.seq = static_cast<int>(seq);
+  a.heads = static_cast<int>(heads);
+  a.num_tiles = (a.rows + b200tx::kSfRows - 1) / b200tx::kSfRows;
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(b200tx::kSfD / heads));
+  a.eps = eps;
+  const int ctas = a.num_tiles < dev->sm_count ? a.num_tiles : dev->sm_count;
+  err = launch(b200tx::seq_forward_kernel, dim3(static_cast<unsigned>(ctas)), dim3(b200tx::kSfThreads),
+               b200tx::kSfSmemBytes, stream, a);
+  if (err != cudaSuccess) return cuda_fail(err, "sequence_forward_noalloc: forward launch");
   return B200TX_OK;
 }
 

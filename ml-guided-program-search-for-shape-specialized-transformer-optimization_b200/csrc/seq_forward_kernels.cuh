@@ -120,6 +120,25 @@ __global__ void seq_weight_image_kernel(const __nv_bfloat16* w, uint8_t* image) 
   *reinterpret_cast<uint4*>(image + sf_offset(r, j * 8)) = v;
 }
 
+// Every weight image of a model in one launch (the allocation-free entry
+// point's images): block (x, y) moves 256 of the 2048 sixteen-byte chunks of
+// image y (layer y / 6, matrix y % 6) from its row-major source.  It waits for
+// the previous launch on the stream to complete before its first access, so
+// that it never rewrites images a previous forward is still reading.
+struct SeqImageSources {
+  const __nv_bfloat16* w[kSfMaxLayers * kSfWeightImages];
+};
+
+__global__ void seq_weight_images_kernel(const __grid_constant__ SeqImageSources src, uint8_t* images) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= kSfRows * (kSfD / 8)) return;
+  const int r = i / (kSfD / 8), j = i % (kSfD / 8);
+  const uint4 v = *reinterpret_cast<const uint4*>(src.w[blockIdx.y] + r * kSfD + j * 8);
+  *reinterpret_cast<uint4*>(images + static_cast<size_t>(blockIdx.y) * kSfMatBytes + sf_offset(r, j * 8)) = v;
+}
+
 // The per-row phases.  Thread (warp w, lane l) owns row 32 (w % 4) + l (its
 // TMEM lane) and the 32 columns [32 (w / 4), 32 (w / 4) + 32): one 32-column
 // TMEM load per phase.  Row reductions (LayerNorm statistics, softmax max and

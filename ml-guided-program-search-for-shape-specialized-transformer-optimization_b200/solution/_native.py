@@ -249,6 +249,22 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_float,  # eps
         _c_void_p,  # stream
     ]
+    lib.b200tx_sequence_forward_noalloc.restype = ctypes.c_int
+    lib.b200tx_sequence_forward_noalloc.argtypes = [
+        _c_void_p,  # x
+        _c_void_p,  # out
+        _c_int64,  # batch
+        _c_int64,  # seq
+        _c_int64,  # d_model
+        _c_int64,  # heads
+        _c_int64,  # ffn_dim
+        ctypes.c_int,  # num_layers
+        ctypes.POINTER(SeqLayerWeights),  # layers
+        _c_void_p,  # ln0 gamma
+        _c_void_p,  # ln0 beta
+        ctypes.c_float,  # eps
+        _c_void_p,  # stream
+    ]
     lib.b200tx_peer_wait.restype = ctypes.c_int
     lib.b200tx_peer_wait.argtypes = [_c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _c_void_p]
     lib.b200tx_attention_generic.restype = ctypes.c_int
@@ -810,7 +826,28 @@ class SeqLayer(ctypes.Structure):
     ]
 
 
+class SeqLayerWeights(ctypes.Structure):
+    """b200tx_seq_layer_weights: device pointers of one layer for
+    b200tx_sequence_forward_noalloc (plain bf16 weights, no images)."""
+
+    _fields_ = [
+        ("w_qkv", ctypes.c_void_p),
+        ("w_o", ctypes.c_void_p),
+        ("w_1", ctypes.c_void_p),
+        ("w_2", ctypes.c_void_p),
+        ("b_qkv", ctypes.c_void_p),
+        ("b_o", ctypes.c_void_p),
+        ("b_1", ctypes.c_void_p),
+        ("b_2", ctypes.c_void_p),
+        ("ln2_gamma", ctypes.c_void_p),
+        ("ln2_beta", ctypes.c_void_p),
+        ("next_gamma", ctypes.c_void_p),
+        ("next_beta", ctypes.c_void_p),
+    ]
+
+
 SEQ_IMAGE_BYTES = 128 * 128 * 2
+SEQ_NOALLOC_MAX_LAYERS = 4  # B200TX_SEQ_NOALLOC_MAX_LAYERS
 
 
 def seq_weight_image(weight: torch.Tensor, image: torch.Tensor) -> None:
@@ -860,6 +897,7 @@ __all__ = [
     "residual_layer_norm_peer",
     "SEQ_IMAGE_BYTES",
     "SeqLayer",
+    "SeqLayerWeights",
     "seq_weight_image",
     "sequence_forward",
     "residual_layer_norm_peer_rs",
