@@ -719,7 +719,8 @@ struct QuadShape {
 template <bool kMasked, int kTiles>
 __global__ void __launch_bounds__(QuadShape<kTiles>::kThreads, QuadShape<kTiles>::kCtasPerSm)
     attention_fwd_dh64_quad_kernel(const __grid_constant__ CUtensorMap tmap_q,
-                                   const __grid_constant__ CUtensorMap tmap_kv, AttnArgs args) {
+                                   const __grid_constant__ CUtensorMap tmap_kv,
+                                   const __grid_constant__ CUtensorMap tmap_out, AttnArgs args) {
   constexpr int kAttn4Tiles = kTiles;
   constexpr int kAttn4Ring = QuadShape<kTiles>::kRing;
   constexpr uint32_t kAttn4TmemCols = QuadShape<kTiles>::kTmemCols;
@@ -767,6 +768,7 @@ __global__ void __launch_bounds__(QuadShape<kTiles>::kThreads, QuadShape<kTiles>
   if (threadIdx.x == 0) {
     prefetch_tensor_map(&tmap_q);
     prefetch_tensor_map(&tmap_kv);
+    prefetch_tensor_map(&tmap_out);
     mbar_init(&q_full_bar, 1);
     for (int s = 0; s < kAttn4Ring; ++s) {
       mbar_init(&k_full_bar[s], 1);
@@ -1042,24 +1044,40 @@ __global__ void __launch_bounds__(QuadShape<kTiles>::kThreads, QuadShape<kTiles>
         tc_fence_after();
         // l = 0 only for a padding query that sees no valid key: zero row.
         const float inv_l = (!kMasked || l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-        __nv_bfloat16* out_row =
-            args.out + (static_cast<int64_t>(batch) * args.seq + q_idx) * d_model + head * kAttnDh;
+        // The warp's 32 output rows leave through its tile's Q slot, idle once
+        // the tile's UMMAs are complete: one 128-byte row per lane in the
+        // 128-byte-swizzled layout of a [32 x 64] box (4 KB-aligned, so row i
+        // swizzles by i % 8), then one TMA store (rows past the sequence are
+        // clipped by the tensor map) instead of 16-byte stores into 32 rows.
+        uint8_t* const box = smem_q + w * kAttnTileBytes + quarter * 32 * 128;
+        const uint32_t row_addr = smem_u32(box) + static_cast<uint32_t>(lane) * 128u;
+        const uint32_t swz = static_cast<uint32_t>(lane) & 7u;
 #pragma unroll 1
         for (int cc = 0; cc < kAttnDh / 32; ++cc) {
           uint32_t r[32];
           tmem_ld_32cols(o_tmem + cc * 32, r);
           tmem_wait_ld();
-          if (q_idx < args.seq) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              st_global_v4(out_row + cc * 32 + i,
-                           pack_bf16x2(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l),
-                           pack_bf16x2(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l),
-                           pack_bf16x2(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l),
-                           pack_bf16x2(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l));
-            }
+          for (int i = 0; i < 32; i += 8) {
+            const uint32_t chunk = static_cast<uint32_t>(cc * 4 + i / 8);
+            st_shared_v4(row_addr + ((chunk ^ swz) << 4),
+                         pack_bf16x2(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l),
+                         pack_bf16x2(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l),
+                         pack_bf16x2(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l),
+                         pack_bf16x2(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l));
           }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int row0 = q_tile * kAttnBM + quarter * 32;
+        if (lane == 0 && row0 < args.seq) {
+          tma_store_3d(&tmap_out, box, head * kAttnDh, row0, batch);
+          bulk_commit_group();
+          // The store has read the box and written its rows before the CTA
+          // (and its shared memory) goes away.
+          bulk_wait_group_all();
+        }
+        __syncwarp();
       }
     }
   }

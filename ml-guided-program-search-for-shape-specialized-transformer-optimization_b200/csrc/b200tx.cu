@@ -679,7 +679,17 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
     const uint32_t box[3] = {b200tx::kAttnDh, b200tx::kAttn4BN, 1};
     rc = encode_bf16_map(&map_kv, qkv, 3, dims, strides, box);
     if (rc != B200TX_OK) return rc;
-    using QuadFn = void (*)(CUtensorMap, CUtensorMap, b200tx::AttnArgs);
+    // The context [batch, seq, d_model] in [32 x 64] boxes: one per softmax
+    // warp's rows of one head.
+    CUtensorMap map_out;
+    const uint64_t out_dims[3] = {static_cast<uint64_t>(d_model), static_cast<uint64_t>(seq),
+                                  static_cast<uint64_t>(batch)};
+    const uint64_t out_strides[2] = {static_cast<uint64_t>(d_model) * 2,
+                                     static_cast<uint64_t>(d_model) * 2 * static_cast<uint64_t>(seq)};
+    const uint32_t out_box[3] = {b200tx::kAttnDh, 32, 1};
+    rc = encode_bf16_map(&map_out, out, 3, out_dims, out_strides, out_box);
+    if (rc != B200TX_OK) return rc;
+    using QuadFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, b200tx::AttnArgs);
     const bool duo = variant == B200TX_ATTN_DUO;
     const QuadFn quad_kernel =
         duo ? (key_valid != nullptr ? b200tx::attention_fwd_dh64_quad_kernel<true, 2>
@@ -700,7 +710,7 @@ int attention_impl(const void* qkv, const uint8_t* key_valid, void* out, int64_t
       }
     }
     cudaError_t err = launch(quad_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), smem,
-                             stream, map_qkv, map_kv, args);
+                             stream, map_qkv, map_kv, map_out, args);
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
     return B200TX_OK;
   }
