@@ -142,31 +142,26 @@ __global__ void seq_weight_images_kernel(const __grid_constant__ SeqImageSources
 // The per-row phases.  Thread (warp w, lane l) owns row 32 (w % 4) + l (its
 // TMEM lane) and the 32 columns [32 (w / 4), 32 (w / 4) + 32): one 32-column
 // TMEM load per phase.  Row reductions (LayerNorm statistics, softmax max and
-// sum) combine the four column groups through `red` (two buffers used in
-// turn, each rewritten only after a CTA barrier that follows its reads).
+// sum) combine the four column groups' partials, one (a, b) pair per group and
+// one CTA barrier per reduction, through `red2` (two buffers used in turn).
 struct SfRow {
-  int row;     // tile row = TMEM lane
-  int grp;     // column group 0..3
-  int col0;    // first column of the group
-  float* red;  // [2][4][128] partials
-  int turn;    // buffer of the next reduction
+  int row;       // tile row = TMEM lane
+  int grp;       // column group 0..3
+  int col0;      // first column of the group
+  float2* red2;  // [2][4][128] paired partials
+  int turn;      // buffer of the next reduction
 };
 
-// Sum over the row's four column groups of `part` (CTA barrier inside).
-__device__ __forceinline__ float sf_row_sum(SfRow& r, float part) {
-  float* buf = r.red + r.turn * 4 * kSfRows;
+// The row's four column groups' (a, b) partials, in group order (one CTA
+// barrier).  The two buffers alternate, so a buffer is rewritten only after
+// the next reduction's barrier, which follows every read of it.
+__device__ __forceinline__ void sf_row_pairs(SfRow& r, float a, float b, float2 (&p)[4]) {
+  float2* buf = r.red2 + r.turn * 4 * kSfRows;
   r.turn ^= 1;
-  buf[r.grp * kSfRows + r.row] = part;
+  buf[r.grp * kSfRows + r.row] = make_float2(a, b);
   __syncthreads();
-  return (buf[r.row] + buf[kSfRows + r.row]) + (buf[2 * kSfRows + r.row] + buf[3 * kSfRows + r.row]);
-}
-
-__device__ __forceinline__ float sf_row_max(SfRow& r, float part) {
-  float* buf = r.red + r.turn * 4 * kSfRows;
-  r.turn ^= 1;
-  buf[r.grp * kSfRows + r.row] = part;
-  __syncthreads();
-  return fmaxf(fmaxf(buf[r.row], buf[kSfRows + r.row]), fmaxf(buf[2 * kSfRows + r.row], buf[3 * kSfRows + r.row]));
+#pragma unroll
+  for (int g = 0; g < 4; ++g) p[g] = buf[g * kSfRows + r.row];
 }
 
 __device__ __forceinline__ void sf_load_bias32(const float* p, float* b) {
@@ -243,20 +238,34 @@ __device__ __forceinline__ void sf_epilogue_copy(uint32_t t_addr, uint32_t image
 template <bool kToGlobal>
 __device__ __forceinline__ void sf_layer_norm(SfRow& r, const float* v, float eps, const float* gamma,
                                               const float* beta, uint32_t image, float* out_row) {
+  // Each group's sum and squared deviations about its own mean (two passes
+  // in registers), then one exchange: the row's mean and M2 by the pairwise
+  // merge of Chan, Golub and LeVeque for four groups of 32.
   uint64_t s2 = f32x2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 32; i += 2) s2 = add_f32x2(s2, f32x2(v[i], v[i + 1]));
   const float2 sv = unpack_f32x2(s2);
-  const float mean = sf_row_sum(r, sv.x + sv.y) * (1.0f / kSfD);
-  const uint64_t mean2 = f32x2(mean, mean);
+  const float gsum = sv.x + sv.y;
+  const float gmean = gsum * (1.0f / 32);
+  const uint64_t gmean2 = f32x2(gmean, gmean);
   uint64_t q2 = f32x2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 32; i += 2) {
-    const uint64_t d = sub_f32x2(f32x2(v[i], v[i + 1]), mean2);
+    const uint64_t d = sub_f32x2(f32x2(v[i], v[i + 1]), gmean2);
     q2 = fma_f32x2(d, d, q2);
   }
   const float2 qv = unpack_f32x2(q2);
-  const float rstd = rsqrtf(sf_row_sum(r, qv.x + qv.y) * (1.0f / kSfD) + eps);
+  float2 part[4];
+  sf_row_pairs(r, gsum, qv.x + qv.y, part);
+  const float mean = ((part[0].x + part[1].x) + (part[2].x + part[3].x)) * (1.0f / kSfD);
+  float m2 = 0.f;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float dm = part[g].x * (1.0f / 32) - mean;
+    m2 += part[g].y + 32.0f * dm * dm;
+  }
+  const uint64_t mean2 = f32x2(mean, mean);
+  const float rstd = rsqrtf(m2 * (1.0f / kSfD) + eps);
   const uint64_t rstd2 = f32x2(rstd, rstd);
   float g[32], b[32];
   sf_load_bias32(gamma + r.col0, g);
@@ -337,7 +346,11 @@ __device__ __forceinline__ void sf_softmax(uint32_t t_addr, uint32_t image, SfRo
     }
     mx = fmaxf(m0, m1);
   }
-  mx = sf_row_max(r, mx);
+  // Exponentials and their sum against the group's own maximum, then one
+  // exchange of (max, sum) per group: the row's maximum M, its sum
+  // l = sum_g l_g 2^((m_g - M) scale) and this group's factor
+  // 2^((m_g - M) scale) / l.  The diagonal group is never empty, so M is
+  // finite; a group above the diagonal has m_g = -inf and l_g = 0.
   uint64_t sum2 = f32x2(0.f, 0.f);
   if (needed) {
     const uint64_t sc = f32x2(scale_log2, scale_log2);
@@ -351,7 +364,13 @@ __device__ __forceinline__ void sf_softmax(uint32_t t_addr, uint32_t image, SfRo
     }
   }
   const float2 sv = unpack_f32x2(sum2);
-  const float inv = 1.0f / sf_row_sum(r, sv.x + sv.y);
+  float2 part[4];
+  sf_row_pairs(r, mx, sv.x + sv.y, part);
+  const float row_max = fmaxf(fmaxf(part[0].x, part[1].x), fmaxf(part[2].x, part[3].x));
+  float total = 0.f;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) total += part[g].y * fast_exp2((part[g].x - row_max) * scale_log2);
+  const float inv = needed ? fast_exp2((mx - row_max) * scale_log2) / total : 0.f;
   const uint64_t inv2 = f32x2(inv, inv);
   float p[32];
 #pragma unroll
@@ -372,7 +391,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) seq_forward_kernel(const __grid
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
-  __shared__ float red[2 * 4 * kSfRows];  // row-reduction partials
+  __shared__ float2 red2[2 * 4 * kSfRows];  // row-reduction partials, (a, b) per group
 
   uint8_t* smem = align_1024(smem_raw);
   const uint32_t img_a = smem_u32(smem);
@@ -390,7 +409,7 @@ __global__ void __launch_bounds__(kSfThreads, 1) seq_forward_kernel(const __grid
   rw.row = quarter * 32 + (tid & 31);
   rw.grp = warp >> 2;
   rw.col0 = rw.grp * 32;
-  rw.red = red;
+  rw.red2 = red2;
   rw.turn = 0;
   const int row = rw.row;
 
