@@ -320,3 +320,44 @@ def test_kernel_wrappers_refuse_cpu_tensors() -> None:
     assert not can_use_sm100_residual_layer_norm(torch.zeros(4, 64), None, torch.nn.LayerNorm(64))
     with pytest.raises(RuntimeError, match="ineligible"):
         sm100_linear(a, w, None)
+
+
+# ------------------------------------------------------- reference install
+
+def test_build_restores_the_reference_install_only_when_it_can(tmp_path: Path, monkeypatch) -> None:  # noqa: ANN001
+    """__graft_entry__._install_reference: nothing to do when baseline/_ref is
+    there, or when BASELINE.json names no reference checkout that exists;
+    otherwise it runs baseline/install_reference.py with that checkout.  It
+    never raises."""
+
+    import subprocess
+    import sys
+
+    sys.path.insert(0, str(REPO))
+    import __graft_entry__ as entry
+
+    calls: list[list[str]] = []
+
+    def fake_run(cmd, **kwargs):  # noqa: ANN001, ANN003
+        calls.append(cmd)
+        return SimpleNamespace(returncode=0, stdout="", stderr="")
+
+    monkeypatch.setattr(subprocess, "run", fake_run)
+    monkeypatch.setattr(entry, "REPO", tmp_path)
+
+    (tmp_path / "BASELINE.json").write_text('{"metric": "m"}')  # no reference_path
+    entry._install_reference()
+    checkout = tmp_path / "ref"
+    (tmp_path / "BASELINE.json").write_text('{"reference_path": "%s"}' % checkout)
+    entry._install_reference()  # the checkout is absent
+    assert calls == []
+
+    (checkout / "official").mkdir(parents=True)
+    entry._install_reference()
+    assert len(calls) == 1 and calls[0][-1] == str(checkout) and calls[0][-2].endswith("install_reference.py")
+
+    installed = tmp_path / "baseline" / "_ref" / "official"
+    installed.mkdir(parents=True)
+    (installed / "torch_transformer_benchmark.py").write_text("")
+    entry._install_reference()
+    assert len(calls) == 1
